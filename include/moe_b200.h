@@ -1,0 +1,105 @@
+/*
+ * moe_b200 -- C ABI of the B200 (sm_100a) fused MoE expert-MLP library.
+ *
+ * Computes, over token rows pre-sorted by expert,
+ *
+ *     Y[rows of e] = GELU_tanh(X[rows of e] @ W_up[e]) @ W_down[e]
+ *
+ * with X (M, D), W_up (E, D, F), W_down (E, F, D), per-expert group sizes
+ * (E,) int32 on the device, and Y (M, D) float32.  Rows at or past
+ * sum(group_sizes) are written as zeros (jax.lax.ragged_dot semantics).
+ *
+ * All pointers are device pointers of the current CUDA device.  Calls are
+ * stream-ordered on `stream` (a cudaStream_t; NULL = legacy default stream),
+ * never synchronise the host, never allocate, and are safe to call from
+ * several host threads on different streams as long as each call has its own
+ * workspace.
+ *
+ * Return value: 0 on success, a negative MOE_ERR_* code otherwise; the text of
+ * the last error of the calling thread is available from moe_last_error().
+ */
+#ifndef MOE_B200_H_
+#define MOE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Precision paths (argument `dtype`). */
+enum {
+  MOE_DTYPE_F32 = 0,            /* f32 X/W, 3xTF32 tensor-core products, f32 Y */
+  MOE_DTYPE_BF16 = 1,           /* bf16 X/W, f32 accumulate, f32 Y              */
+  MOE_DTYPE_FP8_E4M3_BLK128 = 2 /* bf16 X, e4m3 W + f32 128x128 block scales    */
+};
+
+/* Error codes. */
+enum {
+  MOE_OK = 0,
+  MOE_ERR_INVALID_ARG = -1,
+  MOE_ERR_UNSUPPORTED_SHAPE = -2,
+  MOE_ERR_UNSUPPORTED_DTYPE = -3,
+  MOE_ERR_WORKSPACE_TOO_SMALL = -4,
+  MOE_ERR_CUDA = -5,
+  MOE_ERR_DEVICE_TIMEOUT = -6,
+  MOE_ERR_MISALIGNED = -7
+};
+
+/*
+ * Fused expert MLP forward.
+ *
+ * Replaces the body of `fused_ragged_dot_caller(x, w_up, w_down, group_sizes,
+ * *, BM, BF, max_group_size, interpret)` in the reference
+ * (Krushna-B/pallas-moe-kernel src/kernel.py:85-123), i.e. the
+ * `group_sizes_to_offsets` op (src/kernel.py:126-132) plus the
+ * `pl.pallas_call` of `fused_mlp_one_expert` (src/kernel.py:9-82); the result
+ * equals `ref_ragged_mlp` (src/kernel.py:152-175) within the precision of
+ * `dtype`.  BM, BF and max_group_size are not arguments: the kernel walks the
+ * real (expert, 128-row) blocks derived on the device from `group_sizes`.
+ *
+ *   x            (M, D)   f32 (MOE_DTYPE_F32) or bf16 (other dtypes)
+ *   w_up         (E, D, F) f32 / bf16 / e4m3 bytes
+ *   w_down       (E, F, D) f32 / bf16 / e4m3 bytes
+ *   group_sizes  (E,) int32, device memory; negative entries count as 0
+ *   w_up_scale   (E, D/128, F/128) f32 block scales (FP8 only, else NULL)
+ *   w_down_scale (E, F/128, D/128) f32 block scales (FP8 only, else NULL)
+ *   y            (M, D) f32 output
+ *   workspace    device scratch of at least moe_fused_mlp_workspace_size()
+ *                bytes, 256-byte aligned (may be NULL when that size is 0)
+ *   stream       cudaStream_t
+ */
+int moe_fused_mlp(const void* x, const void* w_up, const void* w_down, const int32_t* group_sizes,
+                  const float* w_up_scale, const float* w_down_scale, float* y, int64_t M, int32_t D, int32_t F,
+                  int32_t E, int32_t dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Scratch bytes moe_fused_mlp needs for this problem (0 when none). */
+size_t moe_fused_mlp_workspace_size(int64_t M, int32_t D, int32_t F, int32_t E, int32_t dtype);
+
+/* Text of the calling thread's last error ("" when none). */
+const char* moe_last_error(void);
+
+/*
+ * Reads the device status word of the current device (bits: 1 = a pipeline
+ * wait timed out, 2 = a negative group size was clamped).  Synchronises the
+ * device.  When `reset` is non-zero the word is cleared afterwards.
+ * Returns the bits (>= 0) or MOE_ERR_CUDA.
+ */
+int moe_device_status(int reset);
+
+/* Library version: major * 10000 + minor * 100 + patch. */
+int moe_version(void);
+
+/*
+ * Tuning overrides for tests and benchmarks (0 restores the automatic
+ * choice).  Keys: 1 = F-splits per 128-row block (power of two),
+ * 2 = persistent CTAs per launch.  Returns 0 or MOE_ERR_INVALID_ARG.
+ */
+int moe_set_tuning(int32_t key, int64_t value);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_B200_H_ */

@@ -1,0 +1,207 @@
+"""CPU oracle for the fused MoE expert MLP -- TEST INFRASTRUCTURE ONLY.
+
+This module restates, in numpy, the arithmetic of the reference path
+
+    Y = ragged_dot(gelu_tanh(ragged_dot(X, W_up, gs)), W_down, gs)
+
+as written in Krushna-B/pallas-moe-kernel ``src/kernel.py:137-175``
+(``ref_ragged_mlp_one_line`` / ``ref_ragged_mlp``) and the masking rules of
+the fused Pallas kernel ``src/kernel.py:9-82``.  Only ``tests/``,
+``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py`` may
+import it, and only as the checker or the timed CPU baseline; the product
+(the CUDA library and its Python wrapper) never calls into it.
+
+Parity status
+-------------
+* ``ragged_dot`` and ``gelu`` live in the third-party package JAX
+  (``jax==0.8.0`` pinned by the reference's ``requirements.txt:1-2``; the
+  published results used 0.7.2).  JAX is not installed in this environment,
+  and the reference stores no output values (no golden vectors), so the MLP
+  *values* are **parity unpinned**: the restatement follows JAX's documented
+  semantics --
+    - ``jax.lax.ragged_dot(lhs (M,K), rhs (G,K,N), group_sizes (G,))``:
+      rows ``[off_g, off_{g+1})`` of ``lhs`` are multiplied by ``rhs[g]``;
+      rows at or past ``sum(group_sizes)`` produce zeros;
+    - ``jax.nn.gelu(x, approximate=True)`` =
+      ``0.5 * x * (1 + tanh(sqrt(2/pi) * (x + 0.044715 * x**3)))``.
+* The kernel's block/mask control flow is pinned separately by executing
+  the reference's own Pallas kernel source under a numpy stand-in for
+  Pallas (``oracle/pallas_shim.py``, fixtures in ``tests/golden``).
+* The host-side group-size generators are pinned against the reference's
+  own functions executed here and against the group sizes recorded in the
+  reference's ``results/structured_float32/results.csv``.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional, Sequence
+
+import numpy as np
+
+SQRT_2_OVER_PI = math.sqrt(2.0 / math.pi)
+
+
+def group_sizes_to_offsets(group_sizes: Sequence[int]) -> np.ndarray:
+    """``[0, cumsum(gs)]`` -- ``src/kernel.py:126-132``."""
+    gs = np.asarray(group_sizes, dtype=np.int64)
+    return np.concatenate([np.zeros(1, dtype=np.int64), np.cumsum(gs)])
+
+
+def gelu_tanh(x: np.ndarray) -> np.ndarray:
+    """tanh-form GELU, the form ``jax.nn.gelu`` uses by default
+    (``approximate=True``), as called at ``src/kernel.py:67``,
+    ``src/kernel.py:140-147`` and ``src/ragged_moe_speedup_experiment.py:203-206``.
+    Computed in the dtype of ``x``."""
+    c = x.dtype.type(SQRT_2_OVER_PI)
+    k = x.dtype.type(0.044715)
+    half = x.dtype.type(0.5)
+    one = x.dtype.type(1.0)
+    return half * x * (one + np.tanh(c * (x + k * x * x * x)))
+
+
+def ragged_dot(lhs: np.ndarray, rhs: np.ndarray, group_sizes: Sequence[int],
+               acc_dtype=np.float64) -> np.ndarray:
+    """``jax.lax.ragged_dot`` semantics with ``preferred_element_type=acc_dtype``.
+
+    lhs (M, K), rhs (G, K, N), group_sizes (G,) -> (M, N).  Rows past
+    ``sum(group_sizes)`` are zero (call sites ``src/kernel.py:137-175``).
+    Offsets are clamped to M, matching a well-formed JAX call where
+    ``sum(group_sizes) <= M``.
+    """
+    M = lhs.shape[0]
+    G, K, N = rhs.shape
+    assert lhs.shape[1] == K, (lhs.shape, rhs.shape)
+    out = np.zeros((M, N), dtype=acc_dtype)
+    offs = np.minimum(group_sizes_to_offsets(np.maximum(np.asarray(group_sizes), 0)), M)
+    for g in range(G):
+        a, b = int(offs[g]), int(offs[g + 1])
+        if b > a:
+            out[a:b] = lhs[a:b].astype(acc_dtype) @ rhs[g].astype(acc_dtype)
+    return out
+
+
+def ref_ragged_mlp(x: np.ndarray, w_up: np.ndarray, w_down: np.ndarray,
+                   group_sizes: Sequence[int], acc_dtype=np.float64) -> np.ndarray:
+    """Two ragged dots with tanh-GELU between -- ``src/kernel.py:152-175``.
+
+    With ``acc_dtype=np.float64`` this is the ground truth the tolerances
+    are stated against; with ``np.float32`` it mirrors the reference's
+    ``preferred_element_type=jnp.float32`` accumulation.
+    """
+    h = ragged_dot(x, w_up, group_sizes, acc_dtype)
+    h = gelu_tanh(h)
+    return ragged_dot(h, w_down, group_sizes, acc_dtype)
+
+
+def ref_ragged_mlp_fp8(x: np.ndarray, w_up_q: np.ndarray, w_up_scale: np.ndarray,
+                       w_down_q: np.ndarray, w_down_scale: np.ndarray,
+                       group_sizes: Sequence[int], block: int = 128) -> np.ndarray:
+    """The dequantised reference for FP8 block-scaled weights.
+
+    ``W[e, i, j] = float(W_q[e, i, j]) * scale[e, i // block, j // block]``,
+    then the same two-ragged-dot path.  ``w_*_q`` are float arrays holding
+    the e4m3 values exactly (see :func:`e4m3_decode`).
+    """
+    return ref_ragged_mlp(x, dequant_block(w_up_q, w_up_scale, block),
+                          dequant_block(w_down_q, w_down_scale, block),
+                          group_sizes)
+
+
+def dequant_block(wq: np.ndarray, scale: np.ndarray, block: int = 128) -> np.ndarray:
+    E, R, C = wq.shape
+    s = np.repeat(np.repeat(scale.astype(np.float64), block, axis=1), block, axis=2)
+    return wq.astype(np.float64) * s[:, :R, :C]
+
+
+def e4m3_decode(codes: np.ndarray) -> np.ndarray:
+    """Decode OCP FP8 e4m3fn bytes (bias 7, no inf, 0x7f/0xff = NaN)."""
+    c = codes.astype(np.int64)
+    s = np.where(c & 0x80, -1.0, 1.0)
+    e = (c >> 3) & 0xF
+    m = c & 0x7
+    val = np.where(e == 0, m / 8.0 * 2.0 ** -6, (1.0 + m / 8.0) * 2.0 ** (e - 7.0))
+    val = np.where((e == 0xF) & (m == 0x7), np.nan, val)
+    return s * val
+
+
+def fused_kernel_blocks(x: np.ndarray, w_up: np.ndarray, w_down: np.ndarray,
+                        group_sizes: Sequence[int], *, BM: int, BF: int,
+                        max_group_size: int, fill=np.nan) -> np.ndarray:
+    """Block-structured restatement of the Pallas kernel ``src/kernel.py:9-82``.
+
+    Grid ``(E, cdiv(max_group_size, BM))`` (``:104-107``); program
+    ``(e, pid_m)`` covers rows ``[off_e + pid_m*BM, ...)`` masked to
+    ``< off_{e+1}`` (``:18-24``) and retires when ``m_start >= expert_end``
+    (``:20``); it streams F in ``BF`` chunks (``:74``), accumulating
+    ``gelu(x @ w_up_chunk) @ w_down_chunk`` in f32 (``:38``, ``:67-70``), and
+    stores only masked rows (``:77-82``).  Rows never written keep ``fill``
+    (the Pallas output buffer is uninitialised there, while ``ragged_dot``
+    returns zeros).  Float32 arithmetic throughout, like the kernel.
+    """
+    M, D = x.shape
+    E, _, F = w_up.shape
+    assert F % BF == 0 and M % BM == 0
+    y = np.full((M, D), fill, dtype=np.float32)
+    offs = group_sizes_to_offsets(group_sizes)
+    n_pid = -(-max_group_size // BM)
+    for e in range(E):
+        start, end = int(offs[e]), int(offs[e + 1])
+        for pid_m in range(n_pid):
+            m_start = start + pid_m * BM
+            if not m_start < end:
+                continue
+            rows = np.arange(m_start, m_start + BM)
+            mask = rows < end
+            xb = np.zeros((BM, D), np.float32)
+            valid = rows[mask]
+            valid = valid[valid < M]
+            xb[: len(valid)] = x[valid].astype(np.float32)
+            acc = np.zeros((BM, D), np.float32)
+            for fb in range(F // BF):
+                wu = w_up[e, :, fb * BF:(fb + 1) * BF].astype(np.float32)
+                wd = w_down[e, fb * BF:(fb + 1) * BF, :].astype(np.float32)
+                acc += gelu_tanh(xb @ wu) @ wd
+            y[valid] = acc[: len(valid)]
+    return y
+
+
+def correctness_metrics(y_ref: np.ndarray, y: np.ndarray) -> dict:
+    """The reference's numerical gate quantities --
+    ``src/ragged_moe_speedup_experiment.py:536-580`` and
+    ``src/benchmark.py:226-256``."""
+    y_ref = np.asarray(y_ref, dtype=np.float64)
+    y = np.asarray(y, dtype=np.float64)
+    diff = y - y_ref
+    absd = np.abs(diff)
+    ref_norm = float(np.linalg.norm(y_ref))
+    return {
+        "max_absolute_error": float(absd.max()) if absd.size else 0.0,
+        "mean_absolute_error": float(absd.mean()) if absd.size else 0.0,
+        "l2_relative_error": float(np.linalg.norm(diff) / max(ref_norm, 1e-12)),
+        "normalized_max_error": float((absd.max() if absd.size else 0.0)
+                                      / max(float(np.abs(y_ref).max()) if y_ref.size else 0.0, 1e-12)),
+        "reference_is_finite": bool(np.all(np.isfinite(y_ref))),
+        "fused_is_finite": bool(np.all(np.isfinite(y))),
+    }
+
+
+def time_cpu_reference(x: np.ndarray, w_up: np.ndarray, w_down: np.ndarray,
+                       group_sizes: Sequence[int], threads: Optional[int] = None) -> np.ndarray:
+    """The reference's unfused path on host cores, in float32 like
+    ``ref_ragged_mlp`` (``preferred_element_type=f32``): per-group sgemm
+    (BLAS, all threads), tanh-GELU, per-group sgemm.  Used as the timed CPU
+    baseline; ``threads`` is informational (BLAS threading is set through
+    the environment before numpy is imported)."""
+    M, D = x.shape
+    E, _, F = w_up.shape
+    y = np.zeros((M, D), np.float32)
+    offs = np.minimum(group_sizes_to_offsets(np.maximum(np.asarray(group_sizes), 0)), M)
+    for e in range(E):
+        a, b = int(offs[e]), int(offs[e + 1])
+        if b <= a:
+            continue
+        h = x[a:b].astype(np.float32, copy=False) @ w_up[e].astype(np.float32, copy=False)
+        h = gelu_tanh(h)
+        y[a:b] = h @ w_down[e].astype(np.float32, copy=False)
+    return y

@@ -1,0 +1,356 @@
+// C ABI of the B200 fused MoE expert-MLP library: argument checking, TMA
+// tensor-map setup, operand pre-split for the 3xTF32 path, and dispatch to
+// the sm_100a kernels.  Declarations: include/moe_b200.h.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/moe_b200.h"
+#include "fused_small.cuh"
+
+namespace moe {
+__device__ int g_status = 0;
+
+// ------------------------------------------------------------------ errors
+static thread_local char t_err[512] = {0};
+
+static int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_err, sizeof(t_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+#define MOE_CUDA_TRY(expr)                                                                   \
+  do {                                                                                       \
+    cudaError_t _e = (expr);                                                                 \
+    if (_e != cudaSuccess) return fail(MOE_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(_e)); \
+  } while (0)
+
+// ------------------------------------------------------------------ tuning
+static int64_t g_tune_splits = 0;
+static int64_t g_tune_ctas = 0;
+
+// ------------------------------------------------------------------ driver entry point
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D row-major tensor [rows, cols] with a {box_cols, box_rows} box and the
+// 128-byte swizzle; out-of-range elements read as zero.
+static int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int esz, uint64_t rows,
+                       uint64_t cols, uint32_t box_cols, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+    return fail(MOE_ERR_MISALIGNED, "operand base %p is not 16-byte aligned", base);
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * (uint64_t)esz};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) rows=%llu cols=%llu box=%ux%u", (int)r,
+                (unsigned long long)rows, (unsigned long long)cols, box_cols, box_rows);
+  return 0;
+}
+
+// ------------------------------------------------------------------ device info
+struct DevInfo {
+  int sms = 0;
+  bool attr_set[16] = {};
+};
+static DevInfo g_dev[64];
+static std::mutex g_dev_mu;
+
+static int device_info(int* dev_out, DevInfo** info) {
+  int dev = 0;
+  MOE_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(MOE_ERR_CUDA, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (g_dev[dev].sms == 0) {
+    int sms = 0;
+    MOE_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    int major = 0, minor = 0;
+    MOE_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    MOE_CUDA_TRY(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev));
+    if (major != 10 || minor != 0)
+      return fail(MOE_ERR_CUDA, "device %d is sm_%d%d; this library is built for sm_100a only", dev, major,
+                  minor);
+    g_dev[dev].sms = sms;
+  }
+  *dev_out = dev;
+  *info = &g_dev[dev];
+  return 0;
+}
+
+// ------------------------------------------------------------------ operand pre-split (3xTF32)
+// W (E, R, C) f32 -> hi/lo planes of W^T (E, C, R): hi = W rounded toward
+// zero to tf32, lo = W - hi.  32x32 tiles through shared memory so both the
+// read and the write are coalesced.
+__global__ void __launch_bounds__(256) split_transpose_kernel(const float* __restrict__ w, float* __restrict__ hi,
+                                                              float* __restrict__ lo, int R, int C) {
+  __shared__ float tile[32][33];
+  const int e = blockIdx.z;
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  const float* src = w + (size_t)e * R * C;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int r = r0 + i, c = c0 + threadIdx.x;
+    tile[i][threadIdx.x] = (r < R && c < C) ? src[(size_t)r * C + c] : 0.f;
+  }
+  __syncthreads();
+  float* dh = hi + (size_t)e * R * C;
+  float* dl = lo + (size_t)e * R * C;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int c = c0 + i, r = r0 + threadIdx.x;
+    if (r < R && c < C) {
+      const float v = tile[threadIdx.x][i];
+      const float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+      dh[(size_t)c * R + r] = h;
+      dl[(size_t)c * R + r] = v - h;
+    }
+  }
+}
+
+// X (n floats) -> hi/lo planes, same layout.
+__global__ void __launch_bounds__(256) split_kernel(const float4* __restrict__ x, float4* __restrict__ hi,
+                                                    float4* __restrict__ lo, size_t n4) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+    const float4 v = x[i];
+    float4 h, l;
+    h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+    h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+    h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+    h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+    l.x = v.x - h.x;
+    l.y = v.y - h.y;
+    l.z = v.z - h.z;
+    l.w = v.w - h.w;
+    hi[i] = h;
+    lo[i] = l;
+  }
+}
+
+// ------------------------------------------------------------------ small-D dispatch
+struct SmallPlan {
+  int bf;
+  bool x_res;
+  size_t ws_bytes;
+};
+
+static bool small_supported(int D, int F, int dtype) {
+  if (!(D == 64 || D == 128 || D == 256)) return false;
+  if (dtype == MOE_DTYPE_F32) return F % 64 == 0;
+  if (dtype == MOE_DTYPE_BF16) return F % 128 == 0;
+  return false;
+}
+
+static SmallPlan small_plan(int64_t M, int D, int F, int E, int dtype) {
+  SmallPlan s{};
+  if (dtype == MOE_DTYPE_F32) {
+    s.bf = 64;
+    s.x_res = D <= 128;
+    const size_t w = (size_t)E * D * F * sizeof(float);
+    s.ws_bytes = 4 * w + (s.x_res ? 0 : 2 * (size_t)M * D * sizeof(float));
+  } else {
+    s.bf = 128;
+    s.x_res = true;
+    s.ws_bytes = 0;
+  }
+  return s;
+}
+
+static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+template <int MODE, int D, int BF, bool XR>
+static int launch_small(const FusedMaps& maps, const FusedParams& prm, int ctas, DevInfo* di, cudaStream_t st) {
+  using Cfg = FusedCfg<MODE, D, BF, XR>;
+  auto kern = fused_mlp_small_kernel<MODE, D, BF, XR>;
+  constexpr int slot = (MODE * 3 + (D == 64 ? 0 : D == 128 ? 1 : 2)) * 2 + (XR ? 1 : 0);
+  static_assert(slot < 16, "attribute slot");
+  if (!di->attr_set[slot]) {
+    MOE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    di->attr_set[slot] = true;
+  }
+  kern<<<ctas, 192, Cfg::SMEM, st>>>(maps, prm);
+  MOE_CUDA_TRY(cudaGetLastError());
+  return 0;
+}
+
+static int run_small(const void* x, const void* w_up, const void* w_down, const int32_t* gs, float* y, int64_t M,
+                     int D, int F, int E, int dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
+  int dev;
+  DevInfo* di;
+  if (int r = device_info(&dev, &di)) return r;
+  const SmallPlan plan = small_plan(M, D, F, E, dtype);
+  if (ws_bytes < plan.ws_bytes)
+    return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", ws_bytes, plan.ws_bytes);
+  if (plan.ws_bytes && (reinterpret_cast<uintptr_t>(ws) & 255u))
+    return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+
+  const int nch_total = F / plan.bf;
+  int splits = 1;
+  if (g_tune_splits > 0) {
+    splits = (int)g_tune_splits;
+    if (nch_total % splits != 0)
+      return fail(MOE_ERR_INVALID_ARG, "tuning splits=%d does not divide %d chunks", splits, nch_total);
+  } else {
+    const int64_t blocks_est = (M + 127) / 128;
+    while (blocks_est * splits < di->sms && nch_total % (splits * 2) == 0 && splits * 2 <= nch_total) splits *= 2;
+  }
+  int ctas = g_tune_ctas > 0 ? (int)g_tune_ctas : di->sms;
+
+  int* status = nullptr;
+  MOE_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_status));
+
+  FusedParams prm{};
+  prm.group_sizes = gs;
+  prm.y = y;
+  prm.M = (int)M;
+  prm.E = E;
+  prm.F = F;
+  prm.splits = splits;
+  prm.chunks_per_split = nch_total / splits;
+  prm.atomic_out = splits > 1 ? 1 : 0;
+  prm.status = status;
+
+  FusedMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  if (splits > 1) MOE_CUDA_TRY(cudaMemsetAsync(y, 0, (size_t)M * D * sizeof(float), st));
+
+  if (dtype == MOE_DTYPE_BF16) {
+    const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    if (int r = make_map_2d(&maps.x[0], x, BF16, 2, (uint64_t)M, D, 64, 128)) return r;
+    if (int r = make_map_2d(&maps.wu[0], w_up, BF16, 2, (uint64_t)E * D, F, 64, 64)) return r;
+    if (int r = make_map_2d(&maps.wd[0], w_down, BF16, 2, (uint64_t)E * F, D, 64, 64)) return r;
+    switch (D) {
+      case 64: return launch_small<kModeBF16, 64, 128, true>(maps, prm, ctas, di, st);
+      case 128: return launch_small<kModeBF16, 128, 128, true>(maps, prm, ctas, di, st);
+      case 256: return launch_small<kModeBF16, 256, 128, true>(maps, prm, ctas, di, st);
+    }
+    return fail(MOE_ERR_UNSUPPORTED_SHAPE, "D=%d", D);
+  }
+
+  // 3xTF32: pre-split weights into K-major hi/lo planes.
+  const auto F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  const size_t wsz = (size_t)E * D * F;
+  float* wu_hi = static_cast<float*>(ws);
+  float* wu_lo = wu_hi + wsz;
+  float* wd_hi = wu_lo + wsz;
+  float* wd_lo = wd_hi + wsz;
+  {
+    dim3 blk(32, 8);
+    dim3 g_up_t((F + 31) / 32, (D + 31) / 32, E);  // W_up (E, D, F): R = D, C = F -> (E, F, D)
+    split_transpose_kernel<<<g_up_t, blk, 0, st>>>(static_cast<const float*>(w_up), wu_hi, wu_lo, D, F);
+    MOE_CUDA_TRY(cudaGetLastError());
+    dim3 g_dn_t((D + 31) / 32, (F + 31) / 32, E);  // W_down (E, F, D): R = F, C = D -> (E, D, F)
+    split_transpose_kernel<<<g_dn_t, blk, 0, st>>>(static_cast<const float*>(w_down), wd_hi, wd_lo, F, D);
+    MOE_CUDA_TRY(cudaGetLastError());
+  }
+  if (int r = make_map_2d(&maps.wu[0], wu_hi, F32, 4, (uint64_t)E * F, D, 32, plan.bf)) return r;
+  if (int r = make_map_2d(&maps.wu[1], wu_lo, F32, 4, (uint64_t)E * F, D, 32, plan.bf)) return r;
+  if (int r = make_map_2d(&maps.wd[0], wd_hi, F32, 4, (uint64_t)E * D, F, 32, D)) return r;
+  if (int r = make_map_2d(&maps.wd[1], wd_lo, F32, 4, (uint64_t)E * D, F, 32, D)) return r;
+  if (plan.x_res) {
+    if (int r = make_map_2d(&maps.x[0], x, F32, 4, (uint64_t)M, D, 32, 128)) return r;
+  } else {
+    float* x_hi = wd_lo + wsz;
+    float* x_lo = x_hi + (size_t)M * D;
+    const size_t n4 = (size_t)M * D / 4;
+    const int blocks = (int)std::min<size_t>((n4 + 255) / 256, (size_t)di->sms * 8);
+    split_kernel<<<blocks, 256, 0, st>>>(static_cast<const float4*>(x), reinterpret_cast<float4*>(x_hi),
+                                         reinterpret_cast<float4*>(x_lo), n4);
+    MOE_CUDA_TRY(cudaGetLastError());
+    if (int r = make_map_2d(&maps.x[0], x_hi, F32, 4, (uint64_t)M, D, 32, 128)) return r;
+    if (int r = make_map_2d(&maps.x[1], x_lo, F32, 4, (uint64_t)M, D, 32, 128)) return r;
+  }
+  switch (D) {
+    case 64: return launch_small<kModeTF32x3, 64, 64, true>(maps, prm, ctas, di, st);
+    case 128: return launch_small<kModeTF32x3, 128, 64, true>(maps, prm, ctas, di, st);
+    case 256: return launch_small<kModeTF32x3, 256, 64, false>(maps, prm, ctas, di, st);
+  }
+  return fail(MOE_ERR_UNSUPPORTED_SHAPE, "D=%d", D);
+}
+
+}  // namespace moe
+
+using namespace moe;
+
+extern "C" {
+
+const char* moe_last_error(void) { return t_err; }
+
+int moe_version(void) { return 100; }
+
+int moe_set_tuning(int32_t key, int64_t value) {
+  if (value < 0) return fail(MOE_ERR_INVALID_ARG, "negative tuning value");
+  switch (key) {
+    case 1:
+      if (value & (value - 1)) return fail(MOE_ERR_INVALID_ARG, "splits must be a power of two");
+      g_tune_splits = value;
+      return 0;
+    case 2:
+      g_tune_ctas = value;
+      return 0;
+  }
+  return fail(MOE_ERR_INVALID_ARG, "unknown tuning key %d", key);
+}
+
+int moe_device_status(int reset) {
+  int v = 0;
+  MOE_CUDA_TRY(cudaDeviceSynchronize());
+  MOE_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_status, sizeof(int)));
+  if (reset) {
+    int z = 0;
+    MOE_CUDA_TRY(cudaMemcpyToSymbol(g_status, &z, sizeof(int)));
+  }
+  return v;
+}
+
+size_t moe_fused_mlp_workspace_size(int64_t M, int32_t D, int32_t F, int32_t E, int32_t dtype) {
+  if (M < 0 || D <= 0 || F <= 0 || E <= 0) return 0;
+  if (small_supported(D, F, dtype)) return align256(small_plan(M, D, F, E, dtype).ws_bytes);
+  return 0;
+}
+
+int moe_fused_mlp(const void* x, const void* w_up, const void* w_down, const int32_t* group_sizes,
+                  const float* w_up_scale, const float* w_down_scale, float* y, int64_t M, int32_t D, int32_t F,
+                  int32_t E, int32_t dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  t_err[0] = 0;
+  (void)w_up_scale;
+  (void)w_down_scale;
+  if (M < 0 || D <= 0 || F <= 0 || E <= 0)
+    return fail(MOE_ERR_INVALID_ARG, "bad sizes M=%lld D=%d F=%d E=%d", (long long)M, D, F, E);
+  if (M > (int64_t)0x7fffffff) return fail(MOE_ERR_UNSUPPORTED_SHAPE, "M=%lld exceeds 2^31-1", (long long)M);
+  if (M == 0) return 0;
+  if (!x || !w_up || !w_down || !group_sizes || !y) return fail(MOE_ERR_INVALID_ARG, "null operand pointer");
+  if (reinterpret_cast<uintptr_t>(y) & 15u) return fail(MOE_ERR_MISALIGNED, "y must be 16-byte aligned");
+  if (dtype != MOE_DTYPE_F32 && dtype != MOE_DTYPE_BF16 && dtype != MOE_DTYPE_FP8_E4M3_BLK128)
+    return fail(MOE_ERR_UNSUPPORTED_DTYPE, "dtype %d", dtype);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (small_supported(D, F, dtype))
+    return run_small(x, w_up, w_down, group_sizes, y, M, D, F, E, dtype, workspace, workspace_bytes, st);
+  return fail(MOE_ERR_UNSUPPORTED_SHAPE, "no kernel for D=%d F=%d dtype=%d", D, F, dtype);
+}
+
+}  // extern "C"

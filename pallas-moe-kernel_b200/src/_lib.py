@@ -1,0 +1,78 @@
+"""ctypes binding of ``libmoe_b200.so`` (declarations: include/moe_b200.h).
+
+There is no fallback: if the library is missing or fails to load, every
+entry point raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent.parent / "lib" / "libmoe_b200.so"
+
+MOE_DTYPE_F32 = 0
+MOE_DTYPE_BF16 = 1
+MOE_DTYPE_FP8_E4M3_BLK128 = 2
+
+ERRORS = {
+    -1: "MOE_ERR_INVALID_ARG",
+    -2: "MOE_ERR_UNSUPPORTED_SHAPE",
+    -3: "MOE_ERR_UNSUPPORTED_DTYPE",
+    -4: "MOE_ERR_WORKSPACE_TOO_SMALL",
+    -5: "MOE_ERR_CUDA",
+    -6: "MOE_ERR_DEVICE_TIMEOUT",
+    -7: "MOE_ERR_MISALIGNED",
+}
+
+_lib = None
+
+
+class MoeError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{ERRORS.get(code, code)}: {msg}")
+        self.code = code
+
+
+def lib() -> ctypes.CDLL:
+    """Loads the library once; raises if it is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = Path(os.environ.get("MOE_B200_LIB", LIB_PATH))
+    if not path.exists():
+        raise RuntimeError(f"{path} not found: build it with `python __graft_entry__.py` or "
+                           f"`python pallas-moe-kernel_b200/csrc/build.py`")
+    L = ctypes.CDLL(str(path))
+    vp, sz, i32, i64 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int32, ctypes.c_int64
+    L.moe_fused_mlp.argtypes = [vp, vp, vp, vp, vp, vp, vp, i64, i32, i32, i32, i32, vp, sz, vp]
+    L.moe_fused_mlp.restype = ctypes.c_int
+    L.moe_fused_mlp_workspace_size.argtypes = [i64, i32, i32, i32, i32]
+    L.moe_fused_mlp_workspace_size.restype = sz
+    L.moe_last_error.argtypes = []
+    L.moe_last_error.restype = ctypes.c_char_p
+    L.moe_device_status.argtypes = [ctypes.c_int]
+    L.moe_device_status.restype = ctypes.c_int
+    L.moe_version.argtypes = []
+    L.moe_version.restype = ctypes.c_int
+    L.moe_set_tuning.argtypes = [i32, i64]
+    L.moe_set_tuning.restype = ctypes.c_int
+    _lib = L
+    return L
+
+
+def check(code: int) -> None:
+    if code != 0:
+        raise MoeError(code, lib().moe_last_error().decode(errors="replace"))
+
+
+def set_tuning(key: int, value: int) -> None:
+    check(lib().moe_set_tuning(key, value))
+
+
+def device_status(reset: bool = False) -> int:
+    v = lib().moe_device_status(1 if reset else 0)
+    if v < 0:
+        check(v)
+    return v

@@ -1,0 +1,169 @@
+"""Fused MoE expert MLP on B200 -- drop-in for the reference's ``src/kernel.py``.
+
+``fused_ragged_dot_caller`` keeps the signature and argument checks of the
+reference entry point (Krushna-B/pallas-moe-kernel ``src/kernel.py:85-123``)
+but runs the hand-written sm_100a kernels of ``libmoe_b200.so`` through its C
+ABI on the current CUDA stream.  Arrays are torch CUDA tensors (JAX arrays in
+the reference); the result is a new ``(M, D)`` float32 tensor.
+
+Differences from the reference, by design:
+  * ``BM``, ``BF`` and ``max_group_size`` are validated as the reference does
+    (``M % BM == 0``, ``F % BF == 0``) but do not shape the launch: the kernel
+    enumerates the real (expert, 128-row) blocks on the device from
+    ``group_sizes``, so no host sync and no recompilation per routing.
+  * Rows at or past ``sum(group_sizes)`` are zero, as in ``ragged_dot``; the
+    Pallas kernel leaves them unwritten (``src/kernel.py:77-82``).
+  * ``interpret=True`` (the Pallas CPU interpreter) has no counterpart: there
+    is no CPU path, and the call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+__all__ = [
+    "fused_ragged_dot_caller",
+    "fused_ragged_mlp",
+    "group_sizes_to_offsets",
+    "workspace_size",
+    "ref_ragged_mlp",
+    "ref_ragged_mlp_one_line",
+]
+
+_FP8 = getattr(torch, "float8_e4m3fn", None)
+
+
+def _dtype_code(x: torch.Tensor, w_up: torch.Tensor) -> int:
+    if x.dtype == torch.float32 and w_up.dtype == torch.float32:
+        return _lib.MOE_DTYPE_F32
+    if x.dtype == torch.bfloat16 and w_up.dtype == torch.bfloat16:
+        return _lib.MOE_DTYPE_BF16
+    if x.dtype == torch.bfloat16 and _FP8 is not None and w_up.dtype == _FP8:
+        return _lib.MOE_DTYPE_FP8_E4M3_BLK128
+    raise TypeError(f"unsupported dtypes x={x.dtype} w_up={w_up.dtype} "
+                    f"(f32/f32, bf16/bf16 or bf16/float8_e4m3fn)")
+
+
+def workspace_size(M: int, D: int, F: int, E: int, dtype_code: int) -> int:
+    return int(_lib.lib().moe_fused_mlp_workspace_size(M, D, F, E, dtype_code))
+
+
+def _as_device_group_sizes(group_sizes, device) -> torch.Tensor:
+    if not isinstance(group_sizes, torch.Tensor):
+        group_sizes = torch.as_tensor(group_sizes)
+    gs = group_sizes.to(device=device, dtype=torch.int32, non_blocking=True)
+    return gs.contiguous()
+
+
+def fused_ragged_mlp(x: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor, group_sizes,
+                     *, w_up_scale: Optional[torch.Tensor] = None,
+                     w_down_scale: Optional[torch.Tensor] = None,
+                     out: Optional[torch.Tensor] = None,
+                     workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Core call: ``Y = ragged_dot(gelu_tanh(ragged_dot(X, W_up)), W_down)``.
+
+    x (M, D) f32|bf16, w_up (E, D, F), w_down (E, F, D) of the same dtype
+    (or float8_e4m3fn weights with f32 block scales (E, D/128, F/128) and
+    (E, F/128, D/128)), group_sizes (E,) int -- all on one CUDA device.
+    Stream-ordered on ``torch.cuda.current_stream()``.
+    """
+    if not x.is_cuda:
+        raise ValueError("fused_ragged_mlp runs on CUDA tensors only (no CPU path)")
+    M, D = x.shape
+    E, D2, F = w_up.shape
+    if D != D2 or tuple(w_down.shape) != (E, F, D):
+        raise ValueError(f"shape mismatch x={tuple(x.shape)} w_up={tuple(w_up.shape)} "
+                         f"w_down={tuple(w_down.shape)}")
+    code = _dtype_code(x, w_up)
+    if w_down.dtype != w_up.dtype:
+        raise TypeError("w_up and w_down must share a dtype")
+    dev = x.device
+    for t in (w_up, w_down):
+        if t.device != dev:
+            raise ValueError("all operands must be on the same device")
+    x = x.contiguous()
+    w_up = w_up.contiguous()
+    w_down = w_down.contiguous()
+    gs = _as_device_group_sizes(group_sizes, dev)
+    if gs.numel() != E:
+        raise ValueError(f"group_sizes has {gs.numel()} entries, expected E={E}")
+    if code == _lib.MOE_DTYPE_FP8_E4M3_BLK128:
+        if w_up_scale is None or w_down_scale is None:
+            raise ValueError("FP8 weights need w_up_scale and w_down_scale")
+        w_up_scale = w_up_scale.to(device=dev, dtype=torch.float32).contiguous()
+        w_down_scale = w_down_scale.to(device=dev, dtype=torch.float32).contiguous()
+    if out is None:
+        out = torch.empty((M, D), device=dev, dtype=torch.float32)
+    elif out.shape != (M, D) or out.dtype != torch.float32 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous (M, D) float32 tensor")
+    ws_bytes = workspace_size(M, D, F, E, code)
+    if ws_bytes and (workspace is None or workspace.numel() * workspace.element_size() < ws_bytes):
+        workspace = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    with torch.cuda.device(dev):
+        rc = _lib.lib().moe_fused_mlp(
+            ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(w_up.data_ptr()),
+            ctypes.c_void_p(w_down.data_ptr()), ctypes.c_void_p(gs.data_ptr()),
+            ctypes.c_void_p(w_up_scale.data_ptr() if w_up_scale is not None else 0),
+            ctypes.c_void_p(w_down_scale.data_ptr() if w_down_scale is not None else 0),
+            ctypes.c_void_p(out.data_ptr()), M, D, F, E, code,
+            ctypes.c_void_p(workspace.data_ptr() if ws_bytes else 0), ws_bytes,
+            ctypes.c_void_p(stream))
+    _lib.check(rc)
+    return out
+
+
+def fused_ragged_dot_caller(x, w_up, w_down, group_sizes, *, BM: int = 16, BF: int = 64,
+                            max_group_size: int, interpret: bool = False, **kwargs) -> torch.Tensor:
+    """Reference entry point (``src/kernel.py:85-123``): same arguments and the
+    same assertions; returns the f32 ``(M, D)`` output."""
+    M, D = x.shape
+    E, D2, F = w_up.shape
+    assert D == D2
+    assert tuple(w_down.shape) == (E, F, D)
+    assert M % BM == 0
+    assert F % BF == 0
+    del max_group_size  # the device-side block walk covers every real block
+    if interpret:
+        raise NotImplementedError("interpret=True (Pallas CPU interpreter) has no counterpart: "
+                                  "this library runs on the B200 only")
+    return fused_ragged_mlp(x, w_up, w_down, group_sizes, **kwargs)
+
+
+def group_sizes_to_offsets(group_sizes: torch.Tensor) -> torch.Tensor:
+    """``[0, cumsum(group_sizes)]`` (``src/kernel.py:126-132``)."""
+    gs = torch.as_tensor(group_sizes)
+    return torch.cat([torch.zeros(1, dtype=gs.dtype, device=gs.device), torch.cumsum(gs, 0).to(gs.dtype)])
+
+
+def _ref(x, w_up, w_down, group_sizes) -> torch.Tensor:
+    gs = torch.as_tensor(group_sizes).to("cpu").tolist()
+    M, D = x.shape
+    y = torch.zeros((M, D), dtype=torch.float32, device=x.device)
+    off = 0
+    for e, g in enumerate(gs):
+        g = max(int(g), 0)
+        hi = min(off + g, M)
+        if hi > off:
+            h = x[off:hi].float() @ w_up[e].float()
+            h = torch.nn.functional.gelu(h, approximate="tanh")
+            y[off:hi] = h @ w_down[e].float()
+        off = hi
+    return y
+
+
+def ref_ragged_mlp(x, w_up, w_down, group_sizes) -> torch.Tensor:
+    """Unfused two-ragged-dot path (``src/kernel.py:152-175``) with torch ops on
+    the tensors' own device: materialises H per expert.  For comparison only;
+    it is not the fused path and is not used by it."""
+    return _ref(x, w_up, w_down, group_sizes)
+
+
+def ref_ragged_mlp_one_line(x, w_up, w_down, group_sizes) -> torch.Tensor:
+    """Same as :func:`ref_ragged_mlp` (``src/kernel.py:137-149``)."""
+    return _ref(x, w_up, w_down, group_sizes)
