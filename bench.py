@@ -1,0 +1,405 @@
+"""Benchmark of the B200 fused MoE expert MLP (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+
+A step is one forward of the expert MLP over one batch of synthetic routed
+tokens (seeded; shapes, inits and routing of the named configuration).
+``value`` is routed tokens/s over the whole job with inputs resident in HBM,
+device-timed with CUDA events, L2 flushed before every step; ``e2e`` is the
+same metric through the public call with the step's inputs copied from
+pinned host memory and the result read back inside the timed region.
+
+At N > 1 (torchrun, one rank per GPU) the expert-parallel layer runs: every
+rank owns E/N experts and its own batch of tokens; tokens travel to their
+expert's rank and back through NCCL all-to-all (weak scaling).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+PKG = REPO / "pallas-moe-kernel_b200"
+for _p in (str(PKG), str(REPO)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+L2_FLUSH_BYTES = 256 << 20  # twice the 126 MB L2
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return d, "measured"
+        except Exception:
+            pass
+    return dict(PEAKS_FALLBACK), "fallback"
+
+
+# --------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML every ~10 ms."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int):
+        self.samples: list[tuple[float, int, int]] = []
+        self._stop = threading.Event()
+        self._t = None
+        self.max_mhz = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = device_index
+            if vis:
+                parts = [v for v in vis.split(",") if v.strip()]
+                if device_index < len(parts) and parts[device_index].strip().isdigit():
+                    idx = int(parts[device_index])
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self._nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((time.perf_counter(), mhz, rs))
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def start(self):
+        if self._nv is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+
+    def stop(self):
+        self._stop.set()
+        if self._t is not None:
+            self._t.join()
+
+    def summary(self, t0: float, t1: float) -> dict:
+        win = [s for s in self.samples if t0 <= s[0] <= t1]
+        if not win and self.samples:  # very short timed region: nearest samples
+            win = sorted(self.samples, key=lambda s: min(abs(s[0] - t0), abs(s[0] - t1)))[:3]
+        if not win:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        reasons = set()
+        for _, _, rs in win:
+            for bit, name in self.REASONS.items():
+                if rs & bit and name != "gpu_idle":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(m for _, m, _ in win), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(win)}
+
+
+# --------------------------------------------------------------------- workload
+def make_workload(cfg, device, seed: int = 0):
+    """Seeded synthetic inputs on the device: X ~ N(0,1) (M, D),
+    W_up ~ N(0, 1/D) (E, D, F), W_down ~ N(0, 1/F) (E, F, D)."""
+    import torch
+    from src.routing import config_group_sizes
+
+    gs = config_group_sizes(cfg, seed=seed)
+    g = torch.Generator(device=device)
+    g.manual_seed(1234 + seed)
+    tdt = torch.float32 if cfg.dtype == "f32" else torch.bfloat16
+    x = torch.randn((cfg.M, cfg.D), generator=g, device=device, dtype=torch.float32).to(tdt)
+    w_up = (torch.randn((cfg.E, cfg.D, cfg.F), generator=g, device=device, dtype=torch.float32)
+            / math.sqrt(cfg.D)).to(tdt)
+    w_down = (torch.randn((cfg.E, cfg.F, cfg.D), generator=g, device=device, dtype=torch.float32)
+              / math.sqrt(cfg.F)).to(tdt)
+    return x, w_up, w_down, gs
+
+
+def algorithmic(cfg, gs) -> dict:
+    """FLOPs = 4 M D F (GELU excluded); bytes = X + non-empty experts' weights + Y."""
+    sx = 4 if cfg.dtype == "f32" else 2
+    sw = {"f32": 4, "bf16": 2, "fp8": 1}[cfg.dtype]
+    active = int(np.count_nonzero(np.asarray(gs) > 0))
+    byts = cfg.M * cfg.D * sx + active * 2 * cfg.D * cfg.F * sw + cfg.M * cfg.D * 4
+    return {"flops": 4 * cfg.M * cfg.D * cfg.F, "bytes": byts}
+
+
+def tensor_peak(cfg, peaks) -> tuple[float, str]:
+    bf16 = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
+    if cfg.dtype == "f32":
+        return bf16 / 6.0, (f"bf16 {bf16:.1f} TF/s / 6: kind::tf32 issues at half the f16 rate and "
+                            f"3xTF32 spends 3 products per f32 product")
+    return bf16, f"bf16 {bf16:.1f} TF/s"
+
+
+# --------------------------------------------------------------------- our arm
+def run_ours(args, cfg, rank, world, device) -> dict | None:
+    import torch
+    import torch.distributed as dist
+    from src import _lib
+    from src.kernel import PreparedExperts, fused_ragged_dot_caller
+
+    x, w_up, w_down, gs_np = make_workload(cfg, device, seed=rank)
+    gs_dev = torch.from_numpy(gs_np).to(device)
+    if world > 1:
+        from src.ep import ExpertParallelMLP
+        layer = ExpertParallelMLP(w_up, w_down, rank=rank, world=world, max_tokens=cfg.M)
+        step_fn = lambda: layer(x, gs_dev)  # noqa: E731
+        kern_fn = None
+        launches_per_step = layer.launches_per_step
+    else:
+        experts = PreparedExperts(w_up, w_down, max_tokens=cfg.M)
+        y = torch.empty((cfg.M, cfg.D), device=device, dtype=torch.float32)
+        ws = torch.empty(max(experts.ws_bytes, 1), device=device, dtype=torch.uint8)
+
+        def step_fn():  # the reference entry point: raw weights in, Y out
+            return fused_ragged_dot_caller(x, w_up, w_down, gs_dev, BM=16, BF=64, max_group_size=cfg.M,
+                                           out=y, workspace=ws)
+
+        def kern_fn():  # the dominant kernel alone (weights already prepared)
+            return experts(x, gs_dev, out=y)
+        launches_per_step = 3 if cfg.dtype == "f32" else 1
+
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def timed(fn, steps):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for i in range(steps):
+            flush.zero_()
+            ev[i][0].record(stream)
+            fn()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize(device)
+        return [a.elapsed_time(b) for a, b in ev]
+
+    for _ in range(args.warmup):
+        step_fn()
+        if kern_fn:
+            kern_fn()
+    torch.cuda.synchronize(device)
+    _lib.device_status(reset=True)
+
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    time.sleep(0.05)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    step_ms = timed(step_fn, args.steps)
+    t1 = time.perf_counter()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    clocks.stop()
+    total_ms = float(sum(step_ms))
+    kern_ms = timed(kern_fn, args.steps) if kern_fn else None
+    status = _lib.device_status(reset=True)
+    if status:
+        raise RuntimeError(f"device status {status} after the timed region")
+
+    # e2e: pinned host X -> device, call, Y -> pinned host, every step.
+    xh = x.cpu().pin_memory()
+    gsh = torch.from_numpy(gs_np).pin_memory()
+    yh = torch.empty((cfg.M, cfg.D), dtype=torch.float32).pin_memory()
+    xd = torch.empty_like(x)
+    gsd = torch.empty_like(gs_dev)
+
+    def e2e_step():
+        xd.copy_(xh, non_blocking=True)
+        gsd.copy_(gsh, non_blocking=True)
+        if world > 1:
+            out = layer(xd, gsd)
+        else:
+            out = fused_ragged_dot_caller(xd, w_up, w_down, gsd, BM=16, BF=64, max_group_size=cfg.M,
+                                          out=y, workspace=ws)
+        yh.copy_(out, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    e2e_ms = float(sum(timed(e2e_step, args.steps)))
+
+    vals = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    total_ms, e2e_ms = vals.tolist()
+    if rank != 0:
+        return None
+
+    peaks, peak_src = load_peaks()
+    alg = algorithmic(cfg, gs_np)
+    ms_per_step = total_ms / args.steps
+    value = world * cfg.M * args.steps / (total_ms / 1e3)
+    line = {
+        "metric": "routed_tokens_per_s",
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": {"f32": "f32 (3xTF32)", "bf16": "bf16", "fp8": "fp8e4m3 weights, bf16 x"}[cfg.dtype],
+        "data": "synthetic (seeded; BASELINE config shapes, N(0,1)/N(0,1/D)/N(0,1/F) init)",
+        "config": {"workload": cfg.name, "M_per_gpu": cfg.M, "D": cfg.D, "F": cfg.F, "E": cfg.E,
+                   "routing": cfg.routing, "parallelism": f"ep{world}" if world > 1 else "single",
+                   "l2": "flushed before every step (256 MiB write)"},
+        "useful_tflops": alg["flops"] * world / (ms_per_step / 1e3) / 1e12,
+        "gpu_launches": launches_per_step * args.steps,
+    }
+    if kern_ms is not None:
+        k_avg = statistics.mean(kern_ms)
+        peak, basis = tensor_peak(cfg, peaks)
+        achieved = alg["flops"] / (k_avg / 1e3) / 1e12
+        t_mem = alg["bytes"] / (float(peaks["hbm_gbs"]) * 1e9)
+        t_cmp = alg["flops"] / (peak * 1e12)
+        line["roofline"] = {
+            "bound": "tensor" if t_cmp >= t_mem else "hbm",
+            "kernel": "fused_mlp_small_kernel",
+            "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "peak_source": f"{peak_src}: {basis}",
+            "kernel_ms": k_avg, "algorithmic_flops": alg["flops"], "algorithmic_bytes": alg["bytes"],
+            "hbm_frac": (alg["bytes"] / (k_avg / 1e3)) / (float(peaks["hbm_gbs"]) * 1e9),
+            "traffic": None,
+        }
+        prof = REPO / "profiles" / f"traffic_{cfg.name}.json"
+        if prof.exists():
+            try:
+                line["roofline"]["traffic"] = json.loads(prof.read_text()).get("traffic_bytes_per_launch")
+            except Exception:
+                pass
+    line["clocks"] = clocks.summary(t0, t1)
+    h2d = cfg.M * cfg.D * x.element_size() + gs_np.nbytes
+    line["e2e"] = {"value": world * cfg.M * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
+                   "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": cfg.M * cfg.D * 4}
+    return line
+
+
+# --------------------------------------------------------------------- CPU baseline
+def cpu_reference(cfg, budget_s: float, seed: int = 0) -> dict:
+    """The reference's unfused path (two ragged dots with tanh-GELU, f32) on
+    host cores, timed on a bounded sample of the workload's rows."""
+    from oracle import moe_oracle as orc
+    from src.routing import config_group_sizes
+
+    gs = config_group_sizes(cfg, seed=seed)
+    # Bounded sample: the first `rows` routed rows (whole experts in order).
+    rng = np.random.default_rng(seed)
+    per_row_flops = 4 * cfg.D * cfg.F
+    rows = int(min(cfg.M, max(128, 3e10 / per_row_flops)))  # ~30 GFLOP per timed call at most
+    offs = np.concatenate([[0], np.cumsum(gs)])
+    gs_s = np.clip(np.minimum(offs[1:], rows) - np.minimum(offs[:-1], rows), 0, None).astype(np.int32)
+    active = np.nonzero(gs_s)[0]
+    x = rng.standard_normal((rows, cfg.D), dtype=np.float32)
+    # Only the experts the sample touches are materialised.
+    w_up = [None] * cfg.E
+    w_down = [None] * cfg.E
+    for e in active:
+        w_up[e] = rng.standard_normal((cfg.D, cfg.F), dtype=np.float32) / np.float32(math.sqrt(cfg.D))
+        w_down[e] = rng.standard_normal((cfg.F, cfg.D), dtype=np.float32) / np.float32(math.sqrt(cfg.F))
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while True:
+        t = time.perf_counter()
+        orc.time_cpu_reference(x, w_up, w_down, gs_s)
+        times.append(time.perf_counter() - t)
+        if time.perf_counter() > t_end or len(times) >= 50:
+            break
+    med = statistics.median(times)
+    cores = len(os.sched_getaffinity(0))
+    return {"value": rows / med, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{rows} of {cfg.M} routed rows ({len(active)} experts), f32 numpy/BLAS, "
+                      f"median of {len(times)} calls",
+            "seconds_per_call": med}
+
+
+def run_reference(args, cfg, rank, world) -> dict | None:
+    if rank != 0:
+        return None
+    base = cpu_reference(cfg, budget_s=args.ref_budget)
+    steps_t = base["seconds_per_call"]
+    return {
+        "impl": "reference", "metric": "routed_tokens_per_s", "value": base["value"], "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": steps_t * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded)", "config": {"workload": cfg.name, "M_per_gpu": cfg.M, "D": cfg.D,
+                                                  "F": cfg.F, "E": cfg.E},
+        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+# --------------------------------------------------------------------- main
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c2", help="c1..c5 (default c2: fp32 M=65536 D=128 F=512 E=8)")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ref-budget", type=float, default=10.0, help="seconds of CPU baseline timing")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tokens", type=int, default=0, help="override M (routed rows per GPU)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    from src.routing import CONFIGS, with_shape
+    cfg = CONFIGS[args.config]
+    if args.tokens:
+        cfg = with_shape(cfg, M=args.tokens, name=f"{cfg.name}_M{args.tokens}")
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        line = run_reference(args, cfg, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return 0
+
+    import torch
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    try:
+        line = run_ours(args, cfg, rank, world, device)
+        if line is not None:
+            if not args.no_cpu_baseline:
+                base = cpu_reference(cfg, budget_s=args.ref_budget)
+                line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -77,6 +77,25 @@ int moe_fused_mlp(const void* x, const void* w_up, const void* w_down, const int
 /* Scratch bytes moe_fused_mlp needs for this problem (0 when none). */
 size_t moe_fused_mlp_workspace_size(int64_t M, int32_t D, int32_t F, int32_t E, int32_t dtype);
 
+/*
+ * Two-stage form of moe_fused_mlp for weights that stay fixed across calls
+ * (no counterpart in the reference, whose entry point re-reads the weights
+ * every call; moe_fused_mlp == moe_prepare_weights + moe_fused_mlp_prepared).
+ *
+ * moe_prepare_weights writes the weight operands in the layout the kernel
+ * reads (3xTF32: tf32 hi/lo planes, K-major) at the start of `workspace`;
+ * for bf16 it does nothing.  moe_fused_mlp_prepared then runs the fused
+ * kernel on a workspace prepared for the same (D, F, E, dtype) and the same
+ * weights; its arguments mean what they mean for moe_fused_mlp.
+ */
+int moe_prepare_weights(const void* w_up, const void* w_down, const float* w_up_scale, const float* w_down_scale,
+                        int32_t D, int32_t F, int32_t E, int32_t dtype, void* workspace, size_t workspace_bytes,
+                        void* stream);
+int moe_fused_mlp_prepared(const void* x, const void* w_up, const void* w_down, const int32_t* group_sizes,
+                           const float* w_up_scale, const float* w_down_scale, float* y, int64_t M, int32_t D,
+                           int32_t F, int32_t E, int32_t dtype, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
 /* Text of the calling thread's last error ("" when none). */
 const char* moe_last_error(void);
 

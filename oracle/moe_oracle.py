@@ -186,15 +186,14 @@ def correctness_metrics(y_ref: np.ndarray, y: np.ndarray) -> dict:
     }
 
 
-def time_cpu_reference(x: np.ndarray, w_up: np.ndarray, w_down: np.ndarray,
-                       group_sizes: Sequence[int], threads: Optional[int] = None) -> np.ndarray:
+def time_cpu_reference(x: np.ndarray, w_up, w_down, group_sizes: Sequence[int]) -> np.ndarray:
     """The reference's unfused path on host cores, in float32 like
     ``ref_ragged_mlp`` (``preferred_element_type=f32``): per-group sgemm
     (BLAS, all threads), tanh-GELU, per-group sgemm.  Used as the timed CPU
-    baseline; ``threads`` is informational (BLAS threading is set through
-    the environment before numpy is imported)."""
+    baseline.  ``w_up[e]`` / ``w_down[e]`` may be any per-expert indexable
+    (an (E, D, F) array or a list); experts with no rows are not touched."""
     M, D = x.shape
-    E, _, F = w_up.shape
+    E = len(group_sizes)
     y = np.zeros((M, D), np.float32)
     offs = np.minimum(group_sizes_to_offsets(np.maximum(np.asarray(group_sizes), 0)), M)
     for e in range(E):

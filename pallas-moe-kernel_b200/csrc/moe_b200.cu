@@ -197,16 +197,44 @@ static int launch_small(const FusedMaps& maps, const FusedParams& prm, int ctas,
   return 0;
 }
 
+static int check_workspace(const SmallPlan& plan, const void* ws, size_t ws_bytes) {
+  if (ws_bytes < plan.ws_bytes)
+    return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", ws_bytes, plan.ws_bytes);
+  if (plan.ws_bytes && (reinterpret_cast<uintptr_t>(ws) & 255u))
+    return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+  return 0;
+}
+
+// Weight preparation: for the 3xTF32 path, split W_up / W_down into K-major
+// tf32 hi/lo planes at the start of the workspace.  Nothing for bf16.
+static int prepare_small(const void* w_up, const void* w_down, int D, int F, int E, int dtype, void* ws,
+                         size_t ws_bytes, cudaStream_t st) {
+  const SmallPlan plan = small_plan(0, D, F, E, dtype);
+  if (dtype != MOE_DTYPE_F32) return 0;
+  if (int r = check_workspace(plan, ws, ws_bytes)) return r;
+  const size_t wsz = (size_t)E * D * F;
+  float* wu_hi = static_cast<float*>(ws);
+  float* wu_lo = wu_hi + wsz;
+  float* wd_hi = wu_lo + wsz;
+  float* wd_lo = wd_hi + wsz;
+  dim3 blk(32, 8);
+  dim3 g_up((F + 31) / 32, (D + 31) / 32, E);  // W_up (E, D, F) -> planes (E, F, D)
+  split_transpose_kernel<<<g_up, blk, 0, st>>>(static_cast<const float*>(w_up), wu_hi, wu_lo, D, F);
+  MOE_CUDA_TRY(cudaGetLastError());
+  dim3 g_dn((D + 31) / 32, (F + 31) / 32, E);  // W_down (E, F, D) -> planes (E, D, F)
+  split_transpose_kernel<<<g_dn, blk, 0, st>>>(static_cast<const float*>(w_down), wd_hi, wd_lo, F, D);
+  MOE_CUDA_TRY(cudaGetLastError());
+  return 0;
+}
+
+// Main fused launch; for 3xTF32 the weight planes must already be in `ws`.
 static int run_small(const void* x, const void* w_up, const void* w_down, const int32_t* gs, float* y, int64_t M,
                      int D, int F, int E, int dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
   int dev;
   DevInfo* di;
   if (int r = device_info(&dev, &di)) return r;
   const SmallPlan plan = small_plan(M, D, F, E, dtype);
-  if (ws_bytes < plan.ws_bytes)
-    return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", ws_bytes, plan.ws_bytes);
-  if (plan.ws_bytes && (reinterpret_cast<uintptr_t>(ws) & 255u))
-    return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+  if (int r = check_workspace(plan, ws, ws_bytes)) return r;
 
   const int nch_total = F / plan.bf;
   int splits = 1;
@@ -251,22 +279,12 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
     return fail(MOE_ERR_UNSUPPORTED_SHAPE, "D=%d", D);
   }
 
-  // 3xTF32: pre-split weights into K-major hi/lo planes.
   const auto F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   const size_t wsz = (size_t)E * D * F;
   float* wu_hi = static_cast<float*>(ws);
   float* wu_lo = wu_hi + wsz;
   float* wd_hi = wu_lo + wsz;
   float* wd_lo = wd_hi + wsz;
-  {
-    dim3 blk(32, 8);
-    dim3 g_up_t((F + 31) / 32, (D + 31) / 32, E);  // W_up (E, D, F): R = D, C = F -> (E, F, D)
-    split_transpose_kernel<<<g_up_t, blk, 0, st>>>(static_cast<const float*>(w_up), wu_hi, wu_lo, D, F);
-    MOE_CUDA_TRY(cudaGetLastError());
-    dim3 g_dn_t((D + 31) / 32, (F + 31) / 32, E);  // W_down (E, F, D): R = F, C = D -> (E, D, F)
-    split_transpose_kernel<<<g_dn_t, blk, 0, st>>>(static_cast<const float*>(w_down), wd_hi, wd_lo, F, D);
-    MOE_CUDA_TRY(cudaGetLastError());
-  }
   if (int r = make_map_2d(&maps.wu[0], wu_hi, F32, 4, (uint64_t)E * F, D, 32, plan.bf)) return r;
   if (int r = make_map_2d(&maps.wu[1], wu_lo, F32, 4, (uint64_t)E * F, D, 32, plan.bf)) return r;
   if (int r = make_map_2d(&maps.wd[0], wd_hi, F32, 4, (uint64_t)E * D, F, 32, D)) return r;
@@ -333,24 +351,58 @@ size_t moe_fused_mlp_workspace_size(int64_t M, int32_t D, int32_t F, int32_t E, 
   return 0;
 }
 
+static int check_args(const void* x, const void* w_up, const void* w_down, const int32_t* gs, const float* y,
+                      int64_t M, int32_t D, int32_t F, int32_t E, int32_t dtype) {
+  if (M < 0 || D <= 0 || F <= 0 || E <= 0)
+    return fail(MOE_ERR_INVALID_ARG, "bad sizes M=%lld D=%d F=%d E=%d", (long long)M, D, F, E);
+  if (M > (int64_t)0x7fffffff) return fail(MOE_ERR_UNSUPPORTED_SHAPE, "M=%lld exceeds 2^31-1", (long long)M);
+  if (dtype != MOE_DTYPE_F32 && dtype != MOE_DTYPE_BF16 && dtype != MOE_DTYPE_FP8_E4M3_BLK128)
+    return fail(MOE_ERR_UNSUPPORTED_DTYPE, "dtype %d", dtype);
+  if (M == 0) return 0;
+  if (!x || !w_up || !w_down || !gs || !y) return fail(MOE_ERR_INVALID_ARG, "null operand pointer");
+  if (reinterpret_cast<uintptr_t>(y) & 15u) return fail(MOE_ERR_MISALIGNED, "y must be 16-byte aligned");
+  if (!small_supported(D, F, dtype))
+    return fail(MOE_ERR_UNSUPPORTED_SHAPE, "no kernel for D=%d F=%d dtype=%d", D, F, dtype);
+  return 0;
+}
+
+int moe_prepare_weights(const void* w_up, const void* w_down, const float* w_up_scale, const float* w_down_scale,
+                        int32_t D, int32_t F, int32_t E, int32_t dtype, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  t_err[0] = 0;
+  (void)w_up_scale;
+  (void)w_down_scale;
+  if (D <= 0 || F <= 0 || E <= 0) return fail(MOE_ERR_INVALID_ARG, "bad sizes D=%d F=%d E=%d", D, F, E);
+  if (dtype != MOE_DTYPE_F32 && dtype != MOE_DTYPE_BF16 && dtype != MOE_DTYPE_FP8_E4M3_BLK128)
+    return fail(MOE_ERR_UNSUPPORTED_DTYPE, "dtype %d", dtype);
+  if (!w_up || !w_down) return fail(MOE_ERR_INVALID_ARG, "null weight pointer");
+  if (!small_supported(D, F, dtype))
+    return fail(MOE_ERR_UNSUPPORTED_SHAPE, "no kernel for D=%d F=%d dtype=%d", D, F, dtype);
+  return prepare_small(w_up, w_down, D, F, E, dtype, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int moe_fused_mlp_prepared(const void* x, const void* w_up, const void* w_down, const int32_t* group_sizes,
+                           const float* w_up_scale, const float* w_down_scale, float* y, int64_t M, int32_t D,
+                           int32_t F, int32_t E, int32_t dtype, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  t_err[0] = 0;
+  (void)w_up_scale;
+  (void)w_down_scale;
+  if (int r = check_args(x, w_up, w_down, group_sizes, y, M, D, F, E, dtype)) return r;
+  if (M == 0) return 0;
+  return run_small(x, w_up, w_down, group_sizes, y, M, D, F, E, dtype, workspace, workspace_bytes,
+                   static_cast<cudaStream_t>(stream));
+}
+
 int moe_fused_mlp(const void* x, const void* w_up, const void* w_down, const int32_t* group_sizes,
                   const float* w_up_scale, const float* w_down_scale, float* y, int64_t M, int32_t D, int32_t F,
                   int32_t E, int32_t dtype, void* workspace, size_t workspace_bytes, void* stream) {
   t_err[0] = 0;
-  (void)w_up_scale;
-  (void)w_down_scale;
-  if (M < 0 || D <= 0 || F <= 0 || E <= 0)
-    return fail(MOE_ERR_INVALID_ARG, "bad sizes M=%lld D=%d F=%d E=%d", (long long)M, D, F, E);
-  if (M > (int64_t)0x7fffffff) return fail(MOE_ERR_UNSUPPORTED_SHAPE, "M=%lld exceeds 2^31-1", (long long)M);
+  if (int r = check_args(x, w_up, w_down, group_sizes, y, M, D, F, E, dtype)) return r;
   if (M == 0) return 0;
-  if (!x || !w_up || !w_down || !group_sizes || !y) return fail(MOE_ERR_INVALID_ARG, "null operand pointer");
-  if (reinterpret_cast<uintptr_t>(y) & 15u) return fail(MOE_ERR_MISALIGNED, "y must be 16-byte aligned");
-  if (dtype != MOE_DTYPE_F32 && dtype != MOE_DTYPE_BF16 && dtype != MOE_DTYPE_FP8_E4M3_BLK128)
-    return fail(MOE_ERR_UNSUPPORTED_DTYPE, "dtype %d", dtype);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (small_supported(D, F, dtype))
-    return run_small(x, w_up, w_down, group_sizes, y, M, D, F, E, dtype, workspace, workspace_bytes, st);
-  return fail(MOE_ERR_UNSUPPORTED_SHAPE, "no kernel for D=%d F=%d dtype=%d", D, F, dtype);
+  if (int r = prepare_small(w_up, w_down, D, F, E, dtype, workspace, workspace_bytes, st)) return r;
+  return run_small(x, w_up, w_down, group_sizes, y, M, D, F, E, dtype, workspace, workspace_bytes, st);
 }
 
 }  // extern "C"

@@ -48,6 +48,10 @@ def lib() -> ctypes.CDLL:
     vp, sz, i32, i64 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int32, ctypes.c_int64
     L.moe_fused_mlp.argtypes = [vp, vp, vp, vp, vp, vp, vp, i64, i32, i32, i32, i32, vp, sz, vp]
     L.moe_fused_mlp.restype = ctypes.c_int
+    L.moe_fused_mlp_prepared.argtypes = [vp, vp, vp, vp, vp, vp, vp, i64, i32, i32, i32, i32, vp, sz, vp]
+    L.moe_fused_mlp_prepared.restype = ctypes.c_int
+    L.moe_prepare_weights.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, vp, sz, vp]
+    L.moe_prepare_weights.restype = ctypes.c_int
     L.moe_fused_mlp_workspace_size.argtypes = [i64, i32, i32, i32, i32]
     L.moe_fused_mlp_workspace_size.restype = sz
     L.moe_last_error.argtypes = []

@@ -49,6 +49,16 @@ def _dtype_code(x: torch.Tensor, w_up: torch.Tensor) -> int:
                     f"(f32/f32, bf16/bf16 or bf16/float8_e4m3fn)")
 
 
+def _weight_dtype_code(w_up: torch.Tensor) -> int:
+    if w_up.dtype == torch.float32:
+        return _lib.MOE_DTYPE_F32
+    if w_up.dtype == torch.bfloat16:
+        return _lib.MOE_DTYPE_BF16
+    if _FP8 is not None and w_up.dtype == _FP8:
+        return _lib.MOE_DTYPE_FP8_E4M3_BLK128
+    raise TypeError(f"unsupported weight dtype {w_up.dtype}")
+
+
 def workspace_size(M: int, D: int, F: int, E: int, dtype_code: int) -> int:
     return int(_lib.lib().moe_fused_mlp_workspace_size(M, D, F, E, dtype_code))
 
@@ -116,6 +126,58 @@ def fused_ragged_mlp(x: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor, 
             ctypes.c_void_p(stream))
     _lib.check(rc)
     return out
+
+
+class PreparedExperts:
+    """Expert weights with their kernel-side operand layout built once
+    (``moe_prepare_weights``), for repeated calls with fixed weights.
+
+    ``max_tokens`` bounds M of later calls (it sizes the workspace)."""
+
+    def __init__(self, w_up: torch.Tensor, w_down: torch.Tensor, *, max_tokens: int,
+                 w_up_scale: Optional[torch.Tensor] = None, w_down_scale: Optional[torch.Tensor] = None):
+        self.E, self.D, self.F = w_up.shape
+        if tuple(w_down.shape) != (self.E, self.F, self.D):
+            raise ValueError("w_down must be (E, F, D)")
+        self.w_up = w_up.contiguous()
+        self.w_down = w_down.contiguous()
+        self.w_up_scale = None if w_up_scale is None else w_up_scale.float().contiguous()
+        self.w_down_scale = None if w_down_scale is None else w_down_scale.float().contiguous()
+        self.dtype_code = _weight_dtype_code(w_up)
+        self.max_tokens = int(max_tokens)
+        self.ws_bytes = workspace_size(self.max_tokens, self.D, self.F, self.E, self.dtype_code)
+        self.workspace = torch.empty(max(self.ws_bytes, 1), device=w_up.device, dtype=torch.uint8)
+        stream = torch.cuda.current_stream(w_up.device).cuda_stream
+        with torch.cuda.device(w_up.device):
+            rc = _lib.lib().moe_prepare_weights(
+                ctypes.c_void_p(self.w_up.data_ptr()), ctypes.c_void_p(self.w_down.data_ptr()),
+                ctypes.c_void_p(self.w_up_scale.data_ptr() if self.w_up_scale is not None else 0),
+                ctypes.c_void_p(self.w_down_scale.data_ptr() if self.w_down_scale is not None else 0),
+                self.D, self.F, self.E, self.dtype_code, ctypes.c_void_p(self.workspace.data_ptr()),
+                self.ws_bytes, ctypes.c_void_p(stream))
+        _lib.check(rc)
+
+    def __call__(self, x: torch.Tensor, group_sizes, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        M, D = x.shape
+        if D != self.D:
+            raise ValueError(f"x has D={D}, experts have D={self.D}")
+        if M > self.max_tokens:
+            raise ValueError(f"M={M} exceeds max_tokens={self.max_tokens}")
+        dev = x.device
+        gs = _as_device_group_sizes(group_sizes, dev)
+        if out is None:
+            out = torch.empty((M, D), device=dev, dtype=torch.float32)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        with torch.cuda.device(dev):
+            rc = _lib.lib().moe_fused_mlp_prepared(
+                ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(self.w_up.data_ptr()),
+                ctypes.c_void_p(self.w_down.data_ptr()), ctypes.c_void_p(gs.data_ptr()),
+                ctypes.c_void_p(self.w_up_scale.data_ptr() if self.w_up_scale is not None else 0),
+                ctypes.c_void_p(self.w_down_scale.data_ptr() if self.w_down_scale is not None else 0),
+                ctypes.c_void_p(out.data_ptr()), M, self.D, self.F, self.E, self.dtype_code,
+                ctypes.c_void_p(self.workspace.data_ptr()), self.ws_bytes, ctypes.c_void_p(stream))
+        _lib.check(rc)
+        return out
 
 
 def fused_ragged_dot_caller(x, w_up, w_down, group_sizes, *, BM: int = 16, BF: int = 64,
