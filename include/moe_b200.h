@@ -113,7 +113,10 @@ int moe_version(void);
 /*
  * Tuning overrides for tests and benchmarks (0 restores the automatic
  * choice).  Keys: 1 = F-splits per 128-row block (power of two),
- * 2 = persistent CTAs per launch.  Returns 0 or MOE_ERR_INVALID_ARG.
+ * 2 = persistent CTAs per launch, 3 = device address of an event-trace
+ * buffer (read only by builds compiled with -DMOE_TRACE), 4 = kernel family
+ * (0 automatic, 1 one CTA per 128-row block, 2 CTA pairs per 256 rows).
+ * Returns 0 or MOE_ERR_INVALID_ARG.
  */
 int moe_set_tuning(int32_t key, int64_t value);
 

@@ -26,11 +26,15 @@
 //                toward zero to tf32 (19 bits) and a_lo = a - a_hi, which
 //                keeps the result within ~1e-6 relative of f32 math.
 //                Weights arrive pre-split (hi/lo planes, transposed to
-//                K-major); X is split in shared memory by the GELU warps when
-//                the tile is resident, else pre-split too.
+//                K-major).  With a resident X tile (D <= 128) the GELU warps
+//                split X in place: X_hi stays in shared memory and X_lo goes
+//                to TMEM, where MMA1 reads it as an A operand; this keeps
+//                shared memory for a deeper weight ring.  For D = 256 X is
+//                pre-split and streamed with the weights.
 //
-// Warp roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA
-// issuer, warps 2..5 GELU / epilogue (one TMEM lane quadrant each).
+// Warp roles (320 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA
+// issuer, warps 2..9 GELU / epilogue (two warps per TMEM lane quadrant, each
+// taking half of the columns).
 #pragma once
 #include "ptx.cuh"
 
@@ -46,11 +50,28 @@ struct FusedParams {
   int M;
   int E;
   int F;
-  int splits;            // F-splits per 128-row block
-  int chunks_per_split;  // BF-wide chunks handled by one unit
-  int atomic_out;        // 1: Y was zeroed, units reduce-add into it
-  int* status;           // device status word (kStatus* bits)
+  int splits;                 // F-splits per 128-row block
+  int chunks_per_split;       // BF-wide chunks handled by one unit
+  int atomic_out;             // 1: Y was zeroed, units reduce-add into it
+  int* status;                // device status word (kStatus* bits)
+  unsigned long long* trace;  // MOE_TRACE builds: per-CTA event timeline (else unused)
 };
+
+// Optional timeline of pipeline events (clock64 per event) for CTA-level
+// analysis; compiled in only with -DMOE_TRACE.  Layout per CTA: 4 rows
+// (producer, MMA stage waits, GELU warp, MMA hidden waits) of kTraceLen.
+constexpr int kTraceLen = 256;
+#ifdef MOE_TRACE
+#define MOE_TRACE_EV(row, idx)                                                    \
+  do {                                                                            \
+    if (p.trace && (idx) < kTraceLen)                                             \
+      p.trace[((size_t)blockIdx.x * 4 + (row)) * kTraceLen + (idx)] = clock64(); \
+  } while (0)
+#else
+#define MOE_TRACE_EV(row, idx) \
+  do {                         \
+  } while (0)
+#endif
 
 template <int MODE, int D, int BF, bool X_RES>
 struct FusedCfg {
@@ -59,43 +80,62 @@ struct FusedCfg {
   static constexpr int ATOM = 128 / ESZ;  // elements in one 128-byte swizzle row
   static constexpr int KI = 32 / ESZ;     // K of one MMA instruction
   static constexpr int PL = kTF32 ? 2 : 1;
+  static constexpr bool XLO_TMEM = kTF32 && X_RES;  // X_lo lives in TMEM
   static constexpr int BM = 128;
-  static constexpr int SK = ATOM;                       // K rows per ring stage
-  static constexpr int XBOX = BM * 128;                 // one X k-slice: 128 rows x 128 B
-  static constexpr int X_PLANE = (D / ATOM) * XBOX;     // one full X plane
-  static constexpr int X_BYTES = X_RES ? PL * X_PLANE : 0;
-  static constexpr int S1_X = X_RES ? 0 : PL * XBOX;    // streamed X slice planes
-  static constexpr int S1_WPLANE = BF * 128;            // one W_up slice plane
-  static constexpr int S1_BYTES = S1_X + PL * S1_WPLANE;
-  static constexpr int S2_WPLANE = D * 128;             // one W_down slice plane
+  static constexpr int XBOX = BM * 128;                        // one X k-box: 128 rows x 128 B
+  static constexpr int X_PLANE = (D / ATOM) * XBOX;            // one full X plane
+  static constexpr int X_BYTES = X_RES ? X_PLANE : 0;          // resident X (bf16, or tf32 hi)
+  // MMA1 stage: KB1 k-boxes, each [streamed X planes][W_up planes].
+  static constexpr int KB1 = (kTF32 && X_RES) ? 2 : 1;
+  static constexpr int S1_X = X_RES ? 0 : PL * XBOX;
+  static constexpr int S1_WPLANE = BF * 128;  // one W_up plane of one k-box
+  static constexpr int S1_SUB = S1_X + PL * S1_WPLANE;
+  static constexpr int S1_BYTES = KB1 * S1_SUB;
+  static constexpr int SK1 = KB1 * ATOM;      // K rows per MMA1 stage
+  // MMA2 stage: one k-box of W_down planes.
+  static constexpr int S2_WPLANE = D * 128;
   static constexpr int S2_BYTES = PL * S2_WPLANE;
+  static constexpr int SK2 = ATOM;
   static constexpr int STAGE = S1_BYTES > S2_BYTES ? S1_BYTES : S2_BYTES;
-  static constexpr int N1 = D / SK;   // ring stages per MMA1 chunk
-  static constexpr int N2 = BF / SK;  // ring stages per MMA2 chunk
+  static constexpr int N1 = D / SK1;   // ring stages per MMA1 chunk
+  static constexpr int N2 = BF / SK2;  // ring stages per MMA2 chunk
   static constexpr int BAR_BYTES = 256;
-  static constexpr int NS_FIT = (kMaxSmemPerBlock - 1024 - BAR_BYTES - X_BYTES) / STAGE;
+  static constexpr int Y_STAGE = 8 * 32 * 32 * 4;  // 4 KB per epilogue warp for coalesced Y stores
+  static constexpr int NS_FIT = (kMaxSmemPerBlock - 1024 - BAR_BYTES - X_BYTES - Y_STAGE) / STAGE;
   static constexpr int NS = NS_FIT > 8 ? 8 : NS_FIT;
-  static constexpr int SMEM = 1024 + X_BYTES + NS * STAGE + BAR_BYTES;
-  // TMEM columns: Y accumulator [0, D); hidden buffer b at D + b * PL * BF
-  // (accumulator / hi plane first, lo plane after it).
+  static constexpr int SMEM = 1024 + X_BYTES + NS * STAGE + Y_STAGE + BAR_BYTES;
+  // TMEM columns: Y accumulator [0, D); hidden buffer b at D + b * HCOLS
+  // (accumulator / hi plane first, lo plane after it); X_lo after both.
   static constexpr int HCOLS = PL * BF;
+  static constexpr int XLO_COL = D + 2 * HCOLS;
+  static constexpr int TMEM_USED = XLO_COL + (XLO_TMEM ? D : 0);
   static constexpr int TMEM_COLS = 512;
   static constexpr uint32_t FMT = kTF32 ? kFmtTF32 : kFmtBF16;
   static constexpr uint32_t B_MN = kTF32 ? 0u : 1u;  // bf16 weights are read MN-major
-  static constexpr uint32_t IDESC1 = make_idesc(FMT, 128, BF, 0, B_MN);
+  // 3xTF32 MMA1 reads the hi and lo W_up planes (adjacent in the stage) as
+  // one N = 2*BF operand: D[:, 0:BF] += Xhi*Whi, D[:, BF:2BF] += Xhi*Wlo,
+  // then D[:, 0:BF] += Xlo*Whi; the GELU warps add the two halves.
+  static constexpr uint32_t IDESC1 = make_idesc(FMT, 128, kTF32 ? 2 * BF : BF, 0, B_MN);
+  static constexpr uint32_t IDESC1_LO = make_idesc(FMT, 128, BF, 0, B_MN);
   static constexpr uint32_t IDESC2 = make_idesc(FMT, 128, D, 0, B_MN);
+  static constexpr int EPI_WARPS = 8;  // two per TMEM lane quadrant
+  static constexpr int EPI_THREADS = EPI_WARPS * 32;
+  static constexpr int THREADS = 64 + EPI_THREADS;
   static constexpr uint32_t TX1 = S1_BYTES;
   static constexpr uint32_t TX2 = S2_BYTES;
 
   static_assert(NS >= 2, "shared memory too small for two ring stages");
-  static_assert(D % SK == 0 && BF % SK == 0, "tile shape");
-  static_assert(D + 2 * HCOLS <= TMEM_COLS, "TMEM budget");
+  static_assert(D % SK1 == 0 && BF % SK2 == 0, "tile shape");
+  static_assert(TMEM_USED <= TMEM_COLS, "TMEM budget");
+  static_assert(!kTF32 || 2 * BF <= 256, "concatenated MMA1 N");
   static_assert(D % 16 == 0 && D <= 256 && BF % 16 == 0 && BF <= 256, "UMMA N range");
   static_assert(SMEM <= kMaxSmemPerBlock, "shared memory budget");
 };
 
-// Monotone walk over (expert, 128-row block) pairs built from group sizes.
-struct BlockCursor {
+// Monotone walk over (expert, block) pairs built from group sizes; a block
+// is 2^SHIFT rows (128 for one CTA, 256 for a CTA pair).
+template <int SHIFT>
+struct BlockCursorT {
   int e = -1;
   int blk_begin = 0;
   int nblk = 0;
@@ -113,20 +153,54 @@ struct BlockCursor {
       const int rem = M - row_begin;
       g = g > rem ? (rem > 0 ? rem : 0) : g;
       rows = g;
-      nblk = (g + 127) >> 7;
+      nblk = (g + (1 << SHIFT) - 1) >> SHIFT;
     }
     return true;
   }
 };
+using BlockCursor = BlockCursorT<7>;
+
+// Drains a 32-row x 32-column block of Y (this warp's TMEM lanes) to global
+// memory.  tcgen05.ld gives each thread one row; the block goes through a
+// per-warp 4 KB shared-memory tile (16-byte chunks XOR-swizzled by row, so
+// both the writes and the reads are bank-conflict free) and leaves as
+// row-contiguous 128-byte stores, masked per row at the expert's end.
+template <int D>
+__device__ __forceinline__ void store_y_block(uint32_t taddr, float4* stage, float* y, int row_base, int row_end,
+                                              int c0, uint32_t lane, bool atomic) {
+  uint32_t v[32];
+  tmem_ld32(taddr, v);
+  tmem_ld_wait();
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    stage[lane * 8 + (k ^ (lane & 7))] = make_float4(__uint_as_float(v[4 * k]), __uint_as_float(v[4 * k + 1]),
+                                                     __uint_as_float(v[4 * k + 2]), __uint_as_float(v[4 * k + 3]));
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = 4 * i + (int)(lane >> 3);
+    const int k = (int)(lane & 7);
+    const float4 val = stage[r * 8 + (k ^ (r & 7))];
+    const int row = row_base + r;
+    if (row < row_end) {
+      float* dst = y + (size_t)row * D + c0 + 4 * k;
+      if (atomic)
+        red_add_v4(dst, val.x, val.y, val.z, val.w);
+      else
+        *reinterpret_cast<float4*>(dst) = val;
+    }
+  }
+  __syncwarp();
+}
 
 struct FusedMaps {
-  CUtensorMap x[2];   // X planes (bf16: [0] only; tf32: hi, lo when pre-split)
+  CUtensorMap x[2];   // X (raw, or pre-split hi / lo planes when streamed)
   CUtensorMap wu[2];  // W_up operand planes
   CUtensorMap wd[2];  // W_down operand planes
 };
 
 template <int MODE, int D, int BF, bool X_RES>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(64 + 256, 1)
     fused_mlp_small_kernel(const __grid_constant__ FusedMaps maps, const FusedParams p) {
   using C = FusedCfg<MODE, D, BF, X_RES>;
   extern __shared__ uint8_t smem_raw[];
@@ -134,16 +208,17 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   uint8_t* xbuf = smem;
   uint8_t* ring = smem + C::X_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + C::NS * C::STAGE);
-  uint64_t* full = bars;                 // [NS]
-  uint64_t* empty = bars + C::NS;        // [NS]
-  uint64_t* x_full = bars + 2 * C::NS;   // raw X landed
-  uint64_t* x_ready = x_full + 1;        // X operand (split) ready for MMA
-  uint64_t* x_empty = x_full + 2;        // last MMA1 of the unit finished
-  uint64_t* h_full = x_full + 3;         // [2] MMA1 done -> GELU
-  uint64_t* h_ready = x_full + 5;        // [2] GELU operand written -> MMA2
-  uint64_t* y_full = x_full + 7;         // last MMA2 done -> epilogue
-  uint64_t* y_empty = x_full + 8;        // epilogue drained Y_acc
+  float4* ystage = reinterpret_cast<float4*>(ring + C::NS * C::STAGE);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + C::NS * C::STAGE + C::Y_STAGE);
+  uint64_t* full = bars;                // [NS]
+  uint64_t* empty = bars + C::NS;       // [NS]
+  uint64_t* x_full = bars + 2 * C::NS;  // raw X landed
+  uint64_t* x_ready = x_full + 1;       // X operand (split) ready for MMA
+  uint64_t* x_empty = x_full + 2;       // last MMA1 of the unit finished
+  uint64_t* h_full = x_full + 3;        // [2] MMA1 done -> GELU
+  uint64_t* h_ready = x_full + 5;       // [2] GELU operand written -> MMA2
+  uint64_t* y_full = x_full + 7;        // last MMA2 done -> epilogue
+  uint64_t* y_empty = x_full + 8;       // epilogue drained Y_acc
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(x_full + 9);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -156,14 +231,14 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(empty + i, 1);
     }
     mbar_init(x_full, 1);
-    mbar_init(x_ready, 128);
+    mbar_init(x_ready, C::EPI_THREADS);
     mbar_init(x_empty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(h_full + i, 1);
-      mbar_init(h_ready + i, 128);
+      mbar_init(h_ready + i, C::EPI_THREADS);
     }
     mbar_init(y_full, 1);
-    mbar_init(y_empty, 128);
+    mbar_init(y_empty, C::EPI_THREADS);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -198,8 +273,11 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t ui = 0;
       bool ok = true;
       const uint64_t pol_w = l2_policy_evict_last();
+      int tp = 0;
       auto next_stage = [&]() -> bool {
         if (!mbar_wait(empty + stage, phase ^ 1u, abort_flag, p.status)) return false;
+        MOE_TRACE_EV(0, tp);
+        ++tp;
         return true;
       };
       auto advance = [&]() {
@@ -216,31 +294,42 @@ __global__ void __launch_bounds__(192, 1)
         const int fch0 = (u % S) * NCH;
         if constexpr (X_RES) {
           if (!mbar_wait(x_empty, (ui & 1u) ^ 1u, abort_flag, p.status)) break;
-          // Raw X (bf16 operand, or f32 to be split into hi/lo in place).
+          // Raw X (the bf16 operand, or f32 split in place by the GELU warps).
           mbar_arrive_expect_tx(x_full, C::X_PLANE);
           for (int s = 0; s < D / C::ATOM; ++s)
             tma_load_2d(xbuf + s * C::XBOX, &maps.x[0], x_full, s * C::ATOM, row0);
+          // Warm L2 with the next unit's X tile so its load at the end of this
+          // unit does not wait on HBM.
+          BlockCursor nxt = cur;
+          const int u_next = u + (int)gridDim.x;
+          if (nxt.seek(u_next / S, p.group_sizes, p.E, p.M)) {
+            const int nrow0 = nxt.row_begin + (u_next / S - nxt.blk_begin) * C::BM;
+            for (int s = 0; s < D / C::ATOM; ++s) tma_prefetch_l2_2d(&maps.x[0], s * C::ATOM, nrow0);
+          }
         }
         auto load_s1 = [&](int j, int s) -> bool {
           if (!next_stage()) return false;
           uint8_t* st = ring + stage * C::STAGE;
           mbar_arrive_expect_tx(full + stage, C::TX1);
           const int f0 = (fch0 + j) * BF;
-          if constexpr (!X_RES) {
-            for (int pl = 0; pl < C::PL; ++pl)
-              tma_load_2d(st + pl * C::XBOX, &maps.x[pl], full + stage, s * C::ATOM, row0);
-          }
-          uint8_t* w = st + C::S1_X;
-          if constexpr (C::kTF32) {
-            // W_up^T planes: rows (e, f), K = d contiguous; box {32, BF}.
-            for (int pl = 0; pl < C::PL; ++pl)
-              tma_load_2d_hint(w + pl * C::S1_WPLANE, &maps.wu[pl], full + stage, s * C::ATOM, e * p.F + f0,
-                               pol_w);
-          } else {
-            // W_up rows (e, d), N = f contiguous; box {64, 64} per 64-wide f block.
-            for (int nb = 0; nb < BF / C::ATOM; ++nb)
-              tma_load_2d_hint(w + nb * C::SK * 128, &maps.wu[0], full + stage, f0 + nb * C::ATOM,
-                               e * D + s * C::SK, pol_w);
+          for (int kb = 0; kb < C::KB1; ++kb) {
+            const int k0 = s * C::SK1 + kb * C::ATOM;  // first d of this k-box
+            uint8_t* sub = st + kb * C::S1_SUB;
+            if constexpr (!X_RES) {
+              for (int pl = 0; pl < C::PL; ++pl)
+                tma_load_2d(sub + pl * C::XBOX, &maps.x[pl], full + stage, k0, row0);
+            }
+            uint8_t* w = sub + C::S1_X;
+            if constexpr (C::kTF32) {
+              // W_up^T planes: rows (e, f), K = d contiguous; box {32, BF}.
+              for (int pl = 0; pl < C::PL; ++pl)
+                tma_load_2d_hint(w + pl * C::S1_WPLANE, &maps.wu[pl], full + stage, k0, e * p.F + f0, pol_w);
+            } else {
+              // W_up rows (e, d), N = f contiguous; box {64, 64} per 64-wide f block.
+              for (int nb = 0; nb < BF / C::ATOM; ++nb)
+                tma_load_2d_hint(w + nb * C::ATOM * 128, &maps.wu[0], full + stage, f0 + nb * C::ATOM, e * D + k0,
+                                 pol_w);
+            }
           }
           advance();
           return true;
@@ -249,7 +338,7 @@ __global__ void __launch_bounds__(192, 1)
           if (!next_stage()) return false;
           uint8_t* st = ring + stage * C::STAGE;
           mbar_arrive_expect_tx(full + stage, C::TX2);
-          const int f0 = (fch0 + j) * BF + t * C::SK;
+          const int f0 = (fch0 + j) * BF + t * C::SK2;
           if constexpr (C::kTF32) {
             // W_down^T planes: rows (e, d), K = f contiguous; box {32, D}.
             for (int pl = 0; pl < C::PL; ++pl)
@@ -257,7 +346,7 @@ __global__ void __launch_bounds__(192, 1)
           } else {
             // W_down rows (e, f), N = d contiguous; box {64, 64} per 64-wide d block.
             for (int nb = 0; nb < D / C::ATOM; ++nb)
-              tma_load_2d_hint(st + nb * C::SK * 128, &maps.wd[0], full + stage, nb * C::ATOM, e * p.F + f0,
+              tma_load_2d_hint(st + nb * C::SK2 * 128, &maps.wd[0], full + stage, nb * C::ATOM, e * p.F + f0,
                                pol_w);
           }
           advance();
@@ -272,8 +361,8 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------ MMA issuer (whole warp)
+    {
       BlockCursor cur;
       int stage = 0;
       uint32_t phase = 0;
@@ -281,9 +370,13 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t hcount = 0;  // hidden chunks issued (selects the TMEM buffer)
       bool ok = true;
       const uint32_t t_y = tmem_base;
+      int tm = 0;
       auto wait_full = [&]() -> bool {
-        if (!mbar_wait(full + stage, phase, abort_flag, p.status)) return false;
+        MOE_TRACE_EV(1, 2 * tm);
+        if (!mbar_wait_warp(full + stage, phase, abort_flag, p.status)) return false;
         tc_fence_after();
+        MOE_TRACE_EV(1, 2 * tm + 1);
+        ++tm;
         return true;
       };
       auto release = [&]() {
@@ -297,33 +390,39 @@ __global__ void __launch_bounds__(192, 1)
         const int gb = u / S;
         if (!cur.seek(gb, p.group_sizes, p.E, p.M)) break;
         if constexpr (X_RES) {
-          if (!mbar_wait(x_ready, ui & 1u, abort_flag, p.status)) break;
+          if (!mbar_wait_warp(x_ready, ui & 1u, abort_flag, p.status)) break;
           tc_fence_after();
         }
-        const uint32_t xbase = smem_u32(xbuf);
+        // Descriptor start addresses advance in 16-byte units: adding
+        // (bytes >> 4) to a descriptor moves its operand within the 14-bit
+        // address field (all offsets here stay inside one stage / X tile).
+        const uint64_t x_desc0 = make_sdesc(smem_u32(xbuf), 16, 1024);
         auto mma1 = [&](int j) -> bool {
           const uint32_t hb = (hcount + j) & 1u;
           const uint32_t d_tmem = tmem_base + D + hb * C::HCOLS;
           for (int s = 0; s < C::N1; ++s) {
             if (!wait_full()) return false;
             const uint32_t st = smem_u32(ring + stage * C::STAGE);
-            for (int ki = 0; ki < C::SK / C::KI; ++ki) {
-              uint64_t a[2], b[2];
-              for (int pl = 0; pl < C::PL; ++pl) {
-                const uint32_t xa = X_RES ? xbase + pl * C::X_PLANE + s * C::XBOX + ki * 32
-                                          : st + pl * C::XBOX + ki * 32;
-                a[pl] = make_sdesc(xa, 16, 1024);
-                if constexpr (C::kTF32) {
-                  b[pl] = make_sdesc(st + C::S1_X + pl * C::S1_WPLANE + ki * 32, 16, 1024);
-                } else {
-                  b[pl] = make_sdesc(st + C::S1_X + ki * (C::KI * 128), C::SK * 128, 1024);
+            const uint64_t st_desc = C::kTF32 ? make_sdesc(st, 16, 1024) : make_sdesc(st, C::ATOM * 128, 1024);
+#pragma unroll
+            for (int kb = 0; kb < C::KB1; ++kb) {
+              const int kbox = s * C::KB1 + kb;  // k-box index along D
+#pragma unroll
+              for (int ki = 0; ki < C::ATOM / C::KI; ++ki) {
+                const uint64_t a0 = X_RES ? x_desc0 + (uint64_t)((kbox * C::XBOX + ki * 32) >> 4)
+                                          : st_desc + (uint64_t)((kb * C::S1_SUB + ki * 32) >> 4);
+                const uint64_t b0 =
+                    C::kTF32 ? st_desc + (uint64_t)((kb * C::S1_SUB + C::S1_X + ki * 32) >> 4)
+                             : st_desc + (uint64_t)((kb * C::S1_SUB + C::S1_X + ki * (C::KI * 128)) >> 4);
+                const uint32_t acc0 = (kbox > 0 || ki > 0) ? 1u : 0u;
+                umma_ss<C::kTF32 ? Kind::TF32 : Kind::F16>(d_tmem, a0, b0, C::IDESC1, acc0);
+                if constexpr (C::XLO_TMEM) {
+                  const uint32_t xlo = tmem_base + C::XLO_COL + kbox * C::ATOM + ki * C::KI;
+                  umma_ts<Kind::TF32>(d_tmem, xlo, b0, C::IDESC1_LO, 1u);
+                } else if constexpr (C::kTF32) {
+                  const uint64_t a1 = st_desc + (uint64_t)((kb * C::S1_SUB + C::XBOX + ki * 32) >> 4);
+                  umma_ss<Kind::TF32>(d_tmem, a1, b0, C::IDESC1_LO, 1u);
                 }
-              }
-              const uint32_t acc0 = (s > 0 || ki > 0) ? 1u : 0u;
-              umma_ss<C::kTF32 ? Kind::TF32 : Kind::F16>(d_tmem, a[0], b[0], C::IDESC1, acc0);
-              if constexpr (C::kTF32) {
-                umma_ss<Kind::TF32>(d_tmem, a[0], b[1], C::IDESC1, 1u);
-                umma_ss<Kind::TF32>(d_tmem, a[1], b[0], C::IDESC1, 1u);
               }
             }
             release();
@@ -334,31 +433,30 @@ __global__ void __launch_bounds__(192, 1)
         auto mma2 = [&](int j) -> bool {
           const uint32_t hb = (hcount + j) & 1u;
           const uint32_t use = (hcount + j) >> 1;  // uses of this buffer so far
-          if (!mbar_wait(h_ready + hb, use & 1u, abort_flag, p.status)) return false;
+          MOE_TRACE_EV(3, (int)(2 * (hcount + j)));
+          if (!mbar_wait_warp(h_ready + hb, use & 1u, abort_flag, p.status)) return false;
           tc_fence_after();
+          MOE_TRACE_EV(3, (int)(2 * (hcount + j) + 1));
           if (j == 0) {
-            if (!mbar_wait(y_empty, (ui & 1u) ^ 1u, abort_flag, p.status)) return false;
+            if (!mbar_wait_warp(y_empty, (ui & 1u) ^ 1u, abort_flag, p.status)) return false;
             tc_fence_after();
           }
           const uint32_t h_tmem = tmem_base + D + hb * C::HCOLS;
           for (int t = 0; t < C::N2; ++t) {
             if (!wait_full()) return false;
             const uint32_t st = smem_u32(ring + stage * C::STAGE);
-            for (int ki = 0; ki < C::SK / C::KI; ++ki) {
-              const uint32_t kcol = (t * C::SK + ki * C::KI) * C::ESZ / 4;
-              uint64_t b[2];
-              for (int pl = 0; pl < C::PL; ++pl) {
-                if constexpr (C::kTF32) {
-                  b[pl] = make_sdesc(st + pl * C::S2_WPLANE + ki * 32, 16, 1024);
-                } else {
-                  b[pl] = make_sdesc(st + ki * (C::KI * 128), C::SK * 128, 1024);
-                }
-              }
+            const uint64_t st_desc = C::kTF32 ? make_sdesc(st, 16, 1024) : make_sdesc(st, C::SK2 * 128, 1024);
+#pragma unroll
+            for (int ki = 0; ki < C::SK2 / C::KI; ++ki) {
+              const uint32_t kcol = (t * C::SK2 + ki * C::KI) * C::ESZ / 4;
+              const uint64_t b0 = C::kTF32 ? st_desc + (uint64_t)((ki * 32) >> 4)
+                                           : st_desc + (uint64_t)((ki * (C::KI * 128)) >> 4);
               const uint32_t acc0 = (j > 0 || t > 0 || ki > 0) ? 1u : 0u;
-              umma_ts<C::kTF32 ? Kind::TF32 : Kind::F16>(t_y, h_tmem + kcol, b[0], C::IDESC2, acc0);
+              umma_ts<C::kTF32 ? Kind::TF32 : Kind::F16>(t_y, h_tmem + kcol, b0, C::IDESC2, acc0);
               if constexpr (C::kTF32) {
-                umma_ts<Kind::TF32>(t_y, h_tmem + kcol, b[1], C::IDESC2, 1u);
-                umma_ts<Kind::TF32>(t_y, h_tmem + BF + kcol, b[0], C::IDESC2, 1u);
+                const uint64_t b1 = st_desc + (uint64_t)((C::S2_WPLANE + ki * 32) >> 4);
+                umma_ts<Kind::TF32>(t_y, h_tmem + kcol, b1, C::IDESC2, 1u);
+                umma_ts<Kind::TF32>(t_y, h_tmem + BF + kcol, b0, C::IDESC2, 1u);
               }
             }
             release();
@@ -377,10 +475,12 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ------------------------------------------------------------ GELU / epilogue warps
-    const uint32_t q = warp & 3u;  // TMEM lane quadrant this warp may access
+    const uint32_t q = warp & 3u;            // TMEM lane quadrant this warp may access
+    const uint32_t half = (warp - 2u) >> 2;  // which half of the columns
     const uint32_t lane_base = tmem_base + ((q * 32u) << 16);
     const int erow = (int)(q * 32u + lane);  // row inside the 128-row block
-    const int etid = (int)threadIdx.x - 64;  // 0..127
+    const int etid = (int)threadIdx.x - 64;  // 0..EPI_THREADS-1
+    constexpr int NT = C::EPI_THREADS;
 
     if (etid == 0 && blockIdx.x == 0) {
       for (int e = 0; e < p.E; ++e)
@@ -400,7 +500,7 @@ __global__ void __launch_bounds__(192, 1)
       }
       const size_t n4 = (size_t)(p.M - total) * D / 4;
       float4* base = reinterpret_cast<float4*>(p.y + (size_t)total * D);
-      for (size_t i = (size_t)blockIdx.x * 128 + etid; i < n4; i += (size_t)gridDim.x * 128)
+      for (size_t i = (size_t)blockIdx.x * NT + etid; i < n4; i += (size_t)gridDim.x * NT)
         base[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
 
@@ -413,27 +513,37 @@ __global__ void __launch_bounds__(192, 1)
       r = __all_sync(0xffffffffu, r);
       return r;
     };
-    // In-place split of the resident f32 X tile into tf32 hi (kept in plane 0)
-    // and lo (written to plane 1); layout-agnostic because it is elementwise.
+    // Split of the resident f32 X tile: hi = x rounded toward zero to tf32,
+    // written back in place (shared memory, swizzled K-major layout); lo =
+    // x - hi, written to this thread's TMEM lane as MMA1's second A operand.
+    // Each thread owns one row and half of its D columns.
     auto split_x = [&](uint32_t uidx) -> bool {
       if (!warp_wait(x_full, uidx & 1u)) return false;
-      float4* hi = reinterpret_cast<float4*>(xbuf);
-      float4* lo = reinterpret_cast<float4*>(xbuf + C::X_PLANE);
-      for (int i = etid; i < C::X_PLANE / 16; i += 128) {
-        float4 v = hi[i];
-        float4 h, l;
-        h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-        h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-        h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-        h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
-        l.x = v.x - h.x;
-        l.y = v.y - h.y;
-        l.z = v.z - h.z;
-        l.w = v.w - h.w;
-        hi[i] = h;
-        lo[i] = l;
+      const uint32_t rsw = (uint32_t)erow & 7u;
+#pragma unroll 1
+      for (int k0 = half * (D / 2); k0 < (int)(half + 1) * (D / 2); k0 += 32) {
+        uint8_t* rowp = xbuf + (k0 / C::ATOM) * C::XBOX + erow * 128;
+        uint32_t lo[32];
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          float4* ptr = reinterpret_cast<float4*>(rowp + ((g ^ rsw) << 4));
+          float4 v = *ptr;
+          float4 h;
+          h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+          h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+          h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+          h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+          lo[4 * g + 0] = __float_as_uint(v.x - h.x);
+          lo[4 * g + 1] = __float_as_uint(v.y - h.y);
+          lo[4 * g + 2] = __float_as_uint(v.z - h.z);
+          lo[4 * g + 3] = __float_as_uint(v.w - h.w);
+          *ptr = h;
+        }
+        tmem_st32(lane_base + C::XLO_COL + k0, lo);
       }
+      tmem_st_wait();
       fence_proxy_async_smem();
+      tc_fence_before();
       mbar_arrive(x_ready);
       return true;
     };
@@ -459,35 +569,45 @@ __global__ void __launch_bounds__(192, 1)
           break;
         }
         tc_fence_after();
+        if (warp == 2 && lane == 0) MOE_TRACE_EV(2, (int)(2 * (hcount + j)));
         const uint32_t hcol = D + hb * C::HCOLS;
+        if constexpr (C::kTF32) {
+          // Columns [half*BF/2, +BF/2): sum the two MMA1 halves, GELU, split.
 #pragma unroll 1
-        for (int c0 = 0; c0 < BF; c0 += 32) {
-          uint32_t v[32];
-          tmem_ld32(lane_base + hcol + c0, v);
-          tmem_ld_wait();
-          if constexpr (C::kTF32) {
-            uint32_t lo[32];
+          for (int c0 = half * (BF / 2); c0 < (int)(half + 1) * (BF / 2); c0 += 32) {
+            uint32_t a[32], b[32];
+            tmem_ld32(lane_base + hcol + c0, a);
+            tmem_ld32(lane_base + hcol + BF + c0, b);
+            tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const float g = gelu_tanh_accurate(__uint_as_float(v[i]));
-              const uint32_t hbits = __float_as_uint(g) & 0xFFFFE000u;
-              lo[i] = __float_as_uint(g - __uint_as_float(hbits));
-              v[i] = hbits;
-            }
-            tmem_st32(lane_base + hcol + c0, v);
-            tmem_st32(lane_base + hcol + BF + c0, lo);
-          } else {
+            for (int i = 0; i < 32; i += 2) gelu_split_tf32x2(a[i], a[i + 1], b[i], b[i + 1]);
+            tmem_st32(lane_base + hcol + c0, a);
+            tmem_st32(lane_base + hcol + BF + c0, b);
+          }
+        } else {
+          // The packed bf16 operand overwrites the accumulator columns, so
+          // both warps of a quadrant finish reading before either writes.
+          constexpr int CW = BF / 2;  // accumulator columns per warp
+          uint32_t v[CW];
+#pragma unroll
+          for (int c = 0; c < CW; c += 32)
+            tmem_ld32(lane_base + hcol + half * CW + c, *reinterpret_cast<uint32_t(*)[32]>(v + c));
+          tmem_ld_wait();
+          asm volatile("bar.sync %0, 64;" ::"r"(1 + (int)q) : "memory");
+#pragma unroll
+          for (int c = 0; c < CW; c += 32) {
             uint32_t pk[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i)
-              pk[i] = pack_bf16x2(gelu_tanh_fast(__uint_as_float(v[2 * i])),
-                                  gelu_tanh_fast(__uint_as_float(v[2 * i + 1])));
-            tmem_st16(lane_base + hcol + c0 / 2, pk);
+              pk[i] = pack_bf16x2(gelu_tanh_fast(__uint_as_float(v[c + 2 * i])),
+                                  gelu_tanh_fast(__uint_as_float(v[c + 2 * i + 1])));
+            tmem_st16(lane_base + hcol + (half * CW + c) / 2, pk);
           }
         }
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(h_ready + hb);
+        if (warp == 2 && lane == 0) MOE_TRACE_EV(2, (int)(2 * (hcount + j) + 1));
       }
       if (!ok) break;
       hcount += NCH;
@@ -502,35 +622,16 @@ __global__ void __launch_bounds__(192, 1)
         if (!ok) break;
       }
 
-      // Y epilogue.
+      // Y epilogue: this warp drains columns [half*D/2, +D/2) of its rows.
       if (!warp_wait(y_full, ui & 1u)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const int row = row0 + erow;
-      const bool valid = row < row_end;
-      float* yrow = p.y + (size_t)row * D;
+      float4* wstage = ystage + (warp - 2u) * 256u;
 #pragma unroll 1
-      for (int c0 = 0; c0 < D; c0 += 32) {
-        uint32_t v[32];
-        tmem_ld32(lane_base + c0, v);
-        tmem_ld_wait();
-        if (valid) {
-          if (p.atomic_out) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 4)
-              red_add_v4(yrow + c0 + i, __uint_as_float(v[i]), __uint_as_float(v[i + 1]),
-                         __uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; i += 4)
-              *reinterpret_cast<float4*>(yrow + c0 + i) =
-                  make_float4(__uint_as_float(v[i]), __uint_as_float(v[i + 1]), __uint_as_float(v[i + 2]),
-                              __uint_as_float(v[i + 3]));
-          }
-        }
-      }
+      for (int c0 = half * (D / 2); c0 < (int)(half + 1) * (D / 2); c0 += 32)
+        store_y_block<D>(lane_base + c0, wstage, p.y, row0 + (int)(q * 32u), row_end, c0, lane, p.atomic_out != 0);
       tc_fence_before();
       mbar_arrive(y_empty);
 

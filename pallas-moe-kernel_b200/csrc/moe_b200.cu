@@ -10,7 +10,7 @@
 #include <mutex>
 
 #include "../../include/moe_b200.h"
-#include "fused_small.cuh"
+#include "fused_pair.cuh"
 
 namespace moe {
 __device__ int g_status = 0;
@@ -35,6 +35,8 @@ static int fail(int code, const char* fmt, ...) {
 // ------------------------------------------------------------------ tuning
 static int64_t g_tune_splits = 0;
 static int64_t g_tune_ctas = 0;
+static int64_t g_tune_trace = 0;  // device address of a trace buffer (MOE_TRACE builds)
+static int64_t g_tune_pair = 0;   // 0 auto, 1 single-CTA kernel, 2 CTA-pair kernel
 
 // ------------------------------------------------------------------ driver entry point
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -78,7 +80,8 @@ static int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType d
 // ------------------------------------------------------------------ device info
 struct DevInfo {
   int sms = 0;
-  bool attr_set[16] = {};
+  bool attr_set[32] = {};
+  int pairs[8] = {};  // co-resident CTA pairs per pair-kernel variant (0 = not queried)
 };
 static DevInfo g_dev[64];
 static std::mutex g_dev_mu;
@@ -192,7 +195,7 @@ static int launch_small(const FusedMaps& maps, const FusedParams& prm, int ctas,
     MOE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
     di->attr_set[slot] = true;
   }
-  kern<<<ctas, 192, Cfg::SMEM, st>>>(maps, prm);
+  kern<<<ctas, Cfg::THREADS, Cfg::SMEM, st>>>(maps, prm);
   MOE_CUDA_TRY(cudaGetLastError());
   return 0;
 }
@@ -228,6 +231,46 @@ static int prepare_small(const void* w_up, const void* w_down, int D, int F, int
 }
 
 // Main fused launch; for 3xTF32 the weight planes must already be in `ws`.
+static bool pair_supported(int D, int dtype) {
+  if (dtype == MOE_DTYPE_F32) return D == 64 || D == 128;
+  if (dtype == MOE_DTYPE_BF16) return D == 128 || D == 256;
+  return false;
+}
+
+template <int MODE, int D, int BF>
+static int launch_pair(const FusedMaps& maps, const FusedParams& prm, int pairs_req, DevInfo* di, cudaStream_t st) {
+  using Cfg = PairCfg<MODE, D, BF>;
+  auto kern = fused_mlp_pair_kernel<MODE, D, BF>;
+  constexpr int slot = 16 + MODE * 3 + (D == 64 ? 0 : D == 128 ? 1 : 2);
+  constexpr int pslot = MODE * 3 + (D == 64 ? 0 : D == 128 ? 1 : 2);
+  static_assert(slot < 32 && pslot < 8, "attribute slot");
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!di->attr_set[slot]) {
+    MOE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    cfg.gridDim = dim3(2 * (di->sms / 2));
+    int clusters = 0;
+    MOE_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg));
+    if (clusters < 1) return fail(MOE_ERR_CUDA, "no CTA pair fits on this device");
+    di->pairs[pslot] = clusters;
+    di->attr_set[slot] = true;
+  }
+  int pairs = di->pairs[pslot];
+  if (pairs_req > 0 && pairs_req < pairs) pairs = pairs_req;
+  cfg.gridDim = dim3(2 * pairs);
+  MOE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, maps, prm));
+  return 0;
+}
+
 static int run_small(const void* x, const void* w_up, const void* w_down, const int32_t* gs, float* y, int64_t M,
                      int D, int F, int E, int dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
   int dev;
@@ -237,14 +280,20 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
   if (int r = check_workspace(plan, ws, ws_bytes)) return r;
 
   const int nch_total = F / plan.bf;
+  const bool pair = g_tune_pair == 2 || (g_tune_pair == 0 && pair_supported(D, dtype));
+  if (pair && !pair_supported(D, dtype))
+    return fail(MOE_ERR_INVALID_ARG, "CTA-pair kernel not available for D=%d dtype=%d", D, dtype);
   int splits = 1;
   if (g_tune_splits > 0) {
     splits = (int)g_tune_splits;
     if (nch_total % splits != 0)
       return fail(MOE_ERR_INVALID_ARG, "tuning splits=%d does not divide %d chunks", splits, nch_total);
   } else {
-    const int64_t blocks_est = (M + 127) / 128;
-    while (blocks_est * splits < di->sms && nch_total % (splits * 2) == 0 && splits * 2 <= nch_total) splits *= 2;
+    // Enough units for every SM (or SM pair) while each unit keeps >= 1 chunk.
+    const int rows_per_unit = pair ? 256 : 128;
+    const int64_t workers = pair ? di->sms / 2 : di->sms;
+    const int64_t blocks_est = (M + rows_per_unit - 1) / rows_per_unit;
+    while (blocks_est * splits < workers && nch_total % (splits * 2) == 0 && splits * 2 <= nch_total) splits *= 2;
   }
   int ctas = g_tune_ctas > 0 ? (int)g_tune_ctas : di->sms;
 
@@ -261,6 +310,7 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
   prm.chunks_per_split = nch_total / splits;
   prm.atomic_out = splits > 1 ? 1 : 0;
   prm.status = status;
+  prm.trace = reinterpret_cast<unsigned long long*>(g_tune_trace);
 
   FusedMaps maps;
   memset(&maps, 0, sizeof(maps));
@@ -271,6 +321,11 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
     if (int r = make_map_2d(&maps.x[0], x, BF16, 2, (uint64_t)M, D, 64, 128)) return r;
     if (int r = make_map_2d(&maps.wu[0], w_up, BF16, 2, (uint64_t)E * D, F, 64, 64)) return r;
     if (int r = make_map_2d(&maps.wd[0], w_down, BF16, 2, (uint64_t)E * F, D, 64, 64)) return r;
+    if (pair) {
+      const int pairs_req = g_tune_ctas > 0 ? (int)(g_tune_ctas / 2) : 0;
+      if (D == 128) return launch_pair<kModeBF16, 128, 128>(maps, prm, pairs_req, di, st);
+      return launch_pair<kModeBF16, 256, 128>(maps, prm, pairs_req, di, st);
+    }
     switch (D) {
       case 64: return launch_small<kModeBF16, 64, 128, true>(maps, prm, ctas, di, st);
       case 128: return launch_small<kModeBF16, 128, 128, true>(maps, prm, ctas, di, st);
@@ -287,8 +342,15 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
   float* wd_lo = wd_hi + wsz;
   if (int r = make_map_2d(&maps.wu[0], wu_hi, F32, 4, (uint64_t)E * F, D, 32, plan.bf)) return r;
   if (int r = make_map_2d(&maps.wu[1], wu_lo, F32, 4, (uint64_t)E * F, D, 32, plan.bf)) return r;
-  if (int r = make_map_2d(&maps.wd[0], wd_hi, F32, 4, (uint64_t)E * D, F, 32, D)) return r;
-  if (int r = make_map_2d(&maps.wd[1], wd_lo, F32, 4, (uint64_t)E * D, F, 32, D)) return r;
+  const uint32_t wd_box_rows = pair ? D / 2 : D;
+  if (int r = make_map_2d(&maps.wd[0], wd_hi, F32, 4, (uint64_t)E * D, F, 32, wd_box_rows)) return r;
+  if (int r = make_map_2d(&maps.wd[1], wd_lo, F32, 4, (uint64_t)E * D, F, 32, wd_box_rows)) return r;
+  if (pair) {
+    if (int r = make_map_2d(&maps.x[0], x, F32, 4, (uint64_t)M, D, 32, 128)) return r;
+    const int pairs_req = g_tune_ctas > 0 ? (int)(g_tune_ctas / 2) : 0;
+    if (D == 64) return launch_pair<kModeTF32x3, 64, 64>(maps, prm, pairs_req, di, st);
+    return launch_pair<kModeTF32x3, 128, 64>(maps, prm, pairs_req, di, st);
+  }
   if (plan.x_res) {
     if (int r = make_map_2d(&maps.x[0], x, F32, 4, (uint64_t)M, D, 32, 128)) return r;
   } else {
@@ -329,6 +391,13 @@ int moe_set_tuning(int32_t key, int64_t value) {
       return 0;
     case 2:
       g_tune_ctas = value;
+      return 0;
+    case 3:
+      g_tune_trace = value;
+      return 0;
+    case 4:
+      if (value > 2) return fail(MOE_ERR_INVALID_ARG, "pair mode must be 0, 1 or 2");
+      g_tune_pair = value;
       return 0;
   }
   return fail(MOE_ERR_INVALID_ARG, "unknown tuning key %d", key);

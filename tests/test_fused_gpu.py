@@ -62,18 +62,23 @@ def _oracle_rows(x, w_up, w_down, gs, rows):
     return out
 
 
+def _reset():
+    for key in (1, 2, 4):
+        _lib.set_tuning(key, 0)
+
+
 @pytest.fixture(autouse=True)
 def _reset_tuning():
-    _lib.set_tuning(1, 0)
-    _lib.set_tuning(2, 0)
+    _reset()
     _lib.device_status(reset=True)
     yield
-    _lib.set_tuning(1, 0)
-    _lib.set_tuning(2, 0)
+    _reset()
     assert _lib.device_status(reset=True) == 0
 
 
-def test_c1_fp32_full():
+@pytest.mark.parametrize("family", [1, 2])
+def test_c1_fp32_full(family):
+    _lib.set_tuning(4, family)
     cfg = CONFIGS["c1"]
     gs = config_group_sizes(cfg, seed=0)
     x, wu, wd = make_inputs_numpy(cfg.M, cfg.D, cfg.F, cfg.E, seed=0)
@@ -104,12 +109,19 @@ def test_c3_fp32_zipf_stress(M):
 @pytest.mark.parametrize("D", [64, 128, 256])
 def test_bf16_small_d(D):
     M, F, E = 2048, 512, 4
+    _lib.set_tuning(4, 1)
+    gs = make_group_sizes(M, E)
+    x, wu, wd = make_inputs_numpy(M, D, F, E, seed=D)
+    y1, *_ = _run(x, wu, wd, gs, "bf16")
+    _lib.set_tuning(4, 0)
     gs = make_group_sizes(M, E)
     x, wu, wd = make_inputs_numpy(M, D, F, E, seed=D)
     y, x, wu, wd = _run(x, wu, wd, gs, "bf16")
     _check(y, x, wu, wd, gs, "bf16")
+    _check(y1, x, wu, wd, gs, "bf16")
 
 
+@pytest.mark.parametrize("family", [1, 2])
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
 @pytest.mark.parametrize("gs", [
     [0, 0, 300, 0],            # empty experts around one non-empty expert
@@ -118,8 +130,9 @@ def test_bf16_small_d(D):
     [0, 0, 0, 0],              # nothing routed: all-zero output
     [200, 100, 50, 26],        # sum < M: trailing rows must be zero
 ])
-def test_ragged_edges(dtype, gs):
+def test_ragged_edges(dtype, gs, family):
     M, D, F, E = 512, 128, 256, 4
+    _lib.set_tuning(4, family)
     x, wu, wd = make_inputs_numpy(M, D, F, E, seed=7)
     out = torch.full((M, D), float("nan"), device="cuda:0")  # poisoned output
     y, x, wu, wd = _run(x, wu, wd, gs, dtype, out=out)
@@ -132,15 +145,18 @@ def test_ragged_edges(dtype, gs):
         assert m["l2_relative_error"] <= TOL[dtype], m
 
 
+@pytest.mark.parametrize("family", [1, 2])
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
-@pytest.mark.parametrize("splits,ctas", [(1, 3), (2, 0), (4, 5)])
-def test_schedule_variants(dtype, splits, ctas):
-    """Few persistent CTAs (many units each: barrier phases wrap) and F split
-    across CTAs (reduce-add output)."""
+@pytest.mark.parametrize("splits,ctas", [(1, 6), (2, 0), (4, 10)])
+def test_schedule_variants(dtype, splits, ctas, family):
+    """Both kernel families (1: one CTA per 128 rows, 2: CTA pairs per 256
+    rows), few persistent CTAs (many units each: barrier phases wrap) and F
+    split across CTAs (reduce-add output)."""
     M, D, F, E = 1536, 128, 512, 3
     gs = make_group_sizes_pattern(M, E, "skewed")
     _lib.set_tuning(1, splits)
     _lib.set_tuning(2, ctas)
+    _lib.set_tuning(4, family)
     x, wu, wd = make_inputs_numpy(M, D, F, E, seed=11)
     y, x, wu, wd = _run(x, wu, wd, gs, dtype)
     _check(y, x, wu, wd, gs, dtype)
