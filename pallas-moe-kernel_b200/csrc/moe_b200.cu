@@ -280,7 +280,10 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
   if (int r = check_workspace(plan, ws, ws_bytes)) return r;
 
   const int nch_total = F / plan.bf;
-  const bool pair = g_tune_pair == 2 || (g_tune_pair == 0 && pair_supported(D, dtype));
+  // The single-CTA family is the automatic choice: measured faster on B200
+  // for D <= 256 (the pair family trades half the weight bytes per SM for a
+  // wider X_lo pass and cross-SM hand-offs).  Pairs stay selectable.
+  const bool pair = g_tune_pair == 2;
   if (pair && !pair_supported(D, dtype))
     return fail(MOE_ERR_INVALID_ARG, "CTA-pair kernel not available for D=%d dtype=%d", D, dtype);
   int splits = 1;
