@@ -167,7 +167,7 @@ using BlockCursor = BlockCursorT<7>;
 // row-contiguous 128-byte stores, masked per row at the expert's end.
 template <int D>
 __device__ __forceinline__ void store_y_block(uint32_t taddr, float4* stage, float* y, int row_base, int row_end,
-                                              int c0, uint32_t lane, bool atomic) {
+                                              int c0, uint32_t lane, bool atomic, int ld = D) {
   uint32_t v[32];
   tmem_ld32(taddr, v);
   tmem_ld_wait();
@@ -183,7 +183,7 @@ __device__ __forceinline__ void store_y_block(uint32_t taddr, float4* stage, flo
     const float4 val = stage[r * 8 + (k ^ (r & 7))];
     const int row = row_base + r;
     if (row < row_end) {
-      float* dst = y + (size_t)row * D + c0 + 4 * k;
+      float* dst = y + (size_t)row * ld + c0 + 4 * k;
       if (atomic)
         red_add_v4(dst, val.x, val.y, val.z, val.w);
       else

@@ -1,0 +1,318 @@
+// Persistent grouped GEMM over ragged expert row blocks on CTA pairs
+// (2-SM tcgen05 MMA), sm_100a.  The large-D expert MLP runs as two launches:
+//
+//   up   : H[rows of e, :] = GELU_tanh(X[rows of e, :] @ W_up[e])   (bf16 H)
+//   down : Y[rows of e, :] = H[rows of e, :] @ W_down[e]            (f32 Y)
+//
+// A (X or H, row-major, K-major) tiles of 128 rows come from each CTA of the
+// pair; B (W_up[e] (D, F) or W_down[e] (F, D), N contiguous: MN-major) tiles
+// are split along N between the two CTAs, so each SM streams half of every
+// weight tile.  The leader CTA issues tcgen05.mma.cta_group::2 with
+// M = 256, N = 256, K = 16 into TMEM; accumulators are double-buffered (2 x
+// 256 columns) so the epilogue of one tile overlaps the MMAs of the next.
+//
+// Tiles are (expert, 256-row block, 256-column block), enumerated on the
+// device from the group sizes (no padded grid; the last row block of an
+// expert is row-masked at the store), walked by every pair with a static
+// stride and rasterised in groups of GM row blocks so that the pairs running
+// at the same time share A and B tiles in L2.
+//
+// Warp roles (192 threads): warp 0 TMA producer (both CTAs), warp 1 TMEM
+// owner + MMA issuer (leader), warps 2..5 epilogue (one TMEM lane quadrant
+// each; both CTAs).
+#pragma once
+#include "fused_small.cuh"
+
+namespace moe {
+
+struct GemmParams {
+  const int32_t* group_sizes;
+  void* out;          // H (bf16, [M, N]) or Y (f32, [M, N])
+  int M;              // rows of A / out
+  int E;
+  int N;              // output columns (F for up, D for down)
+  int K;              // reduction (D for up, F for down)
+  int k_rows_per_e;   // rows of the 2-D B tensor map per expert (= K)
+  int group_m;        // tile rasterisation group (row blocks)
+  int* status;
+};
+
+template <int EPI>  // 0: GELU -> bf16 H, 1: f32 Y
+struct GemmCfg {
+  static constexpr int BM = 128;   // rows per CTA (256 per pair)
+  static constexpr int BN = 256;   // output columns per tile (128 per CTA of B)
+  static constexpr int BK = 64;    // bf16 elements = one 128-byte swizzle row
+  static constexpr int A_BYTES = BM * BK * 2;          // 16 KB
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;    // 16 KB (two 64-column atoms)
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int NS = 6;
+  static constexpr int EPI_WARPS = 4;
+  static constexpr int OUT_STAGE = EPI_WARPS * 32 * 128;  // 4 KB per warp: 32 rows x 128 B
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM = 1024 + NS * STAGE + OUT_STAGE + BAR_BYTES;
+  static constexpr int TMEM_COLS = 512;                 // 2 accumulators x 256 columns
+  static constexpr uint32_t IDESC = make_idesc(kFmtBF16, 256, BN, 0, 1);
+  static constexpr uint32_t TX = 2 * STAGE;             // both CTAs
+  static constexpr int THREADS = 64 + EPI_WARPS * 32;
+  static_assert(SMEM <= kMaxSmemPerBlock, "shared memory budget");
+};
+
+struct GemmMaps {
+  CUtensorMap a;  // X or H: [M, K] bf16, box {64, 128}
+  CUtensorMap b;  // W_up / W_down as [E*K, N] bf16, box {64, 64}
+};
+
+// Tile walk: global tile index -> (expert, row block, column block) with
+// grouped rasterisation inside each expert; monotone in the tile index.
+struct TileCursor {
+  int e = -1;
+  int t_begin = 0;   // first global tile of expert e
+  int ntiles = 0;    // tiles of expert e
+  int row_begin = 0;
+  int rows = 0;
+  int mt = 0;        // 256-row blocks of expert e
+
+  __device__ __forceinline__ bool seek(int t, const int32_t* gs, int E, int M, int nt) {
+    while (t >= t_begin + ntiles) {
+      t_begin += ntiles;
+      row_begin += rows;
+      if (++e >= E) return false;
+      int g = __ldg(gs + e);
+      g = g < 0 ? 0 : g;
+      const int rem = M - row_begin;
+      g = g > rem ? (rem > 0 ? rem : 0) : g;
+      rows = g;
+      mt = (g + 255) >> 8;
+      ntiles = mt * nt;
+    }
+    return true;
+  }
+  // (row block, column block) of global tile t (after seek).
+  __device__ __forceinline__ void coords(int t, int nt, int gm_max, int& m, int& n) const {
+    const int l = t - t_begin;
+    const int per_group = gm_max * nt;
+    const int g = l / per_group;
+    const int r = l - g * per_group;
+    int gm = mt - g * gm_max;
+    gm = gm < gm_max ? gm : gm_max;
+    m = g * gm_max + r % gm;
+    n = r / gm;
+  }
+};
+
+template <int EPI>
+__global__ void __launch_bounds__(64 + 128, 1)
+    grouped_gemm_pair_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
+  using C = GemmCfg<EPI>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint8_t* ring = smem;
+  uint8_t* ostage = ring + C::NS * C::STAGE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ostage + C::OUT_STAGE);
+  uint64_t* full = bars;                // [NS] leader
+  uint64_t* empty = bars + C::NS;       // [NS] both (multicast commit)
+  uint64_t* acc_full = bars + 2 * C::NS;  // [2] both (multicast commit)
+  uint64_t* acc_empty = acc_full + 2;     // [2] leader (epilogue warps of both CTAs)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const int pair = (int)(blockIdx.x >> 1);
+  const int npairs = (int)(gridDim.x >> 1);
+  constexpr uint16_t kBoth = 0x3;
+  const int nt = p.N / C::BN;
+  const int nk = p.K / C::BK;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::NS; ++i) {
+      mbar_init(full + i, 1);
+      mbar_init(empty + i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(acc_full + i, 1);
+      mbar_init(acc_empty + i, 2 * C::EPI_WARPS);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&maps.a);
+    tma_prefetch_desc(&maps.b);
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t full_l0 = mapa_shared(smem_u32(full), 0);
+  const uint32_t acc_empty_l = mapa_shared(smem_u32(acc_empty), 0);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      TileCursor cur;
+      int stage = 0;
+      uint32_t phase = 0;
+      const uint64_t pol_a = l2_policy_evict_last();
+      const uint64_t pol_b = l2_policy_evict_last();
+      for (int t = pair;; t += npairs) {
+        if (!cur.seek(t, p.group_sizes, p.E, p.M, nt)) break;
+        int mb, nb;
+        cur.coords(t, nt, p.group_m, mb, nb);
+        const int row0 = cur.row_begin + mb * 256 + (int)rank * C::BM;
+        const int n0 = nb * C::BN + (int)rank * (C::BN / 2);
+        const int brow0 = cur.e * p.k_rows_per_e;
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(empty + stage, phase ^ 1u, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = ring + stage * C::STAGE;
+          const uint32_t bar = full_l0 + stage * 8;
+          if (rank == 0) mbar_arrive_expect_tx(full + stage, C::TX);
+          tma_load_2d_pair(st, &maps.a, bar, kb * C::BK, row0, pol_a);
+          tma_load_2d_pair(st + C::A_BYTES, &maps.b, bar, n0, brow0 + kb * C::BK, pol_b);
+          tma_load_2d_pair(st + C::A_BYTES + 64 * 128, &maps.b, bar, n0 + 64, brow0 + kb * C::BK, pol_b);
+          if (++stage == C::NS) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader, whole warp)
+    if (rank == 0) {
+      TileCursor cur;
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t tcount = 0;
+      for (int t = pair;; t += npairs, ++tcount) {
+        if (!cur.seek(t, p.group_sizes, p.E, p.M, nt)) break;
+        const uint32_t ab = tcount & 1u;
+        const uint32_t use = tcount >> 1;
+        if (!mbar_wait_warp(acc_empty + ab, (use & 1u) ^ 1u, abort_flag, p.status)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + ab * C::BN;
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait_warp(full + stage, phase, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = smem_u32(ring + stage * C::STAGE);
+          const uint64_t a_desc = make_sdesc(st, 16, 1024);
+          const uint64_t b_desc = make_sdesc(st + C::A_BYTES, 64 * 128, 1024);
+#pragma unroll
+          for (int ki = 0; ki < C::BK / 16; ++ki)
+            umma_ss_pair<Kind::F16>(d_tmem, a_desc + (uint64_t)((ki * 32) >> 4),
+                                    b_desc + (uint64_t)((ki * 16 * 128) >> 4), C::IDESC,
+                                    (kb > 0 || ki > 0) ? 1u : 0u);
+          umma_commit_pair(empty + stage, kBoth);
+          if (++stage == C::NS) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(acc_full + ab, kBoth);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const uint32_t q = warp & 3u;
+    const uint32_t lane_base = tmem_base + ((q * 32u) << 16);
+    uint8_t* wst = ostage + (warp - 2u) * 4096u;
+    if constexpr (EPI == 1) {
+      // Rows at or past sum(group_sizes) are zero in ragged_dot.
+      int total = 0;
+      for (int e = 0; e < p.E; ++e) {
+        const int g = __ldg(p.group_sizes + e);
+        total += g < 0 ? 0 : g;
+        if (total >= p.M) {
+          total = p.M;
+          break;
+        }
+      }
+      const size_t n4 = (size_t)(p.M - total) * p.N / 4;
+      float4* base = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (size_t)total * p.N);
+      const int etid = (int)threadIdx.x - 64;
+      for (size_t i = (size_t)blockIdx.x * (C::EPI_WARPS * 32) + etid; i < n4;
+           i += (size_t)gridDim.x * (C::EPI_WARPS * 32))
+        base[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    TileCursor cur;
+    uint32_t tcount = 0;
+    for (int t = pair;; t += npairs, ++tcount) {
+      if (!cur.seek(t, p.group_sizes, p.E, p.M, nt)) break;
+      int mb, nb;
+      cur.coords(t, nt, p.group_m, mb, nb);
+      const int row_end = cur.row_begin + cur.rows;
+      const int wrow0 = cur.row_begin + mb * 256 + (int)rank * C::BM + (int)q * 32;
+      const uint32_t ab = tcount & 1u;
+      const uint32_t use = tcount >> 1;
+      if (!mbar_wait_warp(acc_full + ab, use & 1u, abort_flag, p.status)) break;
+      tc_fence_after();
+      const uint32_t acc = lane_base + ab * C::BN;
+      if constexpr (EPI == 0) {
+        // 64 columns per step: GELU, pack to bf16, stage 32 rows x 128 B,
+        // store rows as full 128-byte lines.
+        uint16_t* H = reinterpret_cast<uint16_t*>(p.out);  // bf16 bits
+#pragma unroll 1
+        for (int c0 = 0; c0 < C::BN; c0 += 64) {
+          uint32_t v[64];
+          tmem_ld32(acc + c0, *reinterpret_cast<uint32_t(*)[32]>(v));
+          tmem_ld32(acc + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+          tmem_ld_wait();
+          uint4* srow = reinterpret_cast<uint4*>(wst) + lane * 8;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            uint4 w;
+            w.x = pack_bf16x2(gelu_tanh_fast(__uint_as_float(v[8 * k + 0])), gelu_tanh_fast(__uint_as_float(v[8 * k + 1])));
+            w.y = pack_bf16x2(gelu_tanh_fast(__uint_as_float(v[8 * k + 2])), gelu_tanh_fast(__uint_as_float(v[8 * k + 3])));
+            w.z = pack_bf16x2(gelu_tanh_fast(__uint_as_float(v[8 * k + 4])), gelu_tanh_fast(__uint_as_float(v[8 * k + 5])));
+            w.w = pack_bf16x2(gelu_tanh_fast(__uint_as_float(v[8 * k + 6])), gelu_tanh_fast(__uint_as_float(v[8 * k + 7])));
+            srow[k ^ (lane & 7)] = w;
+          }
+          __syncwarp();
+          const int gcol = nb * C::BN + c0;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = 4 * i + (int)(lane >> 3);
+            const int k = (int)(lane & 7);
+            const uint4 val = reinterpret_cast<const uint4*>(wst)[r * 8 + (k ^ (r & 7))];
+            const int row = wrow0 + r;
+            if (row < row_end)
+              *reinterpret_cast<uint4*>(H + (size_t)row * p.N + gcol + 8 * k) = val;
+          }
+          __syncwarp();
+        }
+      } else {
+        float* Y = reinterpret_cast<float*>(p.out);
+        float4* wst4 = reinterpret_cast<float4*>(wst);
+#pragma unroll 1
+        for (int c0 = 0; c0 < C::BN; c0 += 32)
+          store_y_block<0>(acc + c0, wst4, Y + (size_t)nb * C::BN, wrow0, row_end, c0, lane, false, p.N);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty_l + ab * 8);
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+}
+
+}  // namespace moe

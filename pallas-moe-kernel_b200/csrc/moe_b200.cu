@@ -11,6 +11,7 @@
 
 #include "../../include/moe_b200.h"
 #include "fused_pair.cuh"
+#include "grouped_gemm.cuh"
 
 namespace moe {
 __device__ int g_status = 0;
@@ -152,6 +153,72 @@ __global__ void __launch_bounds__(256) split_kernel(const float4* __restrict__ x
     hi[i] = h;
     lo[i] = l;
   }
+}
+
+// ------------------------------------------------------------------ large-D dispatch (two grouped GEMMs)
+static bool large_supported(int D, int F, int dtype) {
+  return dtype == MOE_DTYPE_BF16 && D % 256 == 0 && F % 256 == 0 && D >= 256;
+}
+static size_t large_ws_bytes(int64_t M, int F) { return (size_t)M * F * 2; }
+
+template <int EPI>
+static int launch_gemm(const GemmMaps& maps, const GemmParams& prm, DevInfo* di, cudaStream_t st) {
+  using Cfg = GemmCfg<EPI>;
+  auto kern = grouped_gemm_pair_kernel<EPI>;
+  constexpr int slot = 24 + EPI;
+  constexpr int pslot = 6 + EPI;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!di->attr_set[slot]) {
+    MOE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    cfg.gridDim = dim3(2 * (di->sms / 2));
+    int clusters = 0;
+    MOE_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg));
+    if (clusters < 1) return fail(MOE_ERR_CUDA, "no CTA pair fits on this device");
+    di->pairs[pslot] = clusters;
+    di->attr_set[slot] = true;
+  }
+  int pairs = di->pairs[pslot];
+  if (g_tune_ctas > 0 && g_tune_ctas / 2 < pairs) pairs = (int)(g_tune_ctas / 2) > 0 ? (int)(g_tune_ctas / 2) : 1;
+  cfg.gridDim = dim3(2 * pairs);
+  MOE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, maps, prm));
+  return 0;
+}
+
+static int run_large(const void* x, const void* w_up, const void* w_down, const int32_t* gs, float* y, int64_t M,
+                     int D, int F, int E, void* ws, size_t ws_bytes, cudaStream_t st) {
+  int dev;
+  DevInfo* di;
+  if (int r = device_info(&dev, &di)) return r;
+  const size_t need = large_ws_bytes(M, F);
+  if (ws_bytes < need) return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", ws_bytes, need);
+  if (reinterpret_cast<uintptr_t>(ws) & 255u) return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+  int* status = nullptr;
+  MOE_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_status));
+  const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  // up: H = GELU(X @ W_up[e])
+  GemmMaps m1;
+  memset(&m1, 0, sizeof(m1));
+  if (int r = make_map_2d(&m1.a, x, BF16, 2, (uint64_t)M, D, 64, 128)) return r;
+  if (int r = make_map_2d(&m1.b, w_up, BF16, 2, (uint64_t)E * D, F, 64, 64)) return r;
+  GemmParams p1{gs, ws, (int)M, E, F, D, D, 8, status};
+  if (int r = launch_gemm<0>(m1, p1, di, st)) return r;
+  // down: Y = H @ W_down[e]
+  GemmMaps m2;
+  memset(&m2, 0, sizeof(m2));
+  if (int r = make_map_2d(&m2.a, ws, BF16, 2, (uint64_t)M, F, 64, 128)) return r;
+  if (int r = make_map_2d(&m2.b, w_down, BF16, 2, (uint64_t)E * F, D, 64, 64)) return r;
+  GemmParams p2{gs, y, (int)M, E, D, F, F, 8, status};
+  return launch_gemm<1>(m2, p2, di, st);
 }
 
 // ------------------------------------------------------------------ small-D dispatch
@@ -420,6 +487,7 @@ int moe_device_status(int reset) {
 size_t moe_fused_mlp_workspace_size(int64_t M, int32_t D, int32_t F, int32_t E, int32_t dtype) {
   if (M < 0 || D <= 0 || F <= 0 || E <= 0) return 0;
   if (small_supported(D, F, dtype)) return align256(small_plan(M, D, F, E, dtype).ws_bytes);
+  if (large_supported(D, F, dtype)) return align256(large_ws_bytes(M, F));
   return 0;
 }
 
@@ -433,7 +501,7 @@ static int check_args(const void* x, const void* w_up, const void* w_down, const
   if (M == 0) return 0;
   if (!x || !w_up || !w_down || !gs || !y) return fail(MOE_ERR_INVALID_ARG, "null operand pointer");
   if (reinterpret_cast<uintptr_t>(y) & 15u) return fail(MOE_ERR_MISALIGNED, "y must be 16-byte aligned");
-  if (!small_supported(D, F, dtype))
+  if (!small_supported(D, F, dtype) && !large_supported(D, F, dtype))
     return fail(MOE_ERR_UNSUPPORTED_SHAPE, "no kernel for D=%d F=%d dtype=%d", D, F, dtype);
   return 0;
 }
@@ -448,6 +516,7 @@ int moe_prepare_weights(const void* w_up, const void* w_down, const float* w_up_
   if (dtype != MOE_DTYPE_F32 && dtype != MOE_DTYPE_BF16 && dtype != MOE_DTYPE_FP8_E4M3_BLK128)
     return fail(MOE_ERR_UNSUPPORTED_DTYPE, "dtype %d", dtype);
   if (!w_up || !w_down) return fail(MOE_ERR_INVALID_ARG, "null weight pointer");
+  if (large_supported(D, F, dtype) && !small_supported(D, F, dtype)) return 0;  // weights used as given
   if (!small_supported(D, F, dtype))
     return fail(MOE_ERR_UNSUPPORTED_SHAPE, "no kernel for D=%d F=%d dtype=%d", D, F, dtype);
   return prepare_small(w_up, w_down, D, F, E, dtype, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
@@ -462,6 +531,9 @@ int moe_fused_mlp_prepared(const void* x, const void* w_up, const void* w_down, 
   (void)w_down_scale;
   if (int r = check_args(x, w_up, w_down, group_sizes, y, M, D, F, E, dtype)) return r;
   if (M == 0) return 0;
+  if (!small_supported(D, F, dtype))
+    return run_large(x, w_up, w_down, group_sizes, y, M, D, F, E, workspace, workspace_bytes,
+                     static_cast<cudaStream_t>(stream));
   return run_small(x, w_up, w_down, group_sizes, y, M, D, F, E, dtype, workspace, workspace_bytes,
                    static_cast<cudaStream_t>(stream));
 }
@@ -473,6 +545,8 @@ int moe_fused_mlp(const void* x, const void* w_up, const void* w_down, const int
   if (int r = check_args(x, w_up, w_down, group_sizes, y, M, D, F, E, dtype)) return r;
   if (M == 0) return 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (!small_supported(D, F, dtype))
+    return run_large(x, w_up, w_down, group_sizes, y, M, D, F, E, workspace, workspace_bytes, st);
   if (int r = prepare_small(w_up, w_down, D, F, E, dtype, workspace, workspace_bytes, st)) return r;
   return run_small(x, w_up, w_down, group_sizes, y, M, D, F, E, dtype, workspace, workspace_bytes, st);
 }
