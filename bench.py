@@ -340,6 +340,12 @@ def cpu_reference(cfg, budget_s: float, seed: int = 0) -> dict:
     for e in active:
         w_up[e] = rng.standard_normal((cfg.D, cfg.F), dtype=np.float32) / np.float32(math.sqrt(cfg.D))
         w_down[e] = rng.standard_normal((cfg.F, cfg.D), dtype=np.float32) / np.float32(math.sqrt(cfg.F))
+    cores = len(os.sched_getaffinity(0))
+    try:  # torchrun sets OMP_NUM_THREADS=1; the baseline uses every host thread
+        from threadpoolctl import threadpool_limits
+        limiter = threadpool_limits(limits=cores)
+    except Exception:  # pragma: no cover
+        limiter = None
     times = []
     t_end = time.perf_counter() + budget_s
     while True:
@@ -349,7 +355,8 @@ def cpu_reference(cfg, budget_s: float, seed: int = 0) -> dict:
         if time.perf_counter() > t_end or len(times) >= 50:
             break
     med = statistics.median(times)
-    cores = len(os.sched_getaffinity(0))
+    if limiter is not None:
+        limiter.restore_original_limits()
     return {"value": rows / med, "unit": "tokens/s", "cores": cores, "kind": "port",
             "sample": f"{rows} of {cfg.M} routed rows ({len(active)} experts), f32 numpy/BLAS, "
                       f"median of {len(times)} calls",
@@ -411,7 +418,7 @@ def main() -> int:
     try:
         line = run_ours(args, cfg, rank, world, device)
         if line is not None:
-            if not args.no_cpu_baseline:
+            if not args.no_cpu_baseline and world == 1:
                 base = cpu_reference(cfg, budget_s=args.ref_budget)
                 line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
             print(json.dumps(line), flush=True)
