@@ -96,6 +96,32 @@ int moe_fused_mlp_prepared(const void* x, const void* w_up, const void* w_down, 
                            int32_t F, int32_t E, int32_t dtype, void* workspace, size_t workspace_bytes,
                            void* stream);
 
+/*
+ * Allocation-free form of moe_fused_mlp for the f32 (3xTF32) path.  No
+ * counterpart in the reference (its pallas_call always lets XLA allocate).
+ *
+ * For callers that hold only their input and output buffers and cannot
+ * obtain device scratch: for example a host runtime that passes raw device
+ * pointers through an FFI but exposes no device allocator, or a service that
+ * reserves all device memory up front and forbids allocation on its request
+ * path.  The scratch this path needs (the tf32 hi/lo weight planes) lives in
+ * a 16 MiB array inside the library, resident on every GPU that loads the
+ * library until the process exits; the call itself allocates and frees
+ * nothing.
+ *
+ * Limits: D in {64, 128}, F % 64 == 0, E * D * F <= 1,048,576 (else
+ * MOE_ERR_WORKSPACE_TOO_SMALL, and moe_fused_mlp with a workspace is the way).
+ * The first call on a device looks up the scratch array's device address
+ * (cudaGetSymbolAddress), so make that first call before any stream capture.
+ * All calls share the one array: calls that can overlap on the GPU (other
+ * streams, other host threads on the same device) race on it and must be
+ * serialised by the caller.  Nothing in it has to start zeroed -- each call
+ * writes every byte it later reads.  Arguments mean what they mean for
+ * moe_fused_mlp with dtype = MOE_DTYPE_F32.
+ */
+int moe_fused_mlp_noalloc(const float* x, const float* w_up, const float* w_down, const int32_t* group_sizes,
+                          float* y, int64_t M, int32_t D, int32_t F, int32_t E, void* stream);
+
 /* Text of the calling thread's last error ("" when none). */
 const char* moe_last_error(void);
 

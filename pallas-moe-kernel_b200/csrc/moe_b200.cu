@@ -442,6 +442,37 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
   return fail(MOE_ERR_UNSUPPORTED_SHAPE, "D=%d", D);
 }
 
+
+// ------------------------------------------------------------------ allocation-free entry point
+// Scratch of moe_fused_mlp_noalloc: a file-scope device array that every GPU
+// loading this library holds until the process exits.  16 MiB fits the 3xTF32
+// weight planes of E*D*F <= 1,048,576 weight elements per projection (e.g.
+// E=16, D=128, F=512 or E=8, D=128, F=1024).
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// In host code `g_noalloc_scratch` only names a host-side stand-in, so its
+// device address is looked up once per device (with that device current)
+// and cached here.
+static void* g_noalloc_ptr[64] = {};
+static std::mutex g_noalloc_mu;
+
+static int noalloc_scratch(void** out) {
+  int dev = 0;
+  MOE_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(MOE_ERR_CUDA, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || !ptr)
+      return fail(MOE_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed: %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+
 }  // namespace moe
 
 using namespace moe;
@@ -549,6 +580,28 @@ int moe_fused_mlp(const void* x, const void* w_up, const void* w_down, const int
     return run_large(x, w_up, w_down, group_sizes, y, M, D, F, E, workspace, workspace_bytes, st);
   if (int r = prepare_small(w_up, w_down, D, F, E, dtype, workspace, workspace_bytes, st)) return r;
   return run_small(x, w_up, w_down, group_sizes, y, M, D, F, E, dtype, workspace, workspace_bytes, st);
+}
+
+int moe_fused_mlp_noalloc(const float* x, const float* w_up, const float* w_down, const int32_t* group_sizes,
+                          float* y, int64_t M, int32_t D, int32_t F, int32_t E, void* stream) {
+  t_err[0] = 0;
+  if (int r = check_args(x, w_up, w_down, group_sizes, y, M, D, F, E, MOE_DTYPE_F32)) return r;
+  if (M == 0) return 0;
+  if (!(D == 64 || D == 128) || F % 64 != 0)
+    return fail(MOE_ERR_UNSUPPORTED_SHAPE, "moe_fused_mlp_noalloc supports D in {64, 128} and F %% 64 == 0");
+  const size_t need = small_plan(M, D, F, E, MOE_DTYPE_F32).ws_bytes;
+  if (need > kNoAllocScratchBytes)
+    return fail(MOE_ERR_WORKSPACE_TOO_SMALL,
+                "moe_fused_mlp_noalloc: E*D*F = %lld needs %zu scratch bytes, above the %zu-byte static buffer "
+                "(limit E*D*F <= %zu); use moe_fused_mlp with a caller workspace",
+                (long long)E * D * F, need, kNoAllocScratchBytes, kNoAllocScratchBytes / 16);
+  void* scratch = nullptr;
+  if (int r = noalloc_scratch(&scratch)) return r;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // Every scratch byte the fused kernel reads is written by the weight split
+  // earlier in this same call, so nothing needs clearing between calls.
+  if (int r = prepare_small(w_up, w_down, D, F, E, MOE_DTYPE_F32, scratch, kNoAllocScratchBytes, st)) return r;
+  return run_small(x, w_up, w_down, group_sizes, y, M, D, F, E, MOE_DTYPE_F32, scratch, kNoAllocScratchBytes, st);
 }
 
 }  // extern "C"
