@@ -125,19 +125,30 @@ def make_workload(cfg, device, seed: int = 0, experts=None):
     import torch
     from src.routing import config_group_sizes
 
+    from src.routing import quantize_e4m3_blockwise
+
     gs = config_group_sizes(cfg, seed=seed)
     tdt = torch.float32 if cfg.dtype == "f32" else torch.bfloat16
+    wdt = torch.float8_e4m3fn if cfg.dtype == "fp8" else tdt
     g = torch.Generator(device=device)
     g.manual_seed(1234 + seed)
     x = torch.randn((cfg.M, cfg.D), generator=g, device=device, dtype=torch.float32).to(tdt)
     e0, e1 = experts if experts is not None else (0, cfg.E)
-    w_up = torch.empty((e1 - e0, cfg.D, cfg.F), device=device, dtype=tdt)
-    w_down = torch.empty((e1 - e0, cfg.F, cfg.D), device=device, dtype=tdt)
+    w_up = torch.empty((e1 - e0, cfg.D, cfg.F), device=device, dtype=wdt)
+    w_down = torch.empty((e1 - e0, cfg.F, cfg.D), device=device, dtype=wdt)
+    scales = None
+    if cfg.dtype == "fp8":   # e4m3 weights with 128x128 f32 block scales (amax / 448)
+        scales = (torch.empty((e1 - e0, cfg.D // 128, cfg.F // 128), device=device),
+                  torch.empty((e1 - e0, cfg.F // 128, cfg.D // 128), device=device))
     for i, e in enumerate(range(e0, e1)):
         g.manual_seed(99991 * (e + 1))
-        w_up[i] = (torch.randn((cfg.D, cfg.F), generator=g, device=device) / math.sqrt(cfg.D)).to(tdt)
-        w_down[i] = (torch.randn((cfg.F, cfg.D), generator=g, device=device) / math.sqrt(cfg.F)).to(tdt)
-    return x, w_up, w_down, gs
+        wu = torch.randn((cfg.D, cfg.F), generator=g, device=device) / math.sqrt(cfg.D)
+        wd = torch.randn((cfg.F, cfg.D), generator=g, device=device) / math.sqrt(cfg.F)
+        if scales is None:
+            w_up[i], w_down[i] = wu.to(tdt), wd.to(tdt)
+        else:
+            (w_up[i], scales[0][i]), (w_down[i], scales[1][i]) = quantize_e4m3_blockwise(wu), quantize_e4m3_blockwise(wd)
+    return x, w_up, w_down, gs, scales
 
 
 def algorithmic(cfg, gs) -> dict:
@@ -145,7 +156,8 @@ def algorithmic(cfg, gs) -> dict:
     sx = 4 if cfg.dtype == "f32" else 2
     sw = {"f32": 4, "bf16": 2, "fp8": 1}[cfg.dtype]
     active = int(np.count_nonzero(np.asarray(gs) > 0))
-    byts = cfg.M * cfg.D * sx + active * 2 * cfg.D * cfg.F * sw + cfg.M * cfg.D * 4
+    scale_bytes = 2 * (cfg.D // 128) * (cfg.F // 128) * 4 if cfg.dtype == "fp8" else 0
+    byts = cfg.M * cfg.D * sx + active * (2 * cfg.D * cfg.F * sw + scale_bytes) + cfg.M * cfg.D * 4
     return {"flops": 4 * cfg.M * cfg.D * cfg.F, "bytes": byts}
 
 
@@ -175,22 +187,23 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
     if world > 1 and cfg.E % world:
         raise SystemExit(f"E={cfg.E} experts do not shard over {world} ranks")
     el = cfg.E // world
-    x, w_up, w_down, gs_np = make_workload(cfg, device, seed=rank, experts=(rank * el, (rank + 1) * el))
+    x, w_up, w_down, gs_np, scales = make_workload(cfg, device, seed=rank, experts=(rank * el, (rank + 1) * el))
+    sc = {} if scales is None else {"w_up_scale": scales[0], "w_down_scale": scales[1]}
     gs_dev = torch.from_numpy(gs_np).to(device)
     if world > 1:
         from src.ep import ExpertParallelMLP
-        layer = ExpertParallelMLP(w_up, w_down, rank=rank, world=world, max_tokens=cfg.M)
+        layer = ExpertParallelMLP(w_up, w_down, rank=rank, world=world, max_tokens=cfg.M, **sc)
         step_fn = lambda: layer(x, gs_dev)  # noqa: E731
         kern_fn = None
         launches_per_step = layer.launches_per_step
     else:
-        experts = PreparedExperts(w_up, w_down, max_tokens=cfg.M)
+        experts = PreparedExperts(w_up, w_down, max_tokens=cfg.M, **sc)
         y = torch.empty((cfg.M, cfg.D), device=device, dtype=torch.float32)
         ws = torch.empty(max(experts.ws_bytes, 1), device=device, dtype=torch.uint8)
 
         def step_fn():  # the reference entry point: raw weights in, Y out
             return fused_ragged_dot_caller(x, w_up, w_down, gs_dev, BM=16, BF=64, max_group_size=cfg.M,
-                                           out=y, workspace=ws)
+                                           out=y, workspace=ws, **sc)
 
         def kern_fn():  # the dominant kernel alone (weights already prepared)
             return experts(x, gs_dev, out=y)
@@ -249,7 +262,7 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
             out = layer(xd, gsd)
         else:
             out = fused_ragged_dot_caller(xd, w_up, w_down, gsd, BM=16, BF=64, max_group_size=cfg.M,
-                                          out=y, workspace=ws)
+                                          out=y, workspace=ws, **sc)
         yh.copy_(out, non_blocking=True)
 
     for _ in range(max(1, args.warmup)):

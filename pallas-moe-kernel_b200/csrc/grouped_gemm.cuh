@@ -17,9 +17,10 @@
 // stride and rasterised in groups of GM row blocks so that the pairs running
 // at the same time share A and B tiles in L2.
 //
-// Warp roles (192 threads): warp 0 TMA producer (both CTAs), warp 1 TMEM
-// owner + MMA issuer (leader), warps 2..5 epilogue (one TMEM lane quadrant
-// each; both CTAs).
+// Warp roles: warp 0 TMA producer (both CTAs), warp 1 TMEM owner + MMA
+// issuer (leader), warps 2..5 epilogue (one TMEM lane quadrant each; both
+// CTAs), and for e4m3 weights warps 6..9 dequantise each raw B tile
+// (e4m3 x 128x128 block scale -> bf16) into the MMA's operand layout.
 #pragma once
 #include "fused_small.cuh"
 
@@ -35,32 +36,53 @@ struct GemmParams {
   int k_rows_per_e;   // rows of the 2-D B tensor map per expert (= K)
   int group_m;        // tile rasterisation group (row blocks)
   int* status;
+  const float* b_scale;  // FP8 weights: (E, K/128, N/128) f32 block scales, else null
 };
 
-template <int EPI>  // 0: GELU -> bf16 H, 1: f32 Y
+template <int EPI, bool BFP8>  // EPI 0: GELU -> bf16 H, 1: f32 Y; BFP8: e4m3 B dequantised in smem
 struct GemmCfg {
   static constexpr int BM = 128;   // rows per CTA (256 per pair)
   static constexpr int BN = 256;   // output columns per tile (128 per CTA of B)
   static constexpr int BK = 64;    // bf16 elements = one 128-byte swizzle row
   static constexpr int A_BYTES = BM * BK * 2;          // 16 KB
-  static constexpr int B_BYTES = (BN / 2) * BK * 2;    // 16 KB (two 64-column atoms)
-  static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int NS = 6;
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;    // 16 KB (two 64-column atoms, bf16)
+  static constexpr int B8_BYTES = BFP8 ? (BN / 2) * BK : 0;  // 8 KB raw e4m3 tile
+  static constexpr int STAGE = A_BYTES + B_BYTES + B8_BYTES;
+  static constexpr int NS = BFP8 ? 5 : 6;
   static constexpr int EPI_WARPS = 4;
+  static constexpr int CVT_WARPS = BFP8 ? 4 : 0;
   static constexpr int OUT_STAGE = EPI_WARPS * 32 * 128;  // 4 KB per warp: 32 rows x 128 B
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM = 1024 + NS * STAGE + OUT_STAGE + BAR_BYTES;
   static constexpr int TMEM_COLS = 512;                 // 2 accumulators x 256 columns
   static constexpr uint32_t IDESC = make_idesc(kFmtBF16, 256, BN, 0, 1);
-  static constexpr uint32_t TX = 2 * STAGE;             // both CTAs
-  static constexpr int THREADS = 64 + EPI_WARPS * 32;
+  static constexpr uint32_t TX = 2 * (A_BYTES + B_BYTES);  // both CTAs (bf16 B)
+  static constexpr uint32_t TX_RAW = A_BYTES + B8_BYTES;   // this CTA (FP8 B)
+  static constexpr int THREADS = 64 + (EPI_WARPS + CVT_WARPS) * 32;
   static_assert(SMEM <= kMaxSmemPerBlock, "shared memory budget");
 };
 
 struct GemmMaps {
   CUtensorMap a;  // X or H: [M, K] bf16, box {64, 128}
-  CUtensorMap b;  // W_up / W_down as [E*K, N] bf16, box {64, 64}
+  CUtensorMap b;  // W_up / W_down as [E*K, N]: bf16 box {64, 64}, or e4m3 bytes box {128, 64}
 };
+
+// Four e4m3 values (one 32-bit word, lowest byte first) -> f32 x scale ->
+// four bf16 (two bf16x2 words).  e4m3 values are exact in f16, so the only
+// rounding is the final one to bf16 of the dequantised weight.
+__device__ __forceinline__ uint2 e4m3x4_to_bf16x4(uint32_t v, float s) {
+  uint32_t h01, h23;
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, lo;\n\tcvt.rn.f16x2.e4m3x2 %1, hi;\n\t}"
+      : "=r"(h01), "=r"(h23)
+      : "r"(v));
+  float f0, f1, f2, f3;
+  asm("{\n\t.reg .b16 a, b, c, d;\n\tmov.b32 {a, b}, %4;\n\tmov.b32 {c, d}, %5;\n\t"
+      "cvt.f32.f16 %0, a;\n\tcvt.f32.f16 %1, b;\n\tcvt.f32.f16 %2, c;\n\tcvt.f32.f16 %3, d;\n\t}"
+      : "=f"(f0), "=f"(f1), "=f"(f2), "=f"(f3)
+      : "r"(h01), "r"(h23));
+  return make_uint2(pack_bf16x2(f0 * s, f1 * s), pack_bf16x2(f2 * s, f3 * s));
+}
 
 // Tile walk: global tile index -> (expert, row block, column block) with
 // grouped rasterisation inside each expert; monotone in the tile index.
@@ -100,10 +122,10 @@ struct TileCursor {
   }
 };
 
-template <int EPI>
-__global__ void __launch_bounds__(64 + 128, 1)
+template <int EPI, bool BFP8>
+__global__ void __launch_bounds__(64 + 256, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
-  using C = GemmCfg<EPI>;
+  using C = GemmCfg<EPI, BFP8>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -114,7 +136,8 @@ __global__ void __launch_bounds__(64 + 128, 1)
   uint64_t* empty = bars + C::NS;       // [NS] both (multicast commit)
   uint64_t* acc_full = bars + 2 * C::NS;  // [2] both (multicast commit)
   uint64_t* acc_empty = acc_full + 2;     // [2] leader (epilogue warps of both CTAs)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 4);
+  uint64_t* raw = acc_full + 4;           // [NS] local: A + e4m3 B landed (FP8 only)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(raw + C::NS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const uint32_t warp = warp_id();
@@ -128,8 +151,11 @@ __global__ void __launch_bounds__(64 + 128, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::NS; ++i) {
-      mbar_init(full + i, 1);
+      // bf16 B: the leader producer's arrive + both CTAs' TMA bytes.
+      // e4m3 B: one arrival per converter warp of both CTAs.
+      mbar_init(full + i, BFP8 ? 2 * C::CVT_WARPS : 1);
       mbar_init(empty + i, 1);
+      mbar_init(raw + i, 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(acc_full + i, 1);
@@ -175,11 +201,19 @@ __global__ void __launch_bounds__(64 + 128, 1)
             break;
           }
           uint8_t* st = ring + stage * C::STAGE;
-          const uint32_t bar = full_l0 + stage * 8;
-          if (rank == 0) mbar_arrive_expect_tx(full + stage, C::TX);
-          tma_load_2d_pair(st, &maps.a, bar, kb * C::BK, row0, pol_a);
-          tma_load_2d_pair(st + C::A_BYTES, &maps.b, bar, n0, brow0 + kb * C::BK, pol_b);
-          tma_load_2d_pair(st + C::A_BYTES + 64 * 128, &maps.b, bar, n0 + 64, brow0 + kb * C::BK, pol_b);
+          if constexpr (BFP8) {
+            // A and the raw e4m3 B tile land in this CTA; the converter warps
+            // turn B into the bf16 operand and signal the leader.
+            mbar_arrive_expect_tx(raw + stage, C::TX_RAW);
+            tma_load_2d_hint(st, &maps.a, raw + stage, kb * C::BK, row0, pol_a);
+            tma_load_2d_hint(st + C::A_BYTES + C::B_BYTES, &maps.b, raw + stage, n0, brow0 + kb * C::BK, pol_b);
+          } else {
+            const uint32_t bar = full_l0 + stage * 8;
+            if (rank == 0) mbar_arrive_expect_tx(full + stage, C::TX);
+            tma_load_2d_pair(st, &maps.a, bar, kb * C::BK, row0, pol_a);
+            tma_load_2d_pair(st + C::A_BYTES, &maps.b, bar, n0, brow0 + kb * C::BK, pol_b);
+            tma_load_2d_pair(st + C::A_BYTES + 64 * 128, &maps.b, bar, n0 + 64, brow0 + kb * C::BK, pol_b);
+          }
           if (++stage == C::NS) {
             stage = 0;
             phase ^= 1u;
@@ -227,6 +261,52 @@ __global__ void __launch_bounds__(64 + 128, 1)
         umma_commit_pair(acc_full + ab, kBoth);
       }
     }
+  } else if (BFP8 && warp >= 2u + C::EPI_WARPS) {
+    // ------------------------------------------------------------ e4m3 -> bf16 B converters (both CTAs)
+    // Thread t handles k-row r = t/2 of the 64 x 128 raw tile and half h of its
+    // 128 columns (= one 64-column bf16 atom row, 128 bytes).
+    const int ct = (int)threadIdx.x - 64 - C::EPI_WARPS * 32;  // 0..127
+    const int r = ct >> 1, h = ct & 1;
+    const int nkb_scale = p.K / 128, nnb_scale = p.N / 128;
+    TileCursor cur;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = pair; ok; t += npairs) {
+      if (!cur.seek(t, p.group_sizes, p.E, p.M, nt)) break;
+      int mb, nb;
+      cur.coords(t, nt, p.group_m, mb, nb);
+      const int n0 = nb * C::BN + (int)rank * (C::BN / 2);
+      const float* srow = p.b_scale + ((size_t)cur.e * nkb_scale) * nnb_scale + n0 / 128;
+      for (int kb = 0; kb < nk; ++kb) {
+        if (!mbar_wait_warp(raw + stage, phase, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        const float sc = __ldg(srow + (size_t)((kb * C::BK) / 128) * nnb_scale);
+        uint8_t* st = ring + stage * C::STAGE;
+        const uint8_t* src = st + C::A_BYTES + C::B_BYTES + r * 128;  // 128-byte swizzled raw row
+        uint8_t* dst = st + C::A_BYTES + h * (64 * 128) + r * 128;   // atom h, row r (swizzled)
+        const int rsw = r & 7;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int chunk = 4 * h + c;  // 16 raw bytes = columns 16*chunk .. +15
+          const uint4 v = *reinterpret_cast<const uint4*>(src + ((chunk ^ rsw) << 4));
+          const uint2 b0 = e4m3x4_to_bf16x4(v.x, sc), b1 = e4m3x4_to_bf16x4(v.y, sc);
+          const uint2 b2 = e4m3x4_to_bf16x4(v.z, sc), b3 = e4m3x4_to_bf16x4(v.w, sc);
+          const int j0 = 2 * c, j1 = 2 * c + 1;  // output 16-byte chunks in the atom row
+          *reinterpret_cast<uint4*>(dst + ((j0 ^ rsw) << 4)) = make_uint4(b0.x, b0.y, b1.x, b1.y);
+          *reinterpret_cast<uint4*>(dst + ((j1 ^ rsw) << 4)) = make_uint4(b2.x, b2.y, b3.x, b3.y);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(full_l0 + stage * 8);
+        if (++stage == C::NS) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const uint32_t q = warp & 3u;
@@ -245,7 +325,7 @@ __global__ void __launch_bounds__(64 + 128, 1)
       }
       const size_t n4 = (size_t)(p.M - total) * p.N / 4;
       float4* base = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (size_t)total * p.N);
-      const int etid = (int)threadIdx.x - 64;
+      const int etid = (int)threadIdx.x - 64;  // epilogue threads are 64 .. 64 + 127
       for (size_t i = (size_t)blockIdx.x * (C::EPI_WARPS * 32) + etid; i < n4;
            i += (size_t)gridDim.x * (C::EPI_WARPS * 32))
         base[i] = make_float4(0.f, 0.f, 0.f, 0.f);

@@ -157,16 +157,18 @@ __global__ void __launch_bounds__(256) split_kernel(const float4* __restrict__ x
 
 // ------------------------------------------------------------------ large-D dispatch (two grouped GEMMs)
 static bool large_supported(int D, int F, int dtype) {
-  return dtype == MOE_DTYPE_BF16 && D % 256 == 0 && F % 256 == 0 && D >= 256;
+  if (dtype == MOE_DTYPE_BF16) return D % 256 == 0 && F % 256 == 0 && D > 256;
+  if (dtype == MOE_DTYPE_FP8_E4M3_BLK128) return D % 256 == 0 && F % 256 == 0;
+  return false;
 }
 static size_t large_ws_bytes(int64_t M, int F) { return (size_t)M * F * 2; }
 
-template <int EPI>
+template <int EPI, bool BFP8>
 static int launch_gemm(const GemmMaps& maps, const GemmParams& prm, DevInfo* di, cudaStream_t st) {
-  using Cfg = GemmCfg<EPI>;
-  auto kern = grouped_gemm_pair_kernel<EPI>;
-  constexpr int slot = 24 + EPI;
-  constexpr int pslot = 6 + EPI;
+  using Cfg = GemmCfg<EPI, BFP8>;
+  auto kern = grouped_gemm_pair_kernel<EPI, BFP8>;
+  constexpr int slot = 24 + EPI + (BFP8 ? 2 : 0);
+  constexpr int pslot = 4 + EPI + (BFP8 ? 2 : 0);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -194,31 +196,44 @@ static int launch_gemm(const GemmMaps& maps, const GemmParams& prm, DevInfo* di,
   return 0;
 }
 
-static int run_large(const void* x, const void* w_up, const void* w_down, const int32_t* gs, float* y, int64_t M,
-                     int D, int F, int E, void* ws, size_t ws_bytes, cudaStream_t st) {
+static int run_large(const void* x, const void* w_up, const void* w_down, const int32_t* gs,
+                     const float* w_up_scale, const float* w_down_scale, float* y, int64_t M, int D, int F, int E,
+                     int dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
   int dev;
   DevInfo* di;
   if (int r = device_info(&dev, &di)) return r;
   const size_t need = large_ws_bytes(M, F);
   if (ws_bytes < need) return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", ws_bytes, need);
   if (reinterpret_cast<uintptr_t>(ws) & 255u) return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+  const bool fp8 = dtype == MOE_DTYPE_FP8_E4M3_BLK128;
+  if (fp8 && (!w_up_scale || !w_down_scale))
+    return fail(MOE_ERR_INVALID_ARG, "FP8 weights need w_up_scale and w_down_scale");
   int* status = nullptr;
   MOE_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_status));
   const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const auto U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   // up: H = GELU(X @ W_up[e])
   GemmMaps m1;
   memset(&m1, 0, sizeof(m1));
   if (int r = make_map_2d(&m1.a, x, BF16, 2, (uint64_t)M, D, 64, 128)) return r;
-  if (int r = make_map_2d(&m1.b, w_up, BF16, 2, (uint64_t)E * D, F, 64, 64)) return r;
-  GemmParams p1{gs, ws, (int)M, E, F, D, D, 8, status};
-  if (int r = launch_gemm<0>(m1, p1, di, st)) return r;
+  if (fp8) {
+    if (int r = make_map_2d(&m1.b, w_up, U8, 1, (uint64_t)E * D, F, 128, 64)) return r;
+  } else {
+    if (int r = make_map_2d(&m1.b, w_up, BF16, 2, (uint64_t)E * D, F, 64, 64)) return r;
+  }
+  GemmParams p1{gs, ws, (int)M, E, F, D, D, 8, status, w_up_scale};
+  if (int r = fp8 ? launch_gemm<0, true>(m1, p1, di, st) : launch_gemm<0, false>(m1, p1, di, st)) return r;
   // down: Y = H @ W_down[e]
   GemmMaps m2;
   memset(&m2, 0, sizeof(m2));
   if (int r = make_map_2d(&m2.a, ws, BF16, 2, (uint64_t)M, F, 64, 128)) return r;
-  if (int r = make_map_2d(&m2.b, w_down, BF16, 2, (uint64_t)E * F, D, 64, 64)) return r;
-  GemmParams p2{gs, y, (int)M, E, D, F, F, 8, status};
-  return launch_gemm<1>(m2, p2, di, st);
+  if (fp8) {
+    if (int r = make_map_2d(&m2.b, w_down, U8, 1, (uint64_t)E * F, D, 128, 64)) return r;
+  } else {
+    if (int r = make_map_2d(&m2.b, w_down, BF16, 2, (uint64_t)E * F, D, 64, 64)) return r;
+  }
+  GemmParams p2{gs, y, (int)M, E, D, F, F, 8, status, w_down_scale};
+  return fp8 ? launch_gemm<1, true>(m2, p2, di, st) : launch_gemm<1, false>(m2, p2, di, st);
 }
 
 // ------------------------------------------------------------------ small-D dispatch
@@ -558,13 +573,11 @@ int moe_fused_mlp_prepared(const void* x, const void* w_up, const void* w_down, 
                            int32_t F, int32_t E, int32_t dtype, void* workspace, size_t workspace_bytes,
                            void* stream) {
   t_err[0] = 0;
-  (void)w_up_scale;
-  (void)w_down_scale;
   if (int r = check_args(x, w_up, w_down, group_sizes, y, M, D, F, E, dtype)) return r;
   if (M == 0) return 0;
   if (!small_supported(D, F, dtype))
-    return run_large(x, w_up, w_down, group_sizes, y, M, D, F, E, workspace, workspace_bytes,
-                     static_cast<cudaStream_t>(stream));
+    return run_large(x, w_up, w_down, group_sizes, w_up_scale, w_down_scale, y, M, D, F, E, dtype, workspace,
+                     workspace_bytes, static_cast<cudaStream_t>(stream));
   return run_small(x, w_up, w_down, group_sizes, y, M, D, F, E, dtype, workspace, workspace_bytes,
                    static_cast<cudaStream_t>(stream));
 }
@@ -577,7 +590,8 @@ int moe_fused_mlp(const void* x, const void* w_up, const void* w_down, const int
   if (M == 0) return 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (!small_supported(D, F, dtype))
-    return run_large(x, w_up, w_down, group_sizes, y, M, D, F, E, workspace, workspace_bytes, st);
+    return run_large(x, w_up, w_down, group_sizes, w_up_scale, w_down_scale, y, M, D, F, E, dtype, workspace,
+                     workspace_bytes, st);
   if (int r = prepare_small(w_up, w_down, D, F, E, dtype, workspace, workspace_bytes, st)) return r;
   return run_small(x, w_up, w_down, group_sizes, y, M, D, F, E, dtype, workspace, workspace_bytes, st);
 }

@@ -35,7 +35,8 @@ class ExpertParallelMLP:
     def __init__(self, w_up_local: Optional[torch.Tensor], w_down_local: Optional[torch.Tensor], *,
                  rank: int, world: int, num_local_experts: Optional[int] = None, max_tokens: int,
                  group=None, expert_fn: Optional[Callable[[torch.Tensor, torch.Tensor], torch.Tensor]] = None,
-                 out_dtype=torch.float32):
+                 out_dtype=torch.float32, w_up_scale: Optional[torch.Tensor] = None,
+                 w_down_scale: Optional[torch.Tensor] = None):
         self.rank, self.world, self.group = rank, world, group
         if w_up_local is not None:
             self.e_local = w_up_local.shape[0]
@@ -48,7 +49,8 @@ class ExpertParallelMLP:
         if expert_fn is None:
             from .kernel import PreparedExperts
             # A rank can receive up to world * max_tokens rows in the worst routing.
-            self._experts = PreparedExperts(w_up_local, w_down_local, max_tokens=world * max_tokens)
+            self._experts = PreparedExperts(w_up_local, w_down_local, max_tokens=world * max_tokens,
+                                            w_up_scale=w_up_scale, w_down_scale=w_down_scale)
             expert_fn = lambda xr, gs: self._experts(xr, gs)  # noqa: E731
             self.launches_per_step = 2 if w_up_local.shape[1] > 256 else 1
         else:

@@ -177,3 +177,25 @@ def make_inputs_numpy(M: int, D: int, F: int, E: int, seed: int = 0):
     w_up = rng.standard_normal((E, D, F), dtype=np.float32) * np.float32(1.0 / np.sqrt(D))
     w_down = rng.standard_normal((E, F, D), dtype=np.float32) * np.float32(1.0 / np.sqrt(F))
     return x, w_up, w_down
+
+
+def quantize_e4m3_blockwise(w, block: int = 128):
+    """FP8 e4m3 weights with per-(block x block) f32 scales: for each block of
+    the last two dims, scale = amax / 448 (the e4m3 maximum) and
+    q = round_to_e4m3(w / scale).  ``w`` is a torch tensor (..., R, C) with
+    R, C multiples of ``block``; returns (q float8_e4m3fn, scale f32 of shape
+    (..., R/block, C/block)); dequantisation is q * scale per block."""
+    import torch
+    *lead, R, C = w.shape
+    wb = w.float().reshape(*lead, R // block, block, C // block, block)
+    amax = wb.abs().amax(dim=(-3, -1))                         # (..., R/b, C/b)
+    scale = torch.clamp(amax, min=1e-30) / 448.0
+    q = (wb / scale[..., :, None, :, None]).reshape(*lead, R, C).to(torch.float8_e4m3fn)
+    return q, scale.contiguous()
+
+
+def dequantize_e4m3_blockwise(q, scale, block: int = 128):
+    """q * scale per (block x block) tile, as float32."""
+    *lead, R, C = q.shape
+    qb = q.float().reshape(*lead, R // block, block, C // block, block)
+    return (qb * scale[..., :, None, :, None]).reshape(*lead, R, C)

@@ -1,0 +1,100 @@
+"""FP8 e4m3 block-scaled weights (bf16 X, 128x128 f32 block scales) through
+the large-D grouped GEMMs.  Tolerance: L2 relative error <= 2e-2 against the
+float64 oracle on the dequantised weights (BASELINE FP8 contract)."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as orc
+from src import _lib
+from src.kernel import fused_ragged_mlp
+from src.routing import CONFIGS, config_group_sizes, dequantize_e4m3_blockwise, quantize_e4m3_blockwise
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+@pytest.fixture(autouse=True)
+def _status():
+    _lib.device_status(reset=True)
+    yield
+    assert _lib.device_status(reset=True) == 0
+
+
+def _make(M, D, F, E, seed):
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    x = torch.randn((M, D), generator=g, device=dev).to(torch.bfloat16)
+    wu = torch.randn((E, D, F), generator=g, device=dev) / D ** 0.5
+    wd = torch.randn((E, F, D), generator=g, device=dev) / F ** 0.5
+    wu_q, wu_s = quantize_e4m3_blockwise(wu)
+    wd_q, wd_s = quantize_e4m3_blockwise(wd)
+    return x, wu_q, wu_s, wd_q, wd_s
+
+
+def test_quantizer_round_trip():
+    w = torch.randn((2, 256, 384)) * 0.05
+    q, s = quantize_e4m3_blockwise(w)
+    assert q.dtype == torch.float8_e4m3fn and s.shape == (2, 2, 3)
+    back = dequantize_e4m3_blockwise(q, s)
+    assert float((back - w).norm() / w.norm()) < 0.05
+    # the oracle's own e4m3 decoding agrees with torch's
+    codes = q.view(torch.uint8).numpy()
+    deq = orc.dequant_block(orc.e4m3_decode(codes), s.numpy())
+    np.testing.assert_allclose(deq, back.double().numpy(), rtol=1e-6, atol=1e-12)
+
+
+@pytest.mark.parametrize("M,D,F,E,gs", [
+    (1024, 512, 512, 4, [300, 0, 500, 200]),
+    (768, 256, 768, 3, [255, 257, 1]),        # D = 256 also takes this path for FP8
+    (512, 512, 256, 2, [0, 0]),
+])
+def test_fp8_full_oracle(M, D, F, E, gs):
+    x, wu_q, wu_s, wd_q, wd_s = _make(M, D, F, E, seed=M + D)
+    out = torch.full((M, D), float("nan"), device="cuda:0")
+    y = fused_ragged_mlp(x, wu_q, wd_q, torch.tensor(gs, dtype=torch.int32), w_up_scale=wu_s,
+                         w_down_scale=wd_s, out=out)
+    torch.cuda.synchronize()
+    y = y.cpu().numpy()
+    tail = sum(gs)
+    assert np.all(np.isfinite(y)) and np.all(y[tail:] == 0)
+    if tail:
+        ref = orc.ref_ragged_mlp(x.float().cpu().numpy(), dequantize_e4m3_blockwise(wu_q, wu_s).cpu().numpy(),
+                                 dequantize_e4m3_blockwise(wd_q, wd_s).cpu().numpy(), gs)
+        m = orc.correctness_metrics(ref[:tail], y[:tail])
+        assert m["l2_relative_error"] <= TOL, m
+
+
+def test_c5_deepseek_shape_sampled_rows():
+    """Full C5 shape: D=7168, F=2048, E=256, top-8 softmax router over 8192
+    tokens -> M=65536 routed rows; oracle on 6 rows of 16 sampled experts."""
+    cfg = CONFIGS["c5"]
+    gs = config_group_sizes(cfg, seed=0)
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    x = torch.randn((cfg.M, cfg.D), generator=g, device=dev).to(torch.bfloat16)
+    wu_q = torch.empty((cfg.E, cfg.D, cfg.F), dtype=torch.float8_e4m3fn, device=dev)
+    wd_q = torch.empty((cfg.E, cfg.F, cfg.D), dtype=torch.float8_e4m3fn, device=dev)
+    wu_s = torch.empty((cfg.E, cfg.D // 128, cfg.F // 128), device=dev)
+    wd_s = torch.empty((cfg.E, cfg.F // 128, cfg.D // 128), device=dev)
+    for e in range(cfg.E):
+        wu_q[e], wu_s[e] = quantize_e4m3_blockwise(torch.randn((cfg.D, cfg.F), generator=g, device=dev) / cfg.D ** 0.5)
+        wd_q[e], wd_s[e] = quantize_e4m3_blockwise(torch.randn((cfg.F, cfg.D), generator=g, device=dev) / cfg.F ** 0.5)
+    y = fused_ragged_mlp(x, wu_q, wd_q, torch.from_numpy(gs).to(dev), w_up_scale=wu_s, w_down_scale=wd_s)
+    torch.cuda.synchronize()
+    offs = orc.group_sizes_to_offsets(gs)
+    rng = np.random.default_rng(2)
+    experts = rng.choice(np.nonzero(gs)[0], 16, replace=False)
+    refs, gots = [], []
+    for e in experts:
+        a, b = int(offs[e]), int(offs[e + 1])
+        rows = np.unique(np.concatenate([rng.integers(a, b, 4), [a, b - 1]]))
+        wue = dequantize_e4m3_blockwise(wu_q[e], wu_s[e]).cpu().numpy()
+        wde = dequantize_e4m3_blockwise(wd_q[e], wd_s[e]).cpu().numpy()
+        refs.append(orc.ref_ragged_mlp(x[rows].float().cpu().numpy(), wue[None], wde[None], [len(rows)]))
+        gots.append(y[rows].cpu().numpy())
+    m = orc.correctness_metrics(np.concatenate(refs), np.concatenate(gots))
+    assert m["fused_is_finite"] and m["l2_relative_error"] <= TOL, m
