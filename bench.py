@@ -191,11 +191,17 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
     sc = {} if scales is None else {"w_up_scale": scales[0], "w_down_scale": scales[1]}
     gs_dev = torch.from_numpy(gs_np).to(device)
     if world > 1:
-        from src.ep import ExpertParallelMLP
-        layer = ExpertParallelMLP(w_up, w_down, rank=rank, world=world, max_tokens=cfg.M, **sc)
+        from src.ep import ExpertParallelMLP, PeerExpertParallelMLP
+        if args.transport == "peer":
+            layer = PeerExpertParallelMLP(w_up, w_down, rank=rank, world=world, max_tokens=cfg.M,
+                                          waves=args.waves, comm_ctas=args.reserve_sms, **sc)
+            launches_per_step = layer.launches_per_forward
+        else:
+            layer = ExpertParallelMLP(w_up, w_down, rank=rank, world=world, max_tokens=cfg.M,
+                                      waves=args.waves, reserve_sms=args.reserve_sms, **sc)
+            launches_per_step = None
         step_fn = lambda: layer(x, gs_dev)  # noqa: E731
         kern_fn = None
-        launches_per_step = layer.launches_per_step
     else:
         experts = PreparedExperts(w_up, w_down, max_tokens=cfg.M, **sc)
         y = torch.empty((cfg.M, cfg.D), device=device, dtype=torch.float32)
@@ -243,6 +249,8 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
     torch.cuda.synchronize(device)
     clocks.stop()
     total_ms = float(sum(step_ms))
+    if launches_per_step is None:
+        launches_per_step = layer.last_launches
     kern_ms = timed(kern_fn, args.steps) if kern_fn else None
     status = _lib.device_status(reset=True)
     if status:
@@ -273,6 +281,8 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
     vals = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        if hasattr(layer, "close"):
+            layer.close()
     total_ms, e2e_ms = vals.tolist()
     if rank != 0:
         return None
@@ -296,6 +306,8 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
         "data": "synthetic (seeded; BASELINE config shapes, N(0,1)/N(0,1/D)/N(0,1/F) init)",
         "config": {"workload": cfg.name, "M_per_gpu": cfg.M, "D": cfg.D, "F": cfg.F, "E": cfg.E,
                    "routing": cfg.routing, "parallelism": f"ep{world}" if world > 1 else "single",
+                   **({"waves": args.waves, "exchange_sms": args.reserve_sms, "transport": args.transport}
+                      if world > 1 else {}),
                    "l2": "flushed before every step (256 MiB write)"},
         "useful_tflops": alg["flops"] * world / (ms_per_step / 1e3) / 1e12,
         "gpu_launches": launches_per_step * args.steps,
@@ -404,6 +416,14 @@ def main() -> int:
     ap.add_argument("--ref-budget", type=float, default=10.0, help="seconds of CPU baseline timing")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tokens", type=int, default=0, help="override M (routed rows per GPU)")
+    ap.add_argument("--waves", type=int, default=2,
+                    help="N>1: token waves per step (dispatch/combine of one wave overlap the experts of the next)")
+    ap.add_argument("--reserve-sms", type=int, default=0,
+                    help="N>1: SMs left free of the persistent expert kernels for the exchange kernels "
+                         "(0: the engine's default of 16 with --transport peer, none with nccl)")
+    ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
+                    help="N>1: token exchange by the library's kernels over NVLink peer memory (peer) "
+                         "or by NCCL send/recv from Python (nccl)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

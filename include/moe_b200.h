@@ -122,13 +122,70 @@ int moe_fused_mlp_prepared(const void* x, const void* w_up, const void* w_down, 
 int moe_fused_mlp_noalloc(const float* x, const float* w_up, const float* w_down, const int32_t* group_sizes,
                           float* y, int64_t M, int32_t D, int32_t F, int32_t E, void* stream);
 
+/*
+ * Expert-parallel engine: the fused expert MLP with its experts sharded over
+ * `world` GPUs of one NVLink/NVSwitch node, one process (rank) per GPU.  No
+ * counterpart in the reference, which runs on one device; this is the
+ * dispatch -> experts -> combine exchange of an expert-parallel MoE layer
+ * around the same kernels.
+ *
+ * Rank r owns global experts [r * num_local_experts, (r + 1) *
+ * num_local_experts) and holds its own batch of rows sorted by global expert
+ * (group_sizes has world * num_local_experts entries, as for moe_fused_mlp).
+ * Each forward moves every row to its expert's rank, runs the fused MLP there
+ * and brings the f32 result back to the row's original position, so that on
+ * every rank Y equals moe_fused_mlp over all experts.  Transfers are our own
+ * kernels over peer memory (CUDA IPC mappings of one buffer per rank): rows
+ * are stored straight into the owner's landing buffer and results loaded
+ * straight from the owner's outbox, in `waves` slices per step so that the
+ * exchange of one slice overlaps the experts of the next.  Group sizes are
+ * exchanged on the device: a forward never synchronises the host.
+ *
+ * Set-up, on every rank with its own GPU current:
+ *   moe_ep_create   allocates the engine (device memory proportional to
+ *                   world * max_tokens rows; 0 comm_ctas = 16 SMs for the
+ *                   exchange kernels, the experts run on the others);
+ *   moe_ep_export   writes this rank's MOE_EP_HANDLE_BYTES-byte handle;
+ *                   the caller gathers all ranks' handles in rank order by
+ *                   any means (e.g. torch.distributed.all_gather) and then
+ *                   calls
+ *   moe_ep_connect  maps every peer's buffer (ranks must be distinct GPUs);
+ *   moe_ep_set_weights  this rank's expert weights (E_local, D, F) /
+ *                   (E_local, F, D) (+ FP8 block scales), kept by pointer
+ *                   (prepared once for the f32 path).
+ * Step:  moe_ep_forward on every rank, the same number of times on all
+ *        ranks (it is a collective).  M <= max_tokens; x (M, D), y (M, D) f32.
+ * Exit:  moe_ep_destroy on every rank, after a host barrier that follows
+ *        every rank's last forward having completed.
+ *
+ * Failure: every wait for a peer is bounded (5 s); a wait that runs out sets
+ * status bit 4 (moe_device_status) and stops the engine's data movement for
+ * good (later forwards return zeros), so a dead peer never hangs a GPU.
+ * Group sizes beyond M or beyond a landing region are cut (status bit 8).
+ */
+typedef struct moe_ep_s* moe_ep_t;
+#define MOE_EP_HANDLE_BYTES 256
+
+int moe_ep_create(int32_t rank, int32_t world, int32_t num_local_experts, int64_t max_tokens, int32_t D, int32_t F,
+                  int32_t dtype, int32_t waves, int32_t comm_ctas, moe_ep_t* out);
+int moe_ep_export(moe_ep_t ep, void* handle);
+int moe_ep_connect(moe_ep_t ep, const void* handles);
+int moe_ep_set_weights(moe_ep_t ep, const void* w_up_local, const void* w_down_local, const float* w_up_scale,
+                       const float* w_down_scale, void* stream);
+int moe_ep_forward(moe_ep_t ep, const void* x, const int32_t* group_sizes, float* y, int64_t M, void* stream);
+/* Kernels one moe_ep_forward launches (exchange + expert kernels). */
+int moe_ep_launches_per_forward(moe_ep_t ep);
+int moe_ep_destroy(moe_ep_t ep);
+
 /* Text of the calling thread's last error ("" when none). */
 const char* moe_last_error(void);
 
 /*
  * Reads the device status word of the current device (bits: 1 = a pipeline
- * wait timed out, 2 = a negative group size was clamped).  Synchronises the
- * device.  When `reset` is non-zero the word is cleared afterwards.
+ * wait timed out, 2 = a negative group size was clamped, 4 = an
+ * expert-parallel wait for a peer timed out, 8 = group sizes were cut to fit
+ * M or a landing region).  Synchronises the device.  When `reset` is
+ * non-zero the word is cleared afterwards.
  * Returns the bits (>= 0) or MOE_ERR_CUDA.
  */
 int moe_device_status(int reset);

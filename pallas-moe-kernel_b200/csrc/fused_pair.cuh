@@ -345,7 +345,7 @@ __global__ void __launch_bounds__(64 + 256, 1)
       for (int e = 0; e < p.E; ++e)
         if (__ldg(p.group_sizes + e) < 0) atomicOr(p.status, kStatusBadGroupSize);
     }
-    if (!p.atomic_out) {
+    if (!p.atomic_out && !p.skip_tail) {
       int total = 0;
       for (int e = 0; e < p.E; ++e) {
         int g = __ldg(p.group_sizes + e);

@@ -55,6 +55,7 @@ struct FusedParams {
   int atomic_out;             // 1: Y was zeroed, units reduce-add into it
   int* status;                // device status word (kStatus* bits)
   unsigned long long* trace;  // MOE_TRACE builds: per-CTA event timeline (else unused)
+  int skip_tail;              // 1: leave rows at or past sum(group_sizes) unwritten
 };
 
 // Optional timeline of pipeline events (clock64 per event) for CTA-level
@@ -488,7 +489,7 @@ __global__ void __launch_bounds__(64 + 256, 1)
     }
     // Rows at or past sum(group_sizes) are zero in ragged_dot; write them
     // here unless Y was zeroed up front (reduce-add mode).
-    if (!p.atomic_out) {
+    if (!p.atomic_out && !p.skip_tail) {
       int total = 0;
       for (int e = 0; e < p.E; ++e) {
         int g = __ldg(p.group_sizes + e);

@@ -37,6 +37,7 @@ struct GemmParams {
   int group_m;        // tile rasterisation group (row blocks)
   int* status;
   const float* b_scale;  // FP8 weights: (E, K/128, N/128) f32 block scales, else null
+  int skip_tail;         // 1: leave rows at or past sum(group_sizes) unwritten (Y only)
 };
 
 template <int EPI, bool BFP8>  // EPI 0: GELU -> bf16 H, 1: f32 Y; BFP8: e4m3 B dequantised in smem
@@ -312,7 +313,7 @@ __global__ void __launch_bounds__(64 + 256, 1)
     const uint32_t q = warp & 3u;
     const uint32_t lane_base = tmem_base + ((q * 32u) << 16);
     uint8_t* wst = ostage + (warp - 2u) * 4096u;
-    if constexpr (EPI == 1) {
+    if (EPI == 1 && !p.skip_tail) {
       // Rows at or past sum(group_sizes) are zero in ragged_dot.
       int total = 0;
       for (int e = 0; e < p.E; ++e) {

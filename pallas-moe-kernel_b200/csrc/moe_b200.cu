@@ -10,6 +10,7 @@
 #include <mutex>
 
 #include "../../include/moe_b200.h"
+#include "ep_exchange.cuh"
 #include "fused_pair.cuh"
 #include "grouped_gemm.cuh"
 
@@ -164,7 +165,7 @@ static bool large_supported(int D, int F, int dtype) {
 static size_t large_ws_bytes(int64_t M, int F) { return (size_t)M * F * 2; }
 
 template <int EPI, bool BFP8>
-static int launch_gemm(const GemmMaps& maps, const GemmParams& prm, DevInfo* di, cudaStream_t st) {
+static int launch_gemm(const GemmMaps& maps, const GemmParams& prm, DevInfo* di, cudaStream_t st, int ctas_req) {
   using Cfg = GemmCfg<EPI, BFP8>;
   auto kern = grouped_gemm_pair_kernel<EPI, BFP8>;
   constexpr int slot = 24 + EPI + (BFP8 ? 2 : 0);
@@ -190,18 +191,28 @@ static int launch_gemm(const GemmMaps& maps, const GemmParams& prm, DevInfo* di,
     di->attr_set[slot] = true;
   }
   int pairs = di->pairs[pslot];
-  if (g_tune_ctas > 0 && g_tune_ctas / 2 < pairs) pairs = (int)(g_tune_ctas / 2) > 0 ? (int)(g_tune_ctas / 2) : 1;
+  if (ctas_req > 0 && ctas_req / 2 < pairs) pairs = ctas_req / 2 > 0 ? ctas_req / 2 : 1;
   cfg.gridDim = dim3(2 * pairs);
   MOE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, maps, prm));
   return 0;
 }
 
+// Launch options shared by the single-GPU entry points (defaults) and the
+// expert-parallel engine: `ctas` > 0 caps the persistent grid (leaving SMs to
+// concurrent exchange kernels), `skip_tail` leaves Y rows past
+// sum(group_sizes) unwritten (a landing region whose tail nobody reads).
+struct RunOpts {
+  int ctas = 0;
+  bool skip_tail = false;
+};
+
 static int run_large(const void* x, const void* w_up, const void* w_down, const int32_t* gs,
                      const float* w_up_scale, const float* w_down_scale, float* y, int64_t M, int D, int F, int E,
-                     int dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
+                     int dtype, void* ws, size_t ws_bytes, cudaStream_t st, RunOpts opt = RunOpts()) {
   int dev;
   DevInfo* di;
   if (int r = device_info(&dev, &di)) return r;
+  const int ctas = opt.ctas > 0 ? opt.ctas : (int)g_tune_ctas;
   const size_t need = large_ws_bytes(M, F);
   if (ws_bytes < need) return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", ws_bytes, need);
   if (reinterpret_cast<uintptr_t>(ws) & 255u) return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
@@ -221,8 +232,9 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
   } else {
     if (int r = make_map_2d(&m1.b, w_up, BF16, 2, (uint64_t)E * D, F, 64, 64)) return r;
   }
-  GemmParams p1{gs, ws, (int)M, E, F, D, D, 8, status, w_up_scale};
-  if (int r = fp8 ? launch_gemm<0, true>(m1, p1, di, st) : launch_gemm<0, false>(m1, p1, di, st)) return r;
+  GemmParams p1{gs, ws, (int)M, E, F, D, D, 8, status, w_up_scale, 0};
+  if (int r = fp8 ? launch_gemm<0, true>(m1, p1, di, st, ctas) : launch_gemm<0, false>(m1, p1, di, st, ctas))
+    return r;
   // down: Y = H @ W_down[e]
   GemmMaps m2;
   memset(&m2, 0, sizeof(m2));
@@ -232,8 +244,8 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
   } else {
     if (int r = make_map_2d(&m2.b, w_down, BF16, 2, (uint64_t)E * F, D, 64, 64)) return r;
   }
-  GemmParams p2{gs, y, (int)M, E, D, F, F, 8, status, w_down_scale};
-  return fp8 ? launch_gemm<1, true>(m2, p2, di, st) : launch_gemm<1, false>(m2, p2, di, st);
+  GemmParams p2{gs, y, (int)M, E, D, F, F, 8, status, w_down_scale, opt.skip_tail ? 1 : 0};
+  return fp8 ? launch_gemm<1, true>(m2, p2, di, st, ctas) : launch_gemm<1, false>(m2, p2, di, st, ctas);
 }
 
 // ------------------------------------------------------------------ small-D dispatch
@@ -354,7 +366,8 @@ static int launch_pair(const FusedMaps& maps, const FusedParams& prm, int pairs_
 }
 
 static int run_small(const void* x, const void* w_up, const void* w_down, const int32_t* gs, float* y, int64_t M,
-                     int D, int F, int E, int dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
+                     int D, int F, int E, int dtype, void* ws, size_t ws_bytes, cudaStream_t st,
+                     RunOpts opt = RunOpts()) {
   int dev;
   DevInfo* di;
   if (int r = device_info(&dev, &di)) return r;
@@ -380,7 +393,8 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
     const int64_t blocks_est = (M + rows_per_unit - 1) / rows_per_unit;
     while (blocks_est * splits < workers && nch_total % (splits * 2) == 0 && splits * 2 <= nch_total) splits *= 2;
   }
-  int ctas = g_tune_ctas > 0 ? (int)g_tune_ctas : di->sms;
+  const int ctas_req = opt.ctas > 0 ? opt.ctas : (int)g_tune_ctas;
+  int ctas = ctas_req > 0 && ctas_req < di->sms ? ctas_req : di->sms;
 
   int* status = nullptr;
   MOE_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_status));
@@ -396,6 +410,7 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
   prm.atomic_out = splits > 1 ? 1 : 0;
   prm.status = status;
   prm.trace = reinterpret_cast<unsigned long long*>(g_tune_trace);
+  prm.skip_tail = opt.skip_tail ? 1 : 0;
 
   FusedMaps maps;
   memset(&maps, 0, sizeof(maps));
@@ -407,7 +422,7 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
     if (int r = make_map_2d(&maps.wu[0], w_up, BF16, 2, (uint64_t)E * D, F, 64, 64)) return r;
     if (int r = make_map_2d(&maps.wd[0], w_down, BF16, 2, (uint64_t)E * F, D, 64, 64)) return r;
     if (pair) {
-      const int pairs_req = g_tune_ctas > 0 ? (int)(g_tune_ctas / 2) : 0;
+      const int pairs_req = ctas_req > 0 ? ctas_req / 2 : 0;
       if (D == 128) return launch_pair<kModeBF16, 128, 128>(maps, prm, pairs_req, di, st);
       return launch_pair<kModeBF16, 256, 128>(maps, prm, pairs_req, di, st);
     }
@@ -432,7 +447,7 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
   if (int r = make_map_2d(&maps.wd[1], wd_lo, F32, 4, (uint64_t)E * D, F, 32, wd_box_rows)) return r;
   if (pair) {
     if (int r = make_map_2d(&maps.x[0], x, F32, 4, (uint64_t)M, D, 32, 128)) return r;
-    const int pairs_req = g_tune_ctas > 0 ? (int)(g_tune_ctas / 2) : 0;
+    const int pairs_req = ctas_req > 0 ? ctas_req / 2 : 0;
     if (D == 64) return launch_pair<kModeTF32x3, 64, 64>(maps, prm, pairs_req, di, st);
     return launch_pair<kModeTF32x3, 128, 64>(maps, prm, pairs_req, di, st);
   }
@@ -485,6 +500,91 @@ static int noalloc_scratch(void** out) {
     g_noalloc_ptr[dev] = ptr;
   }
   *out = g_noalloc_ptr[dev];
+  return 0;
+}
+
+
+// ------------------------------------------------------------------ expert-parallel engine
+// What one rank publishes to the others (fits MOE_EP_HANDLE_BYTES): the IPC
+// handle of its symmetric buffer plus everything the peers must agree on.
+struct EpHandleBlob {
+  char magic[8];
+  int32_t rank, world, el, D, F, dtype, waves, pad;
+  int64_t region_cap;
+  uint64_t buffer_bytes;
+  unsigned char uuid[16];
+  cudaIpcMemHandle_t ipc;
+};
+static_assert(sizeof(EpHandleBlob) <= MOE_EP_HANDLE_BYTES, "handle blob");
+static const char kEpMagic[8] = {'m', 'o', 'e', 'e', 'p', '0', '0', '1'};
+
+}  // namespace moe
+
+struct moe_ep_s {
+  int dev = -1;
+  int rank = 0, world = 1, el = 1, E = 1, D = 0, F = 0, dtype = 0, waves = 1;
+  int comm_ctas = 16, mlp_ctas = 0;
+  int64_t max_tokens = 0;
+  int region_cap = 0;
+  size_t off_gs = 0, off_x = 0, off_y = 0, region_x_bytes = 0, region_y_bytes = 0, buf_bytes = 0;
+  uint8_t* buf = nullptr;
+  uint8_t* peer[moe::kEpMaxWorld] = {};
+  bool opened[moe::kEpMaxWorld] = {};
+  bool connected = false;
+  uint8_t* tables = nullptr;
+  moe::EpSlice* slices = nullptr;
+  int* wave_rows = nullptr;
+  int* local_gs = nullptr;
+  int* routed = nullptr;
+  unsigned* push_ctr = nullptr;
+  int* abort_word = nullptr;
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  const void* w_up = nullptr;
+  const void* w_down = nullptr;
+  const float* w_up_scale = nullptr;
+  const float* w_down_scale = nullptr;
+  bool weights_set = false;
+  cudaStream_t comm = nullptr;
+  cudaEvent_t ev_start = nullptr, ev_end = nullptr;
+  cudaEvent_t ev_push[moe::kEpMaxWaves] = {}, ev_mlp[moe::kEpMaxWaves] = {};
+  uint32_t epoch = 0;
+  int* status = nullptr;
+};
+
+namespace moe {
+
+static void ep_release(moe_ep_s* ep) {
+  if (!ep) return;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (ep->dev >= 0) cudaSetDevice(ep->dev);
+  if (ep->comm) cudaStreamSynchronize(ep->comm);
+  for (int s = 0; s < kEpMaxWorld; ++s)
+    if (ep->opened[s]) cudaIpcCloseMemHandle(ep->peer[s]);
+  for (int v = 0; v < kEpMaxWaves; ++v) {
+    if (ep->ev_push[v]) cudaEventDestroy(ep->ev_push[v]);
+    if (ep->ev_mlp[v]) cudaEventDestroy(ep->ev_mlp[v]);
+  }
+  if (ep->ev_start) cudaEventDestroy(ep->ev_start);
+  if (ep->ev_end) cudaEventDestroy(ep->ev_end);
+  if (ep->comm) cudaStreamDestroy(ep->comm);
+  if (ep->ws) cudaFree(ep->ws);
+  if (ep->tables) cudaFree(ep->tables);
+  if (ep->buf) cudaFree(ep->buf);
+  if (prev >= 0) cudaSetDevice(prev);
+  delete ep;
+}
+
+static int ep_mlp_launches(const moe_ep_s* ep) {
+  if (!small_supported(ep->D, ep->F, ep->dtype)) return 2;        // up + down grouped GEMMs
+  return (ep->dtype == MOE_DTYPE_F32 && ep->D == 256) ? 2 : 1;   // (+ X split) fused kernel
+}
+
+static int ep_check_device(const moe_ep_s* ep) {
+  int dev = -1;
+  MOE_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev != ep->dev) return fail(MOE_ERR_INVALID_ARG, "engine lives on device %d, current device is %d", ep->dev, dev);
   return 0;
 }
 
@@ -616,6 +716,292 @@ int moe_fused_mlp_noalloc(const float* x, const float* w_up, const float* w_down
   // earlier in this same call, so nothing needs clearing between calls.
   if (int r = prepare_small(w_up, w_down, D, F, E, MOE_DTYPE_F32, scratch, kNoAllocScratchBytes, st)) return r;
   return run_small(x, w_up, w_down, group_sizes, y, M, D, F, E, MOE_DTYPE_F32, scratch, kNoAllocScratchBytes, st);
+}
+
+// ------------------------------------------------------------------ expert-parallel engine
+int moe_ep_create(int32_t rank, int32_t world, int32_t num_local_experts, int64_t max_tokens, int32_t D, int32_t F,
+                  int32_t dtype, int32_t waves, int32_t comm_ctas, moe_ep_t* out) {
+  t_err[0] = 0;
+  if (!out) return fail(MOE_ERR_INVALID_ARG, "null output handle");
+  *out = nullptr;
+  if (world < 1 || world > kEpMaxWorld || rank < 0 || rank >= world)
+    return fail(MOE_ERR_INVALID_ARG, "rank %d / world %d (world must be 1..%d)", rank, world, kEpMaxWorld);
+  if (num_local_experts < 1 || (int64_t)num_local_experts * world > kEpMaxExperts)
+    return fail(MOE_ERR_INVALID_ARG, "%d experts per rank x %d ranks (at most %d experts)", num_local_experts,
+                world, kEpMaxExperts);
+  if (waves < 1 || waves > kEpMaxWaves) return fail(MOE_ERR_INVALID_ARG, "waves %d (1..%d)", waves, kEpMaxWaves);
+  if (max_tokens < 1) return fail(MOE_ERR_INVALID_ARG, "max_tokens %lld", (long long)max_tokens);
+  if (comm_ctas < 0 || comm_ctas > 64) return fail(MOE_ERR_INVALID_ARG, "comm_ctas %d (0..64)", comm_ctas);
+  if (dtype != MOE_DTYPE_F32 && dtype != MOE_DTYPE_BF16 && dtype != MOE_DTYPE_FP8_E4M3_BLK128)
+    return fail(MOE_ERR_UNSUPPORTED_DTYPE, "dtype %d", dtype);
+  if (D <= 0 || F <= 0 || (!small_supported(D, F, dtype) && !large_supported(D, F, dtype)))
+    return fail(MOE_ERR_UNSUPPORTED_SHAPE, "no kernel for D=%d F=%d dtype=%d", D, F, dtype);
+  int dev;
+  DevInfo* di;
+  if (int r = device_info(&dev, &di)) return r;
+
+  // Rows per landing region: wave v of a group of c rows holds at most
+  // ceil(c / waves) <= c / waves + 1 rows, over world sources and el experts.
+  const int64_t cap64 = ((int64_t)world * max_tokens + waves - 1) / waves + (int64_t)world * num_local_experts;
+  const int64_t cap = (cap64 + 255) / 256 * 256;
+  if (cap > (int64_t)1 << 30 || max_tokens > (int64_t)1 << 30)
+    return fail(MOE_ERR_UNSUPPORTED_SHAPE, "landing region of %lld rows", (long long)cap);
+
+  moe_ep_s* ep = new moe_ep_s();
+  ep->dev = dev;
+  ep->rank = rank;
+  ep->world = world;
+  ep->el = num_local_experts;
+  ep->E = world * num_local_experts;
+  ep->D = D;
+  ep->F = F;
+  ep->dtype = dtype;
+  ep->waves = waves;
+  ep->comm_ctas = comm_ctas > 0 ? comm_ctas : 16;
+  ep->max_tokens = max_tokens;
+  ep->region_cap = (int)cap;
+  const int sx = dtype == MOE_DTYPE_F32 ? 4 : 2;
+  ep->off_gs = 4096;
+  ep->off_x = align256(ep->off_gs + (size_t)2 * world * ep->E * sizeof(int32_t));
+  ep->region_x_bytes = align256((size_t)cap * D * sx);
+  ep->off_y = ep->off_x + (size_t)waves * ep->region_x_bytes;
+  ep->region_y_bytes = align256((size_t)cap * D * sizeof(float));
+  ep->buf_bytes = ep->off_y + (size_t)waves * ep->region_y_bytes;
+  // Exchange kernels take the SMs the expert kernels leave free (pairs: even).
+  ep->mlp_ctas = world > 1 ? ((di->sms - ep->comm_ctas) & ~1) : 0;
+  if (world > 1 && ep->mlp_ctas < 2) {
+    ep_release(ep);
+    return fail(MOE_ERR_INVALID_ARG, "comm_ctas %d leaves no SMs for the experts", comm_ctas);
+  }
+
+  auto cuda_fail = [&](cudaError_t e, const char* what) {
+    ep_release(ep);
+    return fail(MOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  };
+  cudaError_t e;
+  if ((e = cudaMalloc(&ep->buf, ep->buf_bytes)) != cudaSuccess) return cuda_fail(e, "cudaMalloc(symmetric buffer)");
+  if ((e = cudaMemset(ep->buf, 0, ep->off_x)) != cudaSuccess) return cuda_fail(e, "cudaMemset(flags)");
+  const size_t t_slices = align256((size_t)waves * ep->E * sizeof(EpSlice));
+  const size_t t_rows = align256((size_t)waves * (ep->E + 1) * sizeof(int));
+  const size_t t_gs = align256((size_t)waves * ep->el * sizeof(int));
+  const size_t t_misc = 256 + (size_t)kEpMaxWaves * sizeof(unsigned) + 256;
+  const size_t t_all = t_slices + t_rows + t_gs + t_misc;
+  if ((e = cudaMalloc(&ep->tables, t_all)) != cudaSuccess) return cuda_fail(e, "cudaMalloc(tables)");
+  if ((e = cudaMemset(ep->tables, 0, t_all)) != cudaSuccess) return cuda_fail(e, "cudaMemset(tables)");
+  ep->slices = reinterpret_cast<EpSlice*>(ep->tables);
+  ep->wave_rows = reinterpret_cast<int*>(ep->tables + t_slices);
+  ep->local_gs = reinterpret_cast<int*>(ep->tables + t_slices + t_rows);
+  ep->routed = reinterpret_cast<int*>(ep->tables + t_slices + t_rows + t_gs);
+  ep->push_ctr = reinterpret_cast<unsigned*>(ep->tables + t_slices + t_rows + t_gs + 256);
+  ep->abort_word = reinterpret_cast<int*>(ep->tables + t_slices + t_rows + t_gs + 256 + 256);
+  ep->ws_bytes = small_supported(D, F, dtype) ? align256(small_plan(cap, D, F, ep->el, dtype).ws_bytes)
+                                              : align256(large_ws_bytes(cap, F));
+  if (ep->ws_bytes && (e = cudaMalloc(&ep->ws, ep->ws_bytes)) != cudaSuccess) return cuda_fail(e, "cudaMalloc(workspace)");
+  if ((e = cudaStreamCreateWithFlags(&ep->comm, cudaStreamNonBlocking)) != cudaSuccess)
+    return cuda_fail(e, "cudaStreamCreate");
+  if ((e = cudaEventCreateWithFlags(&ep->ev_start, cudaEventDisableTiming)) != cudaSuccess ||
+      (e = cudaEventCreateWithFlags(&ep->ev_end, cudaEventDisableTiming)) != cudaSuccess)
+    return cuda_fail(e, "cudaEventCreate");
+  for (int v = 0; v < waves; ++v)
+    if ((e = cudaEventCreateWithFlags(&ep->ev_push[v], cudaEventDisableTiming)) != cudaSuccess ||
+        (e = cudaEventCreateWithFlags(&ep->ev_mlp[v], cudaEventDisableTiming)) != cudaSuccess)
+      return cuda_fail(e, "cudaEventCreate");
+  if ((e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ep->status), g_status)) != cudaSuccess)
+    return cuda_fail(e, "cudaGetSymbolAddress(status)");
+  // The largest engine's need, so that engines of different sizes coexist.
+  const size_t smem = ep_counts_smem(kEpMaxWorld, kEpMaxExperts, kEpMaxWaves);
+  if ((e = cudaFuncSetAttribute(ep_counts_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) !=
+      cudaSuccess)
+    return cuda_fail(e, "cudaFuncSetAttribute(ep_counts_kernel)");
+  if ((e = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  ep->peer[rank] = ep->buf;
+  *out = ep;
+  return 0;
+}
+
+int moe_ep_export(moe_ep_t ep, void* handle) {
+  t_err[0] = 0;
+  if (!ep || !handle) return fail(MOE_ERR_INVALID_ARG, "null argument");
+  if (int r = ep_check_device(ep)) return r;
+  EpHandleBlob b;
+  memset(&b, 0, sizeof(b));
+  memcpy(b.magic, kEpMagic, sizeof(b.magic));
+  b.rank = ep->rank;
+  b.world = ep->world;
+  b.el = ep->el;
+  b.D = ep->D;
+  b.F = ep->F;
+  b.dtype = ep->dtype;
+  b.waves = ep->waves;
+  b.region_cap = ep->region_cap;
+  b.buffer_bytes = ep->buf_bytes;
+  cudaDeviceProp prop;
+  MOE_CUDA_TRY(cudaGetDeviceProperties(&prop, ep->dev));
+  memcpy(b.uuid, &prop.uuid, sizeof(b.uuid));
+  MOE_CUDA_TRY(cudaIpcGetMemHandle(&b.ipc, ep->buf));
+  memset(handle, 0, MOE_EP_HANDLE_BYTES);
+  memcpy(handle, &b, sizeof(b));
+  return 0;
+}
+
+int moe_ep_connect(moe_ep_t ep, const void* handles) {
+  t_err[0] = 0;
+  if (!ep || !handles) return fail(MOE_ERR_INVALID_ARG, "null argument");
+  if (ep->connected) return fail(MOE_ERR_INVALID_ARG, "engine already connected");
+  if (int r = ep_check_device(ep)) return r;
+  const unsigned char* hb = static_cast<const unsigned char*>(handles);
+  EpHandleBlob mine;
+  memcpy(&mine, hb + (size_t)ep->rank * MOE_EP_HANDLE_BYTES, sizeof(mine));
+  cudaDeviceProp prop;
+  MOE_CUDA_TRY(cudaGetDeviceProperties(&prop, ep->dev));
+  for (int s = 0; s < ep->world; ++s) {
+    EpHandleBlob b;
+    memcpy(&b, hb + (size_t)s * MOE_EP_HANDLE_BYTES, sizeof(b));
+    if (memcmp(b.magic, kEpMagic, sizeof(b.magic)) != 0)
+      return fail(MOE_ERR_INVALID_ARG, "handle %d is not an expert-parallel handle", s);
+    if (b.rank != s || b.world != ep->world || b.el != ep->el || b.D != ep->D || b.F != ep->F ||
+        b.dtype != ep->dtype || b.waves != ep->waves || b.region_cap != ep->region_cap ||
+        b.buffer_bytes != ep->buf_bytes)
+      return fail(MOE_ERR_INVALID_ARG,
+                  "handle %d (rank %d of %d, %d experts, D=%d F=%d dtype=%d waves=%d) does not match this engine",
+                  s, b.rank, b.world, b.el, b.D, b.F, b.dtype, b.waves);
+    if (s == ep->rank) continue;
+    // Exchange kernels of two ranks on one GPU would wait on one another
+    // with no guarantee of running at the same time: refuse.
+    if (memcmp(b.uuid, &prop.uuid, sizeof(b.uuid)) == 0)
+      return fail(MOE_ERR_INVALID_ARG, "ranks %d and %d share one GPU; every rank needs its own", s, ep->rank);
+  }
+  for (int s = 0; s < ep->world; ++s) {
+    if (s == ep->rank) continue;
+    EpHandleBlob b;
+    memcpy(&b, hb + (size_t)s * MOE_EP_HANDLE_BYTES, sizeof(b));
+    void* p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, b.ipc, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int q = 0; q < s; ++q)
+        if (ep->opened[q]) {
+          cudaIpcCloseMemHandle(ep->peer[q]);
+          ep->opened[q] = false;
+          ep->peer[q] = nullptr;
+        }
+      return fail(MOE_ERR_CUDA, "cudaIpcOpenMemHandle(rank %d): %s", s, cudaGetErrorString(e));
+    }
+    ep->peer[s] = static_cast<uint8_t*>(p);
+    ep->opened[s] = true;
+  }
+  ep->connected = true;
+  return 0;
+}
+
+int moe_ep_set_weights(moe_ep_t ep, const void* w_up_local, const void* w_down_local, const float* w_up_scale,
+                       const float* w_down_scale, void* stream) {
+  t_err[0] = 0;
+  if (!ep || !w_up_local || !w_down_local) return fail(MOE_ERR_INVALID_ARG, "null argument");
+  if (int r = ep_check_device(ep)) return r;
+  if (ep->dtype == MOE_DTYPE_FP8_E4M3_BLK128 && (!w_up_scale || !w_down_scale))
+    return fail(MOE_ERR_INVALID_ARG, "FP8 weights need w_up_scale and w_down_scale");
+  ep->w_up = w_up_local;
+  ep->w_down = w_down_local;
+  ep->w_up_scale = w_up_scale;
+  ep->w_down_scale = w_down_scale;
+  if (small_supported(ep->D, ep->F, ep->dtype))
+    if (int r = prepare_small(w_up_local, w_down_local, ep->D, ep->F, ep->el, ep->dtype, ep->ws, ep->ws_bytes,
+                              static_cast<cudaStream_t>(stream)))
+      return r;
+  ep->weights_set = true;
+  return 0;
+}
+
+int moe_ep_forward(moe_ep_t ep, const void* x, const int32_t* group_sizes, float* y, int64_t M, void* stream) {
+  t_err[0] = 0;
+  if (!ep) return fail(MOE_ERR_INVALID_ARG, "null engine");
+  if (!ep->connected) return fail(MOE_ERR_INVALID_ARG, "engine not connected (moe_ep_connect)");
+  if (!ep->weights_set) return fail(MOE_ERR_INVALID_ARG, "no expert weights (moe_ep_set_weights)");
+  if (int r = ep_check_device(ep)) return r;
+  if (M < 0 || M > ep->max_tokens)
+    return fail(MOE_ERR_INVALID_ARG, "M=%lld outside [0, max_tokens=%lld]", (long long)M, (long long)ep->max_tokens);
+  if (!group_sizes) return fail(MOE_ERR_INVALID_ARG, "null group_sizes");
+  if (M > 0 && (!x || !y)) return fail(MOE_ERR_INVALID_ARG, "null x or y");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15u)
+    return fail(MOE_ERR_MISALIGNED, "x and y must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  EpArgs a;
+  memset(&a, 0, sizeof(a));
+  for (int s = 0; s < ep->world; ++s) a.base[s] = ep->peer[s];
+  a.rank = ep->rank;
+  a.world = ep->world;
+  a.el = ep->el;
+  a.E = ep->E;
+  a.waves = ep->waves;
+  a.region_cap = ep->region_cap;
+  a.max_rows = (int)ep->max_tokens;
+  a.M = (int)M;
+  a.epoch = ++ep->epoch;
+  a.off_gs = ep->off_gs;
+  a.off_x = ep->off_x;
+  a.off_y = ep->off_y;
+  a.region_x_bytes = ep->region_x_bytes;
+  a.region_y_bytes = ep->region_y_bytes;
+  a.row_bytes_x = ep->D * (ep->dtype == MOE_DTYPE_F32 ? 4 : 2);
+  a.row_bytes_y = ep->D * 4;
+  a.gs = group_sizes;
+  a.x = static_cast<const uint8_t*>(x);
+  a.y = y;
+  a.slices = ep->slices;
+  a.wave_rows = ep->wave_rows;
+  a.local_gs = ep->local_gs;
+  a.routed = ep->routed;
+  a.push_ctr = ep->push_ctr;
+  a.abort_word = ep->abort_word;
+  a.status = ep->status;
+
+  MOE_CUDA_TRY(cudaEventRecord(ep->ev_start, st));
+  MOE_CUDA_TRY(cudaStreamWaitEvent(ep->comm, ep->ev_start, 0));
+  ep_counts_kernel<<<1, 1024, ep_counts_smem(ep->world, ep->E, ep->waves), ep->comm>>>(a);
+  MOE_CUDA_TRY(cudaGetLastError());
+  for (int v = 0; v < ep->waves; ++v) {
+    ep_push_kernel<<<ep->comm_ctas, 1024, 0, ep->comm>>>(a, v);
+    MOE_CUDA_TRY(cudaGetLastError());
+    MOE_CUDA_TRY(cudaEventRecord(ep->ev_push[v], ep->comm));
+  }
+  RunOpts opt;
+  opt.ctas = ep->mlp_ctas;
+  opt.skip_tail = true;
+  for (int v = 0; v < ep->waves; ++v) {
+    MOE_CUDA_TRY(cudaStreamWaitEvent(st, ep->ev_push[v], 0));
+    ep_wait_kernel<<<1, 32, 0, st>>>(a, v);
+    MOE_CUDA_TRY(cudaGetLastError());
+    const void* xr = ep->buf + ep->off_x + (size_t)v * ep->region_x_bytes;
+    float* yr = reinterpret_cast<float*>(ep->buf + ep->off_y + (size_t)v * ep->region_y_bytes);
+    const int32_t* gs_v = ep->local_gs + (size_t)v * ep->el;
+    int r;
+    if (small_supported(ep->D, ep->F, ep->dtype))
+      r = run_small(xr, ep->w_up, ep->w_down, gs_v, yr, ep->region_cap, ep->D, ep->F, ep->el, ep->dtype, ep->ws,
+                    ep->ws_bytes, st, opt);
+    else
+      r = run_large(xr, ep->w_up, ep->w_down, gs_v, ep->w_up_scale, ep->w_down_scale, yr, ep->region_cap, ep->D,
+                    ep->F, ep->el, ep->dtype, ep->ws, ep->ws_bytes, st, opt);
+    if (r) return r;
+    MOE_CUDA_TRY(cudaEventRecord(ep->ev_mlp[v], st));
+    MOE_CUDA_TRY(cudaStreamWaitEvent(ep->comm, ep->ev_mlp[v], 0));
+    ep_pull_kernel<<<ep->comm_ctas, 1024, 0, ep->comm>>>(a, v);
+    MOE_CUDA_TRY(cudaGetLastError());
+  }
+  MOE_CUDA_TRY(cudaEventRecord(ep->ev_end, ep->comm));
+  MOE_CUDA_TRY(cudaStreamWaitEvent(st, ep->ev_end, 0));
+  return 0;
+}
+
+int moe_ep_launches_per_forward(moe_ep_t ep) {
+  if (!ep) return fail(MOE_ERR_INVALID_ARG, "null engine");
+  return 1 + ep->waves * (3 + ep_mlp_launches(ep));
+}
+
+int moe_ep_destroy(moe_ep_t ep) {
+  t_err[0] = 0;
+  ep_release(ep);
+  return 0;
 }
 
 }  // extern "C"

@@ -15,6 +15,7 @@ LIB_PATH = Path(__file__).resolve().parent.parent / "lib" / "libmoe_b200.so"
 MOE_DTYPE_F32 = 0
 MOE_DTYPE_BF16 = 1
 MOE_DTYPE_FP8_E4M3_BLK128 = 2
+MOE_EP_HANDLE_BYTES = 256
 
 ERRORS = {
     -1: "MOE_ERR_INVALID_ARG",
@@ -62,6 +63,20 @@ def lib() -> ctypes.CDLL:
     L.moe_version.restype = ctypes.c_int
     L.moe_set_tuning.argtypes = [i32, i64]
     L.moe_set_tuning.restype = ctypes.c_int
+    L.moe_ep_create.argtypes = [i32, i32, i32, i64, i32, i32, i32, i32, i32, ctypes.POINTER(vp)]
+    L.moe_ep_create.restype = ctypes.c_int
+    L.moe_ep_export.argtypes = [vp, vp]
+    L.moe_ep_export.restype = ctypes.c_int
+    L.moe_ep_connect.argtypes = [vp, vp]
+    L.moe_ep_connect.restype = ctypes.c_int
+    L.moe_ep_set_weights.argtypes = [vp, vp, vp, vp, vp, vp]
+    L.moe_ep_set_weights.restype = ctypes.c_int
+    L.moe_ep_forward.argtypes = [vp, vp, vp, vp, i64, vp]
+    L.moe_ep_forward.restype = ctypes.c_int
+    L.moe_ep_launches_per_forward.argtypes = [vp]
+    L.moe_ep_launches_per_forward.restype = ctypes.c_int
+    L.moe_ep_destroy.argtypes = [vp]
+    L.moe_ep_destroy.restype = ctypes.c_int
     _lib = L
     return L
 

@@ -170,3 +170,18 @@ def test_workspace_sizes():
     # bf16 small-D needs nothing; bf16 large-D holds H (M, F) in bf16.
     assert L.moe_fused_mlp_workspace_size(65536, 128, 512, 8, 1) == 0
     assert L.moe_fused_mlp_workspace_size(32768, 4096, 14336, 8, 1) == 32768 * 14336 * 2
+
+
+def test_ep_engine_validates_arguments_before_any_device_work():
+    L = _lib.lib()
+    h = ctypes.c_void_p()
+    # rank / world out of range, too many waves, unknown dtype, shape without a kernel.
+    assert L.moe_ep_create(2, 2, 4, 1024, 128, 512, 0, 2, 0, ctypes.byref(h)) == -1
+    assert L.moe_ep_create(0, 9, 4, 1024, 128, 512, 0, 2, 0, ctypes.byref(h)) == -1
+    assert L.moe_ep_create(0, 2, 4, 1024, 128, 512, 0, 9, 0, ctypes.byref(h)) == -1
+    assert L.moe_ep_create(0, 2, 1025, 1024, 128, 512, 0, 2, 0, ctypes.byref(h)) == -1
+    assert L.moe_ep_create(0, 2, 4, 1024, 128, 512, 7, 2, 0, ctypes.byref(h)) == -3
+    assert L.moe_ep_create(0, 2, 4, 1024, 300, 512, 1, 2, 0, ctypes.byref(h)) == -2
+    assert h.value is None
+    assert L.moe_ep_forward(None, None, None, None, 0, None) == -1
+    assert L.moe_ep_launches_per_forward(None) == -1

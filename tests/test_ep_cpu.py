@@ -42,7 +42,7 @@ def _rank_inputs(rank, M, D, E, mode):
     return x, gs.astype(np.int32)
 
 
-def _worker(rank, world, port, E, D, F, M, modes, q, fail_rank=-1):
+def _worker(rank, world, port, E, D, F, M, modes, q, fail_rank=-1, waves=1):
     try:
         sys.path[:0] = [str(REPO / "pallas-moe-kernel_b200"), str(REPO)]
         import datetime
@@ -59,7 +59,7 @@ def _worker(rank, world, port, E, D, F, M, modes, q, fail_rank=-1):
             return torch.from_numpy(orc.ref_ragged_mlp(xr.numpy(), wu_l, wd_l, gs.numpy()))
 
         layer = ExpertParallelMLP(None, None, rank=rank, world=world, num_local_experts=El, max_tokens=M,
-                                  expert_fn=expert_fn, out_dtype=torch.float64)
+                                  expert_fn=expert_fn, out_dtype=torch.float64, waves=waves)
         if rank == fail_rank:
             raise SystemExit(3)          # this rank leaves before the exchange
         err = 0.0
@@ -76,11 +76,11 @@ def _worker(rank, world, port, E, D, F, M, modes, q, fail_rank=-1):
         q.put((rank, "error", traceback.format_exc(limit=3)))
 
 
-def _run(world, E, D, F, M, modes, fail_rank=-1, timeout=120):
+def _run(world, E, D, F, M, modes, fail_rank=-1, timeout=120, waves=1):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_worker, args=(r, world, port, E, D, F, M, modes, q, fail_rank)) for r in range(world)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, E, D, F, M, modes, q, fail_rank, waves)) for r in range(world)]
     for p in ps:
         p.start()
     out = {}
@@ -94,11 +94,13 @@ def _run(world, E, D, F, M, modes, fail_rank=-1, timeout=120):
     return out
 
 
-@pytest.mark.parametrize("world,E", [(2, 4), (4, 4)])
-def test_ep_matches_single_process_oracle(world, E):
+@pytest.mark.parametrize("world,E,waves", [(2, 4, 1), (4, 4, 1), (2, 4, 3), (4, 8, 2)])
+def test_ep_matches_single_process_oracle(world, E, waves):
     """Uniform routing with unrouted trailing rows, then one-expert-per-rank
-    skew (most experts empty on every rank), through the same layer."""
-    out = _run(world, E, D=16, F=24, M=40, modes=("uniform", "skewed", "uniform"))
+    skew (most experts empty on every rank), through the same layer; with
+    waves > 1 the groups are cut into slices (some empty: groups smaller than
+    the wave count) whose exchanges overlap."""
+    out = _run(world, E, D=16, F=24, M=40, modes=("uniform", "skewed", "uniform"), waves=waves)
     for r in range(world):
         status, err = out[r]
         assert status == "ok", out
@@ -111,3 +113,16 @@ def test_ep_rank_failure_is_reported_not_hung():
     out = _run(2, 4, D=8, F=8, M=16, modes=("uniform",), fail_rank=1, timeout=90)
     assert out[1][0] == "left"
     assert out[0][0] == "error", out
+
+
+def test_wave_cuts_partition_every_group():
+    from importlib import import_module
+    sys.path[:0] = [str(REPO / "pallas-moe-kernel_b200")]
+    ep = import_module("src.ep")
+    counts = torch.tensor([[0, 1, 2, 7], [5, 3, 100, 64]])
+    for v in (1, 2, 3, 4, 8):
+        cut = ep.ExpertParallelMLP.wave_cuts(counts, v)
+        assert cut.shape == (2, 4, v + 1)
+        assert torch.equal(cut[..., 0], torch.zeros_like(counts)) and torch.equal(cut[..., -1], counts)
+        d = cut.diff(dim=-1)
+        assert bool((d >= 0).all()) and bool((d.max(-1).values - d.min(-1).values <= 1).all())

@@ -35,7 +35,7 @@ def _worker(rank, world, port, case, q):
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
         dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                                 device_id=dev)
-        M, D, F, E, dt = case
+        M, D, F, E, dt, waves = case
         rng = np.random.default_rng(7)
         wu = (rng.standard_normal((E, D, F)) / np.sqrt(D)).astype(np.float32)
         wd = (rng.standard_normal((E, F, D)) / np.sqrt(F)).astype(np.float32)
@@ -44,7 +44,7 @@ def _worker(rank, world, port, case, q):
         wd_t = torch.from_numpy(wd).to(dev, tdt)
         El = E // world
         layer = ExpertParallelMLP(wu_t[rank * El:(rank + 1) * El], wd_t[rank * El:(rank + 1) * El],
-                                  rank=rank, world=world, max_tokens=M)
+                                  rank=rank, world=world, max_tokens=M, waves=waves)
         r2 = np.random.default_rng(100 + rank)
         x = torch.from_numpy(r2.standard_normal((M, D)).astype(np.float32)).to(dev, tdt)
         gs = r2.multinomial(M - 5, np.full(E, 1.0 / E)).astype(np.int32)
@@ -59,7 +59,8 @@ def _worker(rank, world, port, case, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("case,tol", [((2048, 128, 512, 4, "f32"), 1e-5), ((1024, 512, 1024, 4, "bf16"), 1e-2)])
+@pytest.mark.parametrize("case,tol", [((2048, 128, 512, 4, "f32", 1), 1e-5), ((1024, 512, 1024, 4, "bf16", 1), 1e-2),
+                                      ((2048, 128, 512, 4, "f32", 3), 1e-5), ((2048, 512, 1024, 4, "bf16", 2), 1e-2)])
 def test_ep_two_gpus(case, tol):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
