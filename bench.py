@@ -430,7 +430,11 @@ def main() -> int:
     from src.routing import CONFIGS, with_shape
     cfg = CONFIGS[args.config]
     if args.tokens:
-        cfg = with_shape(cfg, M=args.tokens, name=f"{cfg.name}_M{args.tokens}")
+        # Top-k configs route `tokens` router inputs to M = k * tokens rows.
+        k = {"top2": 2, "top8_softmax": 8}.get(cfg.routing, 0)
+        if k and args.tokens % k:
+            raise SystemExit(f"--tokens must be a multiple of {k} for {cfg.routing} routing")
+        cfg = with_shape(cfg, M=args.tokens, tokens=args.tokens // k if k else 0, name=f"{cfg.name}_M{args.tokens}")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
