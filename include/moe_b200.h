@@ -158,9 +158,10 @@ int moe_fused_mlp_noalloc(const float* x, const float* w_up, const float* w_down
  * Exit:  moe_ep_destroy on every rank, after a host barrier that follows
  *        every rank's last forward having completed.
  *
- * Failure: every wait for a peer is bounded (5 s); a wait that runs out sets
+ * Failure: every wait for a peer is bounded (2 s); a wait that runs out sets
  * status bit 4 (moe_device_status) and stops the engine's data movement for
- * good (later forwards return zeros), so a dead peer never hangs a GPU.
+ * good (that forward's and every later forward's routed rows of Y are
+ * undefined; destroy the engine), so a dead peer never hangs a GPU.
  * Group sizes beyond M or beyond a landing region are cut (status bit 8).
  */
 typedef struct moe_ep_s* moe_ep_t;

@@ -41,7 +41,7 @@ namespace moe {
 constexpr int kEpMaxWorld = 8;   // one NVSwitch domain of an HGX B200 node
 constexpr int kEpMaxWaves = 8;
 constexpr int kEpMaxExperts = 2048;
-constexpr uint64_t kEpWaitLimitNs = 5000000000ull;  // 5 s: ranks may start a step a few seconds apart
+constexpr uint64_t kEpWaitLimitNs = 2000000000ull;  // 2 s: far above any skew between ranks of one step
 
 enum : int {
   kStatusPeerTimeout = 4,   // a peer's flag did not arrive within kEpWaitLimitNs

@@ -177,3 +177,62 @@ def test_engine_two_gpus(case, tol):
     for rank, status, err, dev_status in res:
         assert status == "ok", res
         assert err <= tol and dev_status == 0, res
+
+
+def _timeout_worker(rank, world, port, q):
+    """Rank 1 skips a step (between steps: none of its kernels in flight);
+    rank 0's count barrier must give up within its bound, report status bit
+    4 and leave the device usable."""
+    try:
+        sys.path[:0] = [str(REPO / "pallas-moe-kernel_b200"), str(REPO)]
+        import datetime
+        import time
+        import torch.distributed as dist
+        from src import _lib
+        from src.ep import PeerExpertParallelMLP
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=dev)
+        D, F, El = 128, 512, 2
+        wu = torch.randn((El, D, F), device=dev) / D ** 0.5
+        wd = torch.randn((El, F, D), device=dev) / F ** 0.5
+        layer = PeerExpertParallelMLP(wu, wd, rank=rank, world=world, max_tokens=256, waves=1)
+        x = torch.randn((256, D), device=dev)
+        gs = torch.full((El * world,), 64, dtype=torch.int32, device=dev)
+        layer(x, gs)                                   # one good step on both ranks
+        torch.cuda.synchronize()
+        good = _lib.device_status(reset=True)
+        t = 0.0
+        if rank == 0:                                  # rank 1 does not take part in this step
+            t0 = time.time()
+            layer(x, gs)
+            torch.cuda.synchronize()
+            t = time.time() - t0
+        status = _lib.device_status(reset=True)
+        ok_after = float(torch.ones(4, device=dev).sum())   # the context still works
+        layer.close()
+        q.put((rank, "ok", (good, status, t, ok_after)))
+        dist.destroy_process_group()
+    except Exception:
+        q.put((rank, "error", traceback.format_exc(limit=6)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_engine_peer_wait_times_out_with_status():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_timeout_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict((r, (s, v)) for r, s, v in (q.get(timeout=300) for _ in range(2)))
+    for p in ps:
+        p.join(timeout=60)
+    assert res[0][0] == "ok" and res[1][0] == "ok", res
+    good0, status0, t0, after0 = res[0][1]
+    assert good0 == 0 and res[1][1][0] == 0
+    assert status0 & 4, res           # the count barrier gave up
+    assert 1.5 < t0 < 30.0, res       # after its 2 s bound, not forever
+    assert after0 == 4.0 and res[1][1][1] == 0
