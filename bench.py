@@ -416,6 +416,10 @@ def main() -> int:
     ap.add_argument("--ref-budget", type=float, default=10.0, help="seconds of CPU baseline timing")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tokens", type=int, default=0, help="override M (routed rows per GPU)")
+    ap.add_argument("--dtype", default="", choices=["", "f32", "bf16", "fp8"],
+                    help="override the configuration's precision path (same shapes and routing)")
+    ap.add_argument("--experts", type=int, default=0,
+                    help="override E (with --tokens: a smaller case with the same rows per expert)")
     ap.add_argument("--waves", type=int, default=2,
                     help="N>1: token waves per step (dispatch/combine of one wave overlap the experts of the next)")
     ap.add_argument("--reserve-sms", type=int, default=0,
@@ -435,6 +439,10 @@ def main() -> int:
         if k and args.tokens % k:
             raise SystemExit(f"--tokens must be a multiple of {k} for {cfg.routing} routing")
         cfg = with_shape(cfg, M=args.tokens, tokens=args.tokens // k if k else 0, name=f"{cfg.name}_M{args.tokens}")
+    if args.experts:
+        cfg = with_shape(cfg, E=args.experts, name=f"{cfg.name}_E{args.experts}")
+    if args.dtype and args.dtype != cfg.dtype:
+        cfg = with_shape(cfg, dtype=args.dtype, name=f"{cfg.name}_as_{args.dtype}")
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

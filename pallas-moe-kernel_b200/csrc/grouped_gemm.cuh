@@ -19,7 +19,8 @@
 //
 // Warp roles: warp 0 TMA producer (both CTAs), warp 1 TMEM owner + MMA
 // issuer (leader), warps 2..5 epilogue (one TMEM lane quadrant each; both
-// CTAs), and for e4m3 weights warps 6..9 dequantise each raw B tile
+// CTAs), and for e4m3 weights warp 10 streams raw B tiles into a deep ring
+// of their own while warps 6..9 dequantise each raw B tile
 // (e4m3 x 128x128 block scale -> bf16) into the MMA's operand layout.
 #pragma once
 #include "fused_small.cuh"
@@ -48,18 +49,23 @@ struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;          // 16 KB
   static constexpr int B_BYTES = (BN / 2) * BK * 2;    // 16 KB (two 64-column atoms, bf16)
   static constexpr int B8_BYTES = BFP8 ? (BN / 2) * BK : 0;  // 8 KB raw e4m3 tile
-  static constexpr int STAGE = A_BYTES + B_BYTES + B8_BYTES;
-  static constexpr int NS = BFP8 ? 5 : 6;
+  static constexpr int STAGE = A_BYTES + B_BYTES;      // operand stage (A + bf16 B)
+  static constexpr int NS = BFP8 ? 4 : 6;              // operand stages
+  static constexpr int NR = BFP8 ? 10 : 0;             // raw e4m3 stages (HBM stream runs ahead)
   static constexpr int EPI_WARPS = 4;
   static constexpr int CVT_WARPS = BFP8 ? 4 : 0;
   static constexpr int OUT_STAGE = EPI_WARPS * 32 * 128;  // 4 KB per warp: 32 rows x 128 B
-  static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM = 1024 + NS * STAGE + OUT_STAGE + BAR_BYTES;
+  static constexpr int BAR_BYTES = BFP8 ? 512 : 256;
+  static constexpr int SMEM = 1024 + NS * STAGE + NR * B8_BYTES + OUT_STAGE + BAR_BYTES;
   static constexpr int TMEM_COLS = 512;                 // 2 accumulators x 256 columns
   static constexpr uint32_t IDESC = make_idesc(kFmtBF16, 256, BN, 0, 1);
   static constexpr uint32_t TX = 2 * (A_BYTES + B_BYTES);  // both CTAs (bf16 B)
-  static constexpr uint32_t TX_RAW = A_BYTES + B8_BYTES;   // this CTA (FP8 B)
-  static constexpr int THREADS = 64 + (EPI_WARPS + CVT_WARPS) * 32;
+  static constexpr uint32_t TX_A = 2 * A_BYTES;            // both CTAs' A (FP8 B arrives converted)
+  static constexpr int RAW_WARP = 2 + EPI_WARPS + CVT_WARPS;  // FP8: producer of the raw ring
+  static constexpr int THREADS = 64 + (EPI_WARPS + CVT_WARPS) * 32 + (BFP8 ? 32 : 0);
+  // Register cap: that of a 320-thread block at least (the bf16 epilogue
+  // was scheduled under it), or of the FP8 block with its extra warps.
+  static constexpr int LAUNCH_BOUND = THREADS > 320 ? THREADS : 320;
   static_assert(SMEM <= kMaxSmemPerBlock, "shared memory budget");
 };
 
@@ -124,21 +130,23 @@ struct TileCursor {
 };
 
 template <int EPI, bool BFP8>
-__global__ void __launch_bounds__(64 + 256, 1)
+__global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
   using C = GemmCfg<EPI, BFP8>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   uint8_t* ring = smem;
-  uint8_t* ostage = ring + C::NS * C::STAGE;
+  uint8_t* rawring = ring + C::NS * C::STAGE;   // FP8: [NR] raw e4m3 B tiles
+  uint8_t* ostage = rawring + C::NR * C::B8_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(ostage + C::OUT_STAGE);
   uint64_t* full = bars;                // [NS] leader
   uint64_t* empty = bars + C::NS;       // [NS] both (multicast commit)
   uint64_t* acc_full = bars + 2 * C::NS;  // [2] both (multicast commit)
   uint64_t* acc_empty = acc_full + 2;     // [2] leader (epilogue warps of both CTAs)
-  uint64_t* raw = acc_full + 4;           // [NS] local: A + e4m3 B landed (FP8 only)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(raw + C::NS);
+  uint64_t* raw_full = acc_full + 4;      // [NR] local: raw e4m3 B landed (FP8 only)
+  uint64_t* raw_empty = raw_full + C::NR; // [NR] local: converters done with the raw tile
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(raw_empty + C::NR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const uint32_t warp = warp_id();
@@ -152,11 +160,14 @@ __global__ void __launch_bounds__(64 + 256, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::NS; ++i) {
-      // bf16 B: the leader producer's arrive + both CTAs' TMA bytes.
-      // e4m3 B: one arrival per converter warp of both CTAs.
-      mbar_init(full + i, BFP8 ? 2 * C::CVT_WARPS : 1);
+      // The leader producer's arrive + both CTAs' TMA bytes; e4m3 B adds one
+      // arrival per converter warp of both CTAs.
+      mbar_init(full + i, BFP8 ? 1 + 2 * C::CVT_WARPS : 1);
       mbar_init(empty + i, 1);
-      mbar_init(raw + i, 1);
+    }
+    for (int i = 0; i < C::NR; ++i) {
+      mbar_init(raw_full + i, 1);
+      mbar_init(raw_empty + i, C::CVT_WARPS);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(acc_full + i, 1);
@@ -203,11 +214,11 @@ __global__ void __launch_bounds__(64 + 256, 1)
           }
           uint8_t* st = ring + stage * C::STAGE;
           if constexpr (BFP8) {
-            // A and the raw e4m3 B tile land in this CTA; the converter warps
-            // turn B into the bf16 operand and signal the leader.
-            mbar_arrive_expect_tx(raw + stage, C::TX_RAW);
-            tma_load_2d_hint(st, &maps.a, raw + stage, kb * C::BK, row0, pol_a);
-            tma_load_2d_hint(st + C::A_BYTES + C::B_BYTES, &maps.b, raw + stage, n0, brow0 + kb * C::BK, pol_b);
+            // A of both CTAs lands on the leader's barrier; the bf16 B half
+            // of each CTA comes from its converter warps (raw ring below).
+            const uint32_t bar = full_l0 + stage * 8;
+            if (rank == 0) mbar_arrive_expect_tx(full + stage, C::TX_A);
+            tma_load_2d_pair(st, &maps.a, bar, kb * C::BK, row0, pol_a);
           } else {
             const uint32_t bar = full_l0 + stage * 8;
             if (rank == 0) mbar_arrive_expect_tx(full + stage, C::TX);
@@ -262,16 +273,49 @@ __global__ void __launch_bounds__(64 + 256, 1)
         umma_commit_pair(acc_full + ab, kBoth);
       }
     }
+  } else if (BFP8 && warp == (uint32_t)C::RAW_WARP) {
+    // ------------------------------------------------------------ raw e4m3 B producer (both CTAs)
+    // Streams this CTA's half of every B tile from HBM into a ring of NR raw
+    // stages that runs ahead of the operand ring by up to NR tiles.
+    if (lane == 0) {
+      TileCursor cur;
+      int rs = 0;
+      uint32_t rph = 0;
+      const uint64_t pol_b = l2_policy_evict_last();
+      bool ok = true;
+      for (int t = pair; ok; t += npairs) {
+        if (!cur.seek(t, p.group_sizes, p.E, p.M, nt)) break;
+        int mb, nb;
+        cur.coords(t, nt, p.group_m, mb, nb);
+        const int n0 = nb * C::BN + (int)rank * (C::BN / 2);
+        const int brow0 = cur.e * p.k_rows_per_e;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(raw_empty + rs, rph ^ 1u, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(raw_full + rs, C::B8_BYTES);
+          tma_load_2d_hint(rawring + rs * C::B8_BYTES, &maps.b, raw_full + rs, n0, brow0 + kb * C::BK, pol_b);
+          if (++rs == C::NR) {
+            rs = 0;
+            rph ^= 1u;
+          }
+        }
+      }
+    }
   } else if (BFP8 && warp >= 2u + C::EPI_WARPS) {
     // ------------------------------------------------------------ e4m3 -> bf16 B converters (both CTAs)
-    // Thread t handles k-row r = t/2 of the 64 x 128 raw tile and half h of its
-    // 128 columns (= one 64-column bf16 atom row, 128 bytes).
+    // Thread t handles k-row r = t % 64 of the 64 x 128 raw tile and half
+    // h = t / 64 of its 128 columns (= one 64-column bf16 atom row, 128
+    // bytes): the 8 threads of a quarter-warp own 8 consecutive rows, so their
+    // swizzled 16-byte accesses fall in 8 distinct bank groups.  A raw tile is
+    // converted as soon as it has landed and its operand stage is free.
     const int ct = (int)threadIdx.x - 64 - C::EPI_WARPS * 32;  // 0..127
-    const int r = ct >> 1, h = ct & 1;
+    const int r = ct & 63, h = ct >> 6;
     const int nkb_scale = p.K / 128, nnb_scale = p.N / 128;
     TileCursor cur;
-    int stage = 0;
-    uint32_t phase = 0;
+    int stage = 0, rs = 0;
+    uint32_t phase = 0, rph = 0;
     bool ok = true;
     for (int t = pair; ok; t += npairs) {
       if (!cur.seek(t, p.group_sizes, p.E, p.M, nt)) break;
@@ -279,15 +323,22 @@ __global__ void __launch_bounds__(64 + 256, 1)
       cur.coords(t, nt, p.group_m, mb, nb);
       const int n0 = nb * C::BN + (int)rank * (C::BN / 2);
       const float* srow = p.b_scale + ((size_t)cur.e * nkb_scale) * nnb_scale + n0 / 128;
+      // The tile's block scales along K (one per 128 rows of B), fetched once
+      // per tile -- lane l holds k-blocks l and l + 32 -- and broadcast per
+      // stage, so no stage waits on a global load.
+      const float s_lo = (int)lane < nkb_scale ? __ldg(srow + (size_t)lane * nnb_scale) : 0.f;
+      const float s_hi = (int)lane + 32 < nkb_scale ? __ldg(srow + (size_t)(lane + 32) * nnb_scale) : 0.f;
       for (int kb = 0; kb < nk; ++kb) {
-        if (!mbar_wait_warp(raw + stage, phase, abort_flag, p.status)) {
+        if (!mbar_wait_warp(raw_full + rs, rph, abort_flag, p.status) ||
+            !mbar_wait_warp(empty + stage, phase ^ 1u, abort_flag, p.status)) {
           ok = false;
           break;
         }
-        const float sc = __ldg(srow + (size_t)((kb * C::BK) / 128) * nnb_scale);
-        uint8_t* st = ring + stage * C::STAGE;
-        const uint8_t* src = st + C::A_BYTES + C::B_BYTES + r * 128;  // 128-byte swizzled raw row
-        uint8_t* dst = st + C::A_BYTES + h * (64 * 128) + r * 128;   // atom h, row r (swizzled)
+        const int kblk = (kb * C::BK) / 128;
+        const float s_reg = __shfl_sync(0xffffffffu, kblk < 32 ? s_lo : s_hi, kblk & 31);
+        const float sc = kblk < 64 ? s_reg : __ldg(srow + (size_t)kblk * nnb_scale);
+        const uint8_t* src = rawring + rs * C::B8_BYTES + r * 128;             // 128-byte swizzled raw row
+        uint8_t* dst = ring + stage * C::STAGE + C::A_BYTES + h * (64 * 128) + r * 128;  // atom h, row r
         const int rsw = r & 7;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -301,10 +352,17 @@ __global__ void __launch_bounds__(64 + 256, 1)
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(full_l0 + stage * 8);
+        if (lane == 0) {
+          mbar_arrive(raw_empty + rs);
+          mbar_arrive_cluster_cta(full_l0 + stage * 8);
+        }
         if (++stage == C::NS) {
           stage = 0;
           phase ^= 1u;
+        }
+        if (++rs == C::NR) {
+          rs = 0;
+          rph ^= 1u;
         }
       }
     }
