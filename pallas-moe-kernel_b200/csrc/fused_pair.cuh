@@ -373,7 +373,7 @@ __global__ void __launch_bounds__(64 + 256, 1)
     // TMEM / shared-memory writes are complete.
     auto warp_arrive_leader = [&](uint32_t leader_bar) {
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(leader_bar);
+      if (lane == 0) mbar_arrive_cluster_cta(leader_bar);
     };
     auto prep_x = [&](uint32_t uidx) -> bool {
       if (!warp_wait(x_full, uidx & 1u)) return false;

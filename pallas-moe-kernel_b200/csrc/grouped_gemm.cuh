@@ -444,7 +444,7 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(acc_empty_l + ab * 8);
+      if (lane == 0) mbar_arrive_cluster_cta(acc_empty_l + ab * 8);
     }
   }
 
