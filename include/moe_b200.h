@@ -136,10 +136,13 @@ int moe_fused_mlp_noalloc(const float* x, const float* w_up, const float* w_down
  * and brings the f32 result back to the row's original position, so that on
  * every rank Y equals moe_fused_mlp over all experts.  Transfers are our own
  * kernels over peer memory (CUDA IPC mappings of one buffer per rank): rows
- * are stored straight into the owner's landing buffer and results loaded
- * straight from the owner's outbox, in `waves` slices per step so that the
- * exchange of one slice overlaps the experts of the next.  Group sizes are
- * exchanged on the device: a forward never synchronises the host.
+ * are stored straight into the owner's landing buffer.  For D > 256 (the
+ * two-GEMM experts) the combine is fused into the down GEMM: its epilogue
+ * stores every Y row straight into the row's source rank (`waves` is then
+ * 1).  For D <= 256 results are loaded back from the owner's outbox in
+ * `waves` slices per step, so that the exchange of one slice overlaps the
+ * experts of the next.  Group sizes are exchanged on the device: a forward
+ * never synchronises the host.
  *
  * Set-up, on every rank with its own GPU current:
  *   moe_ep_create   allocates the engine (device memory proportional to
@@ -155,6 +158,9 @@ int moe_fused_mlp_noalloc(const float* x, const float* w_up, const float* w_down
  *                   (prepared once for the f32 path).
  * Step:  moe_ep_forward on every rank, the same number of times on all
  *        ranks (it is a collective).  M <= max_tokens; x (M, D), y (M, D) f32.
+ *        For D > 256, y may be NULL: Y is then left in the engine's own
+ *        buffer (moe_ep_output; rows [0, M), valid until the next forward),
+ *        which saves the final copy into the caller's array.
  * Exit:  moe_ep_destroy on every rank, after a host barrier that follows
  *        every rank's last forward having completed.
  *
@@ -176,6 +182,8 @@ int moe_ep_set_weights(moe_ep_t ep, const void* w_up_local, const void* w_down_l
 int moe_ep_forward(moe_ep_t ep, const void* x, const int32_t* group_sizes, float* y, int64_t M, void* stream);
 /* Kernels one moe_ep_forward launches (exchange + expert kernels). */
 int moe_ep_launches_per_forward(moe_ep_t ep);
+/* Device address of the engine's own Y (D > 256 engines; NULL otherwise). */
+void* moe_ep_output(moe_ep_t ep);
 int moe_ep_destroy(moe_ep_t ep);
 
 /* Text of the calling thread's last error ("" when none). */

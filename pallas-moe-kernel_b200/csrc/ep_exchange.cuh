@@ -24,6 +24,12 @@
 //                      from every owner's Y outbox into the caller's Y (peer
 //                      loads); the last wave also zeroes Y's unrouted tail.
 //
+// Scatter mode (two-GEMM experts, one wave): there is no outbox; the down
+// GEMM's epilogue stores each Y row into its source's Y landing area (peer
+// stores), ep_ydone_kernel raises ydone[r] = t on every source, and
+// ep_finish_kernel waits for every owner's ydone and copies the landing area
+// into the caller's Y.
+//
 // Flags hold epochs, so they never need resetting.  Every wait targets flags
 // raised by OTHER GPUs only (a rank's own slices are ordered by stream
 // events), each is bounded in time, and a wait that runs out records
@@ -52,6 +58,7 @@ struct EpFlags {
   uint32_t cnt[kEpMaxWorld];                 // cnt[s] = t: source s published its group sizes of step t
   uint32_t data[kEpMaxWaves][kEpMaxWorld];   // data[v][s] = t: source s's rows of wave v have landed here
   uint32_t done[kEpMaxWaves][kEpMaxWorld];   // done[v][s] = t: owner s's outputs of wave v are ready
+  uint32_t ydone[kEpMaxWorld];               // ydone[p] = t: owner p stored all of this rank's Y rows
 };
 static_assert(sizeof(EpFlags) <= 4096, "flag block");
 
@@ -89,6 +96,8 @@ struct EpArgs {
   EpSlice* slices;       // [waves][E]
   int* wave_rows;        // [waves][E + 1] prefix of slice rows (row -> slice search)
   int* local_gs;         // [waves][el] group sizes of each landing region
+  int4* recv;            // scatter mode: [el][world] {first region row, rows, first source row, source}
+  size_t off_yl;         // scatter mode: byte offset of the Y landing area (max_tokens rows)
   int* routed;           // rows of this rank's X that are routed (<= M)
   unsigned* push_ctr;    // [waves] CTAs finished with a push
   int* abort_word;
@@ -189,9 +198,10 @@ __device__ __forceinline__ int block_exclusive_scan(int* data, int n, int cap) {
 }
 
 // Shared memory of ep_counts_kernel beyond its static arrays: the count
-// table [world][E] and the per-wave expert totals [waves][E].
+// table [world][E], the per-wave expert totals [waves][E] and the sources'
+// row offsets [world][E].
 __host__ __device__ constexpr size_t ep_counts_smem(int world, int E, int waves) {
-  return (size_t)(world + waves) * E * sizeof(int);
+  return (size_t)(2 * world + waves) * E * sizeof(int);
 }
 
 // ---------------------------------------------------------------- kernels
@@ -205,6 +215,7 @@ __global__ void __launch_bounds__(1024) ep_counts_kernel(const __grid_constant__
   const int E = a.E, W = a.world, V = a.waves, EL = a.el;
   int* s_cnt = s_dyn;              // [W][E]
   int* s_T = s_dyn + W * E;        // [V][E]
+  int* s_src = s_T + V * E;        // [W][E] first row of (source, expert) in the source's X
   const int par = (int)(a.epoch & 1u);
 
   // This rank's group sizes: negatives count as 0, the running total is cut at M.
@@ -256,6 +267,13 @@ __global__ void __launch_bounds__(1024) ep_counts_kernel(const __grid_constant__
     s_cnt[i] = ok ? c : 0;
   }
   __syncthreads();
+  if (a.recv) {
+    // Scatter mode: where each source's rows of each expert start in that
+    // source's X (its own exclusive prefix over experts).
+    for (int i = tid; i < W * E; i += blockDim.x) s_src[i] = s_cnt[i];
+    __syncthreads();
+    for (int sr = 0; sr < W; ++sr) block_exclusive_scan(s_src + sr * E, E, 0x7fffffff);
+  }
   // T[v][g]: rows of expert g in wave v over all sources.
   for (int i = tid; i < V * E; i += blockDim.x) {
     const int v = i / E, g = i - v * E;
@@ -303,6 +321,21 @@ __global__ void __launch_bounds__(1024) ep_counts_kernel(const __grid_constant__
     }
     a.slices[i] = sl;
     s_T[i] = sl.n;
+  }
+  if (a.recv) {
+    // Scatter mode (one wave): for each of this rank's experts and each
+    // source, the region rows the source's rows landed on and where they go
+    // back to.  Same arithmetic as the owners' side of the slices above.
+    for (int i = tid; i < EL * W; i += blockDim.x) {
+      const int e = i / W, sr = i - e * W;
+      const int g = a.rank * EL + e;
+      int start = 0;
+      for (int e2 = 0; e2 < e; ++e2) start += a.local_gs[e2];
+      for (int s2 = 0; s2 < sr; ++s2) start += s_cnt[s2 * E + g];
+      int n = s_cnt[sr * E + g];
+      if (start + n > a.region_cap) n = max(0, a.region_cap - start);
+      a.recv[i] = make_int4(start, n, s_src[sr * E + g], sr);
+    }
   }
   __syncthreads();
   // Row prefix of every wave's slices (for the row -> slice search).
@@ -411,6 +444,35 @@ __global__ void __launch_bounds__(1024) ep_pull_kernel(const __grid_constant__ E
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x)
       t[i] = make_int4(0, 0, 0, 0);
   }
+}
+
+// Scatter mode: after this rank's down GEMM has stored every Y row it owns
+// into the sources' landing areas, tell every source (one warp).
+__global__ void ep_ydone_kernel(const __grid_constant__ EpArgs a) {
+  const int p = threadIdx.x;
+  if (*reinterpret_cast<volatile int*>(a.abort_word) != 0) return;
+  __threadfence_system();
+  if (p < a.world && p != a.rank) st_release_sys(&ep_flags(a, p)->ydone[a.rank], a.epoch);
+}
+
+// Scatter mode: waits until every owner has stored this rank's rows, then
+// copies the landing area into the caller's Y (unless Y is the landing area)
+// and zeroes Y's unrouted tail.
+__global__ void __launch_bounds__(1024) ep_finish_kernel(const __grid_constant__ EpArgs a) {
+  if (threadIdx.x < a.world && (int)threadIdx.x != a.rank && *reinterpret_cast<volatile int*>(a.abort_word) == 0)
+    ep_wait_flag(&ep_flags(a, a.rank)->ydone[threadIdx.x], a.epoch, a);
+  __syncthreads();
+  const bool ok = *reinterpret_cast<volatile int*>(a.abort_word) == 0;
+  const int routed = *a.routed;
+  const int4* src = reinterpret_cast<const int4*>(a.base[a.rank] + a.off_yl);
+  int4* y = reinterpret_cast<int4*>(a.y);
+  const size_t n_routed = (size_t)routed * (a.row_bytes_y >> 4);
+  const size_t n_all = (size_t)a.M * (a.row_bytes_y >> 4);
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  if (ok && y != src)
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_routed; i += stride) y[i] = src[i];
+  for (size_t i = n_routed + (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_all; i += stride)
+    y[i] = make_int4(0, 0, 0, 0);
 }
 
 }  // namespace moe

@@ -27,6 +27,19 @@
 
 namespace moe {
 
+// Expert-parallel combine fused into the f32 epilogue: each output row goes
+// straight to its source rank's Y landing area (peer stores over NVLink)
+// instead of this rank's Y.  `recv` lists, per local expert and source rank,
+// {first row of the expert's rows that came from that source, rows, first row
+// in the source's Y, source rank}.
+struct EpScatter {
+  uint8_t* base[8];    // every rank's symmetric buffer, in this process's address space
+  size_t off;          // byte offset of the Y landing area inside those buffers
+  const int4* recv;    // [E][world]
+  int world;
+  int on;
+};
+
 struct GemmParams {
   const int32_t* group_sizes;
   void* out;          // H (bf16, [M, N]) or Y (f32, [M, N])
@@ -39,7 +52,32 @@ struct GemmParams {
   int* status;
   const float* b_scale;  // FP8 weights: (E, K/128, N/128) f32 block scales, else null
   int skip_tail;         // 1: leave rows at or past sum(group_sizes) unwritten (Y only)
+  EpScatter scatter;     // Y only: rows go to their source ranks (expert parallelism)
 };
+
+// store_y_block with one destination row pointer per row: lane l of the warp
+// holds the pointer of row l of the 32-row block (null = not stored).
+__device__ __forceinline__ void store_y_rows(uint32_t taddr, float4* stage, uint8_t* row_ptr, int col0,
+                                             uint32_t lane) {
+  uint32_t v[32];
+  tmem_ld32(taddr, v);
+  tmem_ld_wait();
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    stage[lane * 8 + (k ^ (lane & 7))] = make_float4(__uint_as_float(v[4 * k]), __uint_as_float(v[4 * k + 1]),
+                                                     __uint_as_float(v[4 * k + 2]), __uint_as_float(v[4 * k + 3]));
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = 4 * i + (int)(lane >> 3);
+    const int k = (int)(lane & 7);
+    const float4 val = stage[r * 8 + (k ^ (r & 7))];
+    uint8_t* dst = reinterpret_cast<uint8_t*>(
+        __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(row_ptr), r));
+    if (dst) *reinterpret_cast<float4*>(dst + (size_t)(col0 + 4 * k) * 4) = val;
+  }
+  __syncwarp();
+}
 
 template <int EPI, bool BFP8>  // EPI 0: GELU -> bf16 H, 1: f32 Y; BFP8: e4m3 B dequantised in smem
 struct GemmCfg {
@@ -435,6 +473,24 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
           }
           __syncwarp();
         }
+      } else if (p.scatter.on) {
+        // Destination of row wrow0 + lane: the source rank whose rows of
+        // this expert cover it, at the row it came from.
+        const int R = wrow0 + (int)lane;
+        uint8_t* row_ptr = nullptr;
+        if (R < row_end) {
+          const int4* rc = p.scatter.recv + (size_t)cur.e * p.scatter.world;
+          for (int sr = 0; sr < p.scatter.world; ++sr) {
+            const int4 q = rc[sr];
+            if (R >= q.x && R < q.x + q.y) {
+              row_ptr = p.scatter.base[q.w] + p.scatter.off + (size_t)(q.z + (R - q.x)) * (size_t)p.N * 4;
+              break;
+            }
+          }
+        }
+        float4* wst4 = reinterpret_cast<float4*>(wst);
+#pragma unroll 1
+        for (int c0 = 0; c0 < C::BN; c0 += 32) store_y_rows(acc + c0, wst4, row_ptr, nb * C::BN + c0, lane);
       } else {
         float* Y = reinterpret_cast<float*>(p.out);
         float4* wst4 = reinterpret_cast<float4*>(wst);

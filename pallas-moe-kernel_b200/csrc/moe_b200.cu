@@ -204,6 +204,7 @@ static int launch_gemm(const GemmMaps& maps, const GemmParams& prm, DevInfo* di,
 struct RunOpts {
   int ctas = 0;
   bool skip_tail = false;
+  const EpScatter* scatter = nullptr;  // large-D path: rows of Y go to their source ranks
 };
 
 static int run_large(const void* x, const void* w_up, const void* w_down, const int32_t* gs,
@@ -245,6 +246,7 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
     if (int r = make_map_2d(&m2.b, w_down, BF16, 2, (uint64_t)E * F, D, 64, 64)) return r;
   }
   GemmParams p2{gs, y, (int)M, E, D, F, F, 8, status, w_down_scale, opt.skip_tail ? 1 : 0};
+  if (opt.scatter) p2.scatter = *opt.scatter;
   return fp8 ? launch_gemm<1, true>(m2, p2, di, st, ctas) : launch_gemm<1, false>(m2, p2, di, st, ctas);
 }
 
@@ -524,6 +526,9 @@ struct moe_ep_s {
   int dev = -1;
   int rank = 0, world = 1, el = 1, E = 1, D = 0, F = 0, dtype = 0, waves = 1;
   int comm_ctas = 16, mlp_ctas = 0;
+  bool scatter = false;  // large-D: combine fused into the down GEMM's epilogue
+  size_t off_yl = 0;     // scatter mode: Y landing area (max_tokens rows, f32)
+  int4* recv = nullptr;  // scatter mode: [el][world] receive table
   int64_t max_tokens = 0;
   int region_cap = 0;
   size_t off_gs = 0, off_x = 0, off_y = 0, region_x_bytes = 0, region_y_bytes = 0, buf_bytes = 0;
@@ -575,6 +580,8 @@ static void ep_release(moe_ep_s* ep) {
   if (prev >= 0) cudaSetDevice(prev);
   delete ep;
 }
+
+static_assert(kEpMaxWorld == 8, "EpScatter holds 8 peer buffers");
 
 static int ep_mlp_launches(const moe_ep_s* ep) {
   if (!small_supported(ep->D, ep->F, ep->dtype)) return 2;        // up + down grouped GEMMs
@@ -740,6 +747,11 @@ int moe_ep_create(int32_t rank, int32_t world, int32_t num_local_experts, int64_
   DevInfo* di;
   if (int r = device_info(&dev, &di)) return r;
 
+  // Large-D experts (two grouped GEMMs) take the combine into the down GEMM's
+  // epilogue: one wave on every SM, rows stored straight back to their
+  // sources.  Small-D experts pull their results back in `waves` slices.
+  const bool scatter = !small_supported(D, F, dtype);
+  if (scatter) waves = 1;
   // Rows per landing region: wave v of a group of c rows holds at most
   // ceil(c / waves) <= c / waves + 1 rows, over world sources and el experts.
   const int64_t cap64 = ((int64_t)world * max_tokens + waves - 1) / waves + (int64_t)world * num_local_experts;
@@ -764,12 +776,15 @@ int moe_ep_create(int32_t rank, int32_t world, int32_t num_local_experts, int64_
   ep->off_gs = 4096;
   ep->off_x = align256(ep->off_gs + (size_t)2 * world * ep->E * sizeof(int32_t));
   ep->region_x_bytes = align256((size_t)cap * D * sx);
+  ep->scatter = scatter;
   ep->off_y = ep->off_x + (size_t)waves * ep->region_x_bytes;
-  ep->region_y_bytes = align256((size_t)cap * D * sizeof(float));
-  ep->buf_bytes = ep->off_y + (size_t)waves * ep->region_y_bytes;
-  // Exchange kernels take the SMs the expert kernels leave free (pairs: even).
-  ep->mlp_ctas = world > 1 ? ((di->sms - ep->comm_ctas) & ~1) : 0;
-  if (world > 1 && ep->mlp_ctas < 2) {
+  ep->region_y_bytes = scatter ? 0 : align256((size_t)cap * D * sizeof(float));
+  ep->off_yl = ep->off_y + (size_t)waves * ep->region_y_bytes;
+  ep->buf_bytes = ep->off_yl + (scatter ? align256((size_t)max_tokens * D * sizeof(float)) : 0);
+  // Exchange kernels that run beside the experts take the SMs the expert
+  // kernels leave free (pairs: even); in scatter mode nothing runs beside them.
+  ep->mlp_ctas = world > 1 && !scatter ? ((di->sms - ep->comm_ctas) & ~1) : 0;
+  if (world > 1 && !scatter && ep->mlp_ctas < 2) {
     ep_release(ep);
     return fail(MOE_ERR_INVALID_ARG, "comm_ctas %d leaves no SMs for the experts", comm_ctas);
   }
@@ -785,7 +800,8 @@ int moe_ep_create(int32_t rank, int32_t world, int32_t num_local_experts, int64_
   const size_t t_rows = align256((size_t)waves * (ep->E + 1) * sizeof(int));
   const size_t t_gs = align256((size_t)waves * ep->el * sizeof(int));
   const size_t t_misc = 256 + (size_t)kEpMaxWaves * sizeof(unsigned) + 256;
-  const size_t t_all = t_slices + t_rows + t_gs + t_misc;
+  const size_t t_recv = scatter ? align256((size_t)ep->el * world * sizeof(int4)) : 0;
+  const size_t t_all = t_slices + t_rows + t_gs + t_misc + t_recv;
   if ((e = cudaMalloc(&ep->tables, t_all)) != cudaSuccess) return cuda_fail(e, "cudaMalloc(tables)");
   if ((e = cudaMemset(ep->tables, 0, t_all)) != cudaSuccess) return cuda_fail(e, "cudaMemset(tables)");
   ep->slices = reinterpret_cast<EpSlice*>(ep->tables);
@@ -794,6 +810,7 @@ int moe_ep_create(int32_t rank, int32_t world, int32_t num_local_experts, int64_
   ep->routed = reinterpret_cast<int*>(ep->tables + t_slices + t_rows + t_gs);
   ep->push_ctr = reinterpret_cast<unsigned*>(ep->tables + t_slices + t_rows + t_gs + 256);
   ep->abort_word = reinterpret_cast<int*>(ep->tables + t_slices + t_rows + t_gs + 256 + 256);
+  if (scatter) ep->recv = reinterpret_cast<int4*>(ep->tables + t_slices + t_rows + t_gs + t_misc);
   ep->ws_bytes = small_supported(D, F, dtype) ? align256(small_plan(cap, D, F, ep->el, dtype).ws_bytes)
                                               : align256(large_ws_bytes(cap, F));
   if (ep->ws_bytes && (e = cudaMalloc(&ep->ws, ep->ws_bytes)) != cudaSuccess) return cuda_fail(e, "cudaMalloc(workspace)");
@@ -921,7 +938,8 @@ int moe_ep_forward(moe_ep_t ep, const void* x, const int32_t* group_sizes, float
   if (M < 0 || M > ep->max_tokens)
     return fail(MOE_ERR_INVALID_ARG, "M=%lld outside [0, max_tokens=%lld]", (long long)M, (long long)ep->max_tokens);
   if (!group_sizes) return fail(MOE_ERR_INVALID_ARG, "null group_sizes");
-  if (M > 0 && (!x || !y)) return fail(MOE_ERR_INVALID_ARG, "null x or y");
+  if (M > 0 && (!x || (!y && !ep->scatter))) return fail(MOE_ERR_INVALID_ARG, "null x or y");
+  if (!y && ep->scatter) y = reinterpret_cast<float*>(ep->buf + ep->off_yl);
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15u)
     return fail(MOE_ERR_MISALIGNED, "x and y must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -951,6 +969,8 @@ int moe_ep_forward(moe_ep_t ep, const void* x, const int32_t* group_sizes, float
   a.slices = ep->slices;
   a.wave_rows = ep->wave_rows;
   a.local_gs = ep->local_gs;
+  a.recv = ep->recv;
+  a.off_yl = ep->off_yl;
   a.routed = ep->routed;
   a.push_ctr = ep->push_ctr;
   a.abort_word = ep->abort_word;
@@ -968,6 +988,34 @@ int moe_ep_forward(moe_ep_t ep, const void* x, const int32_t* group_sizes, float
   RunOpts opt;
   opt.ctas = ep->mlp_ctas;
   opt.skip_tail = true;
+  if (ep->scatter) {
+    // One wave: land every row, run both GEMMs on every SM with the down
+    // GEMM storing each Y row straight into its source's landing area, tell
+    // the sources, and finish this rank's Y once every owner has told it.
+    EpScatter sc;
+    memset(&sc, 0, sizeof(sc));
+    for (int s2 = 0; s2 < ep->world; ++s2) sc.base[s2] = ep->peer[s2];
+    sc.off = ep->off_yl;
+    sc.recv = ep->recv;
+    sc.world = ep->world;
+    sc.on = 1;
+    opt.scatter = &sc;
+    MOE_CUDA_TRY(cudaStreamWaitEvent(st, ep->ev_push[0], 0));
+    ep_wait_kernel<<<1, 32, 0, st>>>(a, 0);
+    MOE_CUDA_TRY(cudaGetLastError());
+    float* yl = reinterpret_cast<float*>(ep->buf + ep->off_yl);
+    if (int r = run_large(ep->buf + ep->off_x, ep->w_up, ep->w_down, ep->local_gs, ep->w_up_scale, ep->w_down_scale,
+                          yl, ep->region_cap, ep->D, ep->F, ep->el, ep->dtype, ep->ws, ep->ws_bytes, st, opt))
+      return r;
+    ep_ydone_kernel<<<1, 32, 0, st>>>(a);
+    MOE_CUDA_TRY(cudaGetLastError());
+    int dev;
+    DevInfo* di;
+    if (int r = device_info(&dev, &di)) return r;
+    ep_finish_kernel<<<di->sms, 1024, 0, st>>>(a);
+    MOE_CUDA_TRY(cudaGetLastError());
+    return 0;
+  }
   for (int v = 0; v < ep->waves; ++v) {
     MOE_CUDA_TRY(cudaStreamWaitEvent(st, ep->ev_push[v], 0));
     ep_wait_kernel<<<1, 32, 0, st>>>(a, v);
@@ -995,7 +1043,13 @@ int moe_ep_forward(moe_ep_t ep, const void* x, const int32_t* group_sizes, float
 
 int moe_ep_launches_per_forward(moe_ep_t ep) {
   if (!ep) return fail(MOE_ERR_INVALID_ARG, "null engine");
+  if (ep->scatter) return 3 + ep_mlp_launches(ep) + 2;  // counts, push, wait, GEMMs, ydone, finish
   return 1 + ep->waves * (3 + ep_mlp_launches(ep));
+}
+
+void* moe_ep_output(moe_ep_t ep) {
+  if (!ep || !ep->scatter) return nullptr;
+  return ep->buf + ep->off_yl;
 }
 
 int moe_ep_destroy(moe_ep_t ep) {

@@ -75,6 +75,8 @@ def lib() -> ctypes.CDLL:
     L.moe_ep_forward.restype = ctypes.c_int
     L.moe_ep_launches_per_forward.argtypes = [vp]
     L.moe_ep_launches_per_forward.restype = ctypes.c_int
+    L.moe_ep_output.argtypes = [vp]
+    L.moe_ep_output.restype = vp
     L.moe_ep_destroy.argtypes = [vp]
     L.moe_ep_destroy.restype = ctypes.c_int
     _lib = L

@@ -267,6 +267,15 @@ class PeerExpertParallelMLP:
         if world > 1:
             dist.barrier(group=group)
         self.launches_per_forward = L.moe_ep_launches_per_forward(self._ep)
+        # D > 256 engines store Y rows straight into their own buffer; without
+        # `out` the result is a view of it (valid until the next call).
+        self._own_y = L.moe_ep_output(self._ep)
+
+    def _own_view(self, M: int) -> torch.Tensor:
+        iface = {"shape": (M, self.d), "typestr": "<f4", "version": 3,
+                 "data": (int(self._own_y), False), "strides": None}
+        view = type("_EngineY", (), {"__cuda_array_interface__": iface})()
+        return torch.as_tensor(view, device=self.device)
 
     def __call__(self, x: torch.Tensor, group_sizes, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         if self._ep is None:
@@ -278,10 +287,13 @@ class PeerExpertParallelMLP:
         gs = torch.as_tensor(group_sizes).to(device=self.device, dtype=torch.int32, non_blocking=True).contiguous()
         if gs.numel() != self.num_experts:
             raise ValueError(f"group_sizes has {gs.numel()} entries, expected {self.num_experts}")
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        if out is None and self._own_y and M > 0:
+            self._check(self._L.moe_ep_forward(self._ep, x.data_ptr(), gs.data_ptr(), None, M, stream))
+            return self._own_view(M)
         y = out if out is not None else torch.empty((M, self.d), dtype=torch.float32, device=self.device)
         if y.shape != (M, self.d) or y.dtype != torch.float32 or not y.is_contiguous():
             raise ValueError("out must be a contiguous (M, D) float32 tensor")
-        stream = torch.cuda.current_stream(self.device).cuda_stream
         self._check(self._L.moe_ep_forward(self._ep, x.data_ptr(), gs.data_ptr(), y.data_ptr(), M, stream))
         return y
 
