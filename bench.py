@@ -306,7 +306,7 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
         "data": "synthetic (seeded; BASELINE config shapes, N(0,1)/N(0,1/D)/N(0,1/F) init)",
         "config": {"workload": cfg.name, "M_per_gpu": cfg.M, "D": cfg.D, "F": cfg.F, "E": cfg.E,
                    "routing": cfg.routing, "parallelism": f"ep{world}" if world > 1 else "single",
-                   **({"waves": args.waves, "exchange_sms": args.reserve_sms, "transport": args.transport}
+                   **({"waves": getattr(layer, "waves", args.waves), "transport": args.transport}
                       if world > 1 else {}),
                    "l2": "flushed before every step (256 MiB write)"},
         "useful_tflops": alg["flops"] * world / (ms_per_step / 1e3) / 1e12,

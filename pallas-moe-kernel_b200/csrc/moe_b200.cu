@@ -980,8 +980,16 @@ int moe_ep_forward(moe_ep_t ep, const void* x, const int32_t* group_sizes, float
   MOE_CUDA_TRY(cudaStreamWaitEvent(ep->comm, ep->ev_start, 0));
   ep_counts_kernel<<<1, 1024, ep_counts_smem(ep->world, ep->E, ep->waves), ep->comm>>>(a);
   MOE_CUDA_TRY(cudaGetLastError());
+  // In scatter mode the push runs before the experts, alone: it gets every SM.
+  int push_ctas = ep->comm_ctas;
+  if (ep->scatter) {
+    int dev;
+    DevInfo* di;
+    if (int r = device_info(&dev, &di)) return r;
+    push_ctas = di->sms;
+  }
   for (int v = 0; v < ep->waves; ++v) {
-    ep_push_kernel<<<ep->comm_ctas, 1024, 0, ep->comm>>>(a, v);
+    ep_push_kernel<<<push_ctas, 1024, 0, ep->comm>>>(a, v);
     MOE_CUDA_TRY(cudaGetLastError());
     MOE_CUDA_TRY(cudaEventRecord(ep->ev_push[v], ep->comm));
   }

@@ -270,6 +270,7 @@ class PeerExpertParallelMLP:
         # D > 256 engines store Y rows straight into their own buffer; without
         # `out` the result is a view of it (valid until the next call).
         self._own_y = L.moe_ep_output(self._ep)
+        self.waves = 1 if self._own_y else int(waves)   # two-GEMM engines run one wave
 
     def _own_view(self, M: int) -> torch.Tensor:
         iface = {"shape": (M, self.d), "typestr": "<f4", "version": 3,
