@@ -186,6 +186,42 @@ int moe_ep_launches_per_forward(moe_ep_t ep);
 void* moe_ep_output(moe_ep_t ep);
 int moe_ep_destroy(moe_ep_t ep);
 
+/*
+ * Routing and permutation around the fused expert MLP.  No counterpart in the
+ * reference, whose path starts from rows already sorted by expert (its
+ * benchmarks build group_sizes directly, README.md:13); these produce that
+ * input from router logits and fold the expert outputs back per token, so a
+ * whole MoE layer runs as
+ *     route_topk -> permute -> gather_rows -> moe_fused_mlp -> combine_rows.
+ * Pointers are device pointers; calls are stream-ordered and allocate nothing.
+ *
+ * moe_route_topk   logits (T, E) f32 -> topk_ids (T, k) int32 (larger logit
+ *                  first; ties to the lower expert id) and topk_weights
+ *                  (T, k) f32 = softmax over the selected logits (the full
+ *                  softmax renormalised to the top k).  E <= 1024, k <= 16.
+ *                  A slot without a finite winner gets id -1, weight 0.
+ * moe_permute      expert_ids (N = T * k entries, entry i = t * k + j) ->
+ *                  group_sizes (E,), sorted_src (N,) = entry index of each
+ *                  row in expert order (stable: entries of one expert keep
+ *                  their order), inverse (N,) = row of each entry (-1 for an
+ *                  id outside [0, E): dropped, status bit 16).  Needs
+ *                  moe_permute_workspace_size(N, E) bytes of workspace.
+ *                  Rows past sum(group_sizes) of sorted_src are untouched.
+ * moe_gather_rows  out[r] = x[sorted_src[r] / k] for rows of row_bytes (a
+ *                  multiple of 16) -- X in expert order for moe_fused_mlp.
+ * moe_combine_rows y[t] = sum_j topk_weights[t, j] * y_sorted[inverse[t*k+j]]
+ *                  (f32, D a multiple of 4, slots summed in order).
+ */
+int moe_route_topk(const float* logits, int64_t T, int32_t E, int32_t k, int32_t* topk_ids, float* topk_weights,
+                   void* stream);
+size_t moe_permute_workspace_size(int64_t N, int32_t E);
+int moe_permute(const int32_t* expert_ids, int64_t N, int32_t E, int32_t* group_sizes, int32_t* sorted_src,
+                int32_t* inverse, void* workspace, size_t workspace_bytes, void* stream);
+int moe_gather_rows(const void* x, const int32_t* sorted_src, int64_t rows, int32_t k, int32_t row_bytes, void* out,
+                    void* stream);
+int moe_combine_rows(const float* y_sorted, const int32_t* inverse, const float* topk_weights, int64_t T, int32_t k,
+                     int32_t D, float* y, void* stream);
+
 /* Text of the calling thread's last error ("" when none). */
 const char* moe_last_error(void);
 
@@ -193,7 +229,8 @@ const char* moe_last_error(void);
  * Reads the device status word of the current device (bits: 1 = a pipeline
  * wait timed out, 2 = a negative group size was clamped, 4 = an
  * expert-parallel wait for a peer timed out, 8 = group sizes were cut to fit
- * M or a landing region).  Synchronises the device.  When `reset` is
+ * M or a landing region, 16 = an expert id outside [0, E) was dropped by
+ * moe_permute).  Synchronises the device.  When `reset` is
  * non-zero the word is cleared afterwards.
  * Returns the bits (>= 0) or MOE_ERR_CUDA.
  */

@@ -24,9 +24,9 @@ Parity status
       rows at or past ``sum(group_sizes)`` produce zeros;
     - ``jax.nn.gelu(x, approximate=True)`` =
       ``0.5 * x * (1 + tanh(sqrt(2/pi) * (x + 0.044715 * x**3)))``.
-* The kernel's block/mask control flow is pinned separately by executing
-  the reference's own Pallas kernel source under a numpy stand-in for
-  Pallas (``oracle/pallas_shim.py``, fixtures in ``tests/golden``).
+* The kernel's block/mask control flow (``src/kernel.py:9-82``) is restated
+  in ``fused_kernel_blocks`` and checked against ``ref_ragged_mlp`` (tests);
+  it is not executed from the reference's source.
 * The host-side group-size generators are pinned against the reference's
   own functions executed here and against the group sizes recorded in the
   reference's ``results/structured_float32/results.csv``.
@@ -203,4 +203,56 @@ def time_cpu_reference(x: np.ndarray, w_up, w_down, group_sizes: Sequence[int]) 
         h = x[a:b].astype(np.float32, copy=False) @ w_up[e].astype(np.float32, copy=False)
         h = gelu_tanh(h)
         y[a:b] = h @ w_down[e].astype(np.float32, copy=False)
+    return y
+
+
+# ----------------------------------------------------------------------------- routing and permutation
+# The reference has no router: its benchmarks build `group_sizes` directly
+# and feed rows already sorted by expert (README.md:13).  These restate the
+# steps on either side of its path that the library's routing kernels
+# perform, with numpy's stable sort as the definition of the order.
+
+def route_topk(logits: np.ndarray, k: int):
+    """Top-k experts per token (larger logit first, ties to the lower expert
+    id) and their weights: the softmax over all experts renormalised to the
+    selected ones, which equals the softmax over the selected logits.
+    Returns (ids (T, k) int32, weights (T, k) float64)."""
+    lg = np.asarray(logits, dtype=np.float64)
+    order = np.argsort(-lg, axis=1, kind="stable")[:, :k]
+    sel = np.take_along_axis(lg, order, axis=1)
+    w = np.exp(sel - sel[:, :1])
+    w /= w.sum(axis=1, keepdims=True)
+    return order.astype(np.int32), w
+
+
+def permute_by_expert(ids: np.ndarray, num_experts: int):
+    """Stable counting sort of the (token, slot) entries i = t * k + j by
+    expert.  Returns (group_sizes (E,), sorted_src (N,) with the entry index
+    of each sorted row, inverse (N,) with the sorted row of each entry or -1
+    for an id outside [0, E))."""
+    flat = np.asarray(ids, dtype=np.int64).reshape(-1)
+    valid = (flat >= 0) & (flat < num_experts)
+    idx = np.nonzero(valid)[0]
+    order = idx[np.argsort(flat[idx], kind="stable")]
+    group_sizes = np.bincount(flat[idx], minlength=num_experts).astype(np.int32)
+    inverse = np.full(flat.shape, -1, dtype=np.int64)
+    inverse[order] = np.arange(order.size)
+    return group_sizes, order.astype(np.int32), inverse.astype(np.int32)
+
+
+def gather_rows(x: np.ndarray, sorted_src: np.ndarray, k: int) -> np.ndarray:
+    """Row r of the result is row sorted_src[r] // k of x."""
+    return np.asarray(x)[np.asarray(sorted_src, dtype=np.int64) // k]
+
+
+def combine_rows(y_sorted: np.ndarray, inverse: np.ndarray, weights: np.ndarray, k: int) -> np.ndarray:
+    """y[t] = sum_j weights[t, j] * y_sorted[inverse[t * k + j]] (slots with
+    inverse -1 contribute nothing), in float64."""
+    inv = np.asarray(inverse, dtype=np.int64).reshape(-1, k)
+    w = np.asarray(weights, dtype=np.float64).reshape(-1, k)
+    ys = np.asarray(y_sorted, dtype=np.float64)
+    y = np.zeros((inv.shape[0], ys.shape[1]))
+    for j in range(k):
+        ok = inv[:, j] >= 0
+        y[ok] += w[ok, j:j + 1] * ys[inv[ok, j]]
     return y

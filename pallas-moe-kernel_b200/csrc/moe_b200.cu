@@ -11,6 +11,7 @@
 
 #include "../../include/moe_b200.h"
 #include "ep_exchange.cuh"
+#include "router.cuh"
 #include "fused_pair.cuh"
 #include "grouped_gemm.cuh"
 
@@ -1063,6 +1064,112 @@ void* moe_ep_output(moe_ep_t ep) {
 int moe_ep_destroy(moe_ep_t ep) {
   t_err[0] = 0;
   ep_release(ep);
+  return 0;
+}
+
+// ------------------------------------------------------------------ routing and permutation
+int moe_route_topk(const float* logits, int64_t T, int32_t E, int32_t k, int32_t* topk_ids, float* topk_weights,
+                   void* stream) {
+  t_err[0] = 0;
+  if (T < 0 || E < 1 || E > kRouteMaxExperts || k < 1 || k > kRouteMaxK || k > E)
+    return fail(MOE_ERR_INVALID_ARG, "T=%lld E=%d k=%d (1 <= k <= min(%d, E), E <= %d)", (long long)T, E, k,
+                kRouteMaxK, kRouteMaxExperts);
+  if (T == 0) return 0;
+  if (!logits || !topk_ids || !topk_weights) return fail(MOE_ERR_INVALID_ARG, "null pointer");
+  int dev;
+  DevInfo* di;
+  if (int r = device_info(&dev, &di)) return r;
+  const int blocks = (int)std::min<int64_t>((T + 7) / 8, (int64_t)di->sms * 8);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int pl = (E + 31) / 32;
+  if (pl <= 1) launch_topk<1>(logits, T, E, k, topk_ids, topk_weights, blocks, st);
+  else if (pl <= 2) launch_topk<2>(logits, T, E, k, topk_ids, topk_weights, blocks, st);
+  else if (pl <= 4) launch_topk<4>(logits, T, E, k, topk_ids, topk_weights, blocks, st);
+  else if (pl <= 8) launch_topk<8>(logits, T, E, k, topk_ids, topk_weights, blocks, st);
+  else if (pl <= 16) launch_topk<16>(logits, T, E, k, topk_ids, topk_weights, blocks, st);
+  else launch_topk<32>(logits, T, E, k, topk_ids, topk_weights, blocks, st);
+  MOE_CUDA_TRY(cudaGetLastError());
+  return 0;
+}
+
+size_t moe_permute_workspace_size(int64_t N, int32_t E) {
+  if (N < 0 || E < 1) return 0;
+  return align256((size_t)((N + kPermBlock - 1) / kPermBlock) * (size_t)E * sizeof(int32_t));
+}
+
+int moe_permute(const int32_t* expert_ids, int64_t N, int32_t E, int32_t* group_sizes, int32_t* sorted_src,
+                int32_t* inverse, void* workspace, size_t workspace_bytes, void* stream) {
+  t_err[0] = 0;
+  if (N < 0 || N > 0x7fffffff || E < 1 || E > kRouteMaxExperts)
+    return fail(MOE_ERR_INVALID_ARG, "N=%lld E=%d (N < 2^31, 1 <= E <= %d)", (long long)N, E, kRouteMaxExperts);
+  if (!group_sizes) return fail(MOE_ERR_INVALID_ARG, "null group_sizes");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (N == 0) {
+    MOE_CUDA_TRY(cudaMemsetAsync(group_sizes, 0, (size_t)E * sizeof(int32_t), st));
+    return 0;
+  }
+  if (!expert_ids || !sorted_src || !inverse) return fail(MOE_ERR_INVALID_ARG, "null pointer");
+  const size_t need = moe_permute_workspace_size(N, E);
+  if (workspace_bytes < need || !workspace)
+    return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", workspace_bytes, need);
+  int* status = nullptr;
+  MOE_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_status));
+  static bool attr_done[64] = {};
+  int dev;
+  DevInfo* di;
+  if (int r = device_info(&dev, &di)) return r;
+  const size_t smem_scatter = (size_t)(kPermBlock / 32) * E * sizeof(int);
+  if (!attr_done[dev]) {
+    MOE_CUDA_TRY(cudaFuncSetAttribute(perm_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)((kPermBlock / 32) * kRouteMaxExperts * sizeof(int))));
+    attr_done[dev] = true;
+  }
+  const int64_t nb = (N + kPermBlock - 1) / kPermBlock;
+  int32_t* hist = static_cast<int32_t*>(workspace);
+  perm_hist_kernel<<<(unsigned)nb, kPermBlock, E * sizeof(int), st>>>(expert_ids, N, E, hist, status);
+  MOE_CUDA_TRY(cudaGetLastError());
+  perm_scan_kernel<<<1, 1024, 0, st>>>(hist, nb, E, group_sizes);
+  MOE_CUDA_TRY(cudaGetLastError());
+  perm_scatter_kernel<<<(unsigned)nb, kPermBlock, smem_scatter, st>>>(expert_ids, N, E, hist, sorted_src, inverse);
+  MOE_CUDA_TRY(cudaGetLastError());
+  return 0;
+}
+
+int moe_gather_rows(const void* x, const int32_t* sorted_src, int64_t rows, int32_t k, int32_t row_bytes, void* out,
+                    void* stream) {
+  t_err[0] = 0;
+  if (rows < 0 || k < 1 || row_bytes <= 0 || (row_bytes & 15))
+    return fail(MOE_ERR_INVALID_ARG, "rows=%lld k=%d row_bytes=%d (a positive multiple of 16)", (long long)rows, k,
+                row_bytes);
+  if (rows == 0) return 0;
+  if (!x || !sorted_src || !out) return fail(MOE_ERR_INVALID_ARG, "null pointer");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15u)
+    return fail(MOE_ERR_MISALIGNED, "x and out must be 16-byte aligned");
+  int dev;
+  DevInfo* di;
+  if (int r = device_info(&dev, &di)) return r;
+  const int blocks = (int)std::min<int64_t>((rows + 15) / 16, (int64_t)di->sms * 4);
+  gather_rows_kernel<<<blocks, 512, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(x), sorted_src, rows, k, row_bytes, static_cast<uint8_t*>(out));
+  MOE_CUDA_TRY(cudaGetLastError());
+  return 0;
+}
+
+int moe_combine_rows(const float* y_sorted, const int32_t* inverse, const float* weights, int64_t T, int32_t k,
+                     int32_t D, float* y, void* stream) {
+  t_err[0] = 0;
+  if (T < 0 || k < 1 || D <= 0 || (D & 3))
+    return fail(MOE_ERR_INVALID_ARG, "T=%lld k=%d D=%d (D a positive multiple of 4)", (long long)T, k, D);
+  if (T == 0) return 0;
+  if (!y_sorted || !inverse || !weights || !y) return fail(MOE_ERR_INVALID_ARG, "null pointer");
+  if ((reinterpret_cast<uintptr_t>(y_sorted) | reinterpret_cast<uintptr_t>(y)) & 15u)
+    return fail(MOE_ERR_MISALIGNED, "y_sorted and y must be 16-byte aligned");
+  int dev;
+  DevInfo* di;
+  if (int r = device_info(&dev, &di)) return r;
+  const int blocks = (int)std::min<int64_t>((T + 15) / 16, (int64_t)di->sms * 4);
+  combine_rows_kernel<<<blocks, 512, 0, static_cast<cudaStream_t>(stream)>>>(y_sorted, inverse, weights, T, k, D, y);
+  MOE_CUDA_TRY(cudaGetLastError());
   return 0;
 }
 

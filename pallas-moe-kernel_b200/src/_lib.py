@@ -77,6 +77,16 @@ def lib() -> ctypes.CDLL:
     L.moe_ep_launches_per_forward.restype = ctypes.c_int
     L.moe_ep_output.argtypes = [vp]
     L.moe_ep_output.restype = vp
+    L.moe_route_topk.argtypes = [vp, i64, i32, i32, vp, vp, vp]
+    L.moe_route_topk.restype = ctypes.c_int
+    L.moe_permute_workspace_size.argtypes = [i64, i32]
+    L.moe_permute_workspace_size.restype = sz
+    L.moe_permute.argtypes = [vp, i64, i32, vp, vp, vp, vp, sz, vp]
+    L.moe_permute.restype = ctypes.c_int
+    L.moe_gather_rows.argtypes = [vp, vp, i64, i32, i32, vp, vp]
+    L.moe_gather_rows.restype = ctypes.c_int
+    L.moe_combine_rows.argtypes = [vp, vp, vp, i64, i32, i32, vp, vp]
+    L.moe_combine_rows.restype = ctypes.c_int
     L.moe_ep_destroy.argtypes = [vp]
     L.moe_ep_destroy.restype = ctypes.c_int
     _lib = L
