@@ -343,6 +343,117 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
     return line
 
 
+
+# --------------------------------------------------------------------- whole MoE layer (routing stage)
+def run_layer(args, cfg, device) -> dict:
+    """Routing stage around the expert MLP on one GPU: top-k routing of
+    ``tokens`` router inputs over E experts, stable permutation by expert, row
+    gather, and the weighted combine (HBM-bound kernels, timed alone), plus
+    the whole layer (routing + the fused expert MLP)."""
+    import torch
+    from src import router
+    from src.kernel import PreparedExperts
+
+    k = {"top2": 2, "top8_softmax": 8}.get(cfg.routing)
+    if not k:
+        raise SystemExit("--stage layer needs a top-k configuration (c4 or c5)")
+    T = cfg.M // k
+    g = torch.Generator(device=device)
+    g.manual_seed(7)
+    tdt = torch.float32 if cfg.dtype == "f32" else torch.bfloat16
+    x = torch.randn((T, cfg.D), generator=g, device=device).to(tdt)
+    logits = torch.randn((T, cfg.E), generator=g, device=device)
+    ys = torch.randn((T * k, cfg.D), generator=g, device=device)
+    _, w_up, w_down, _, scales = make_workload(cfg, device)
+    sc = {} if scales is None else {"w_up_scale": scales[0], "w_down_scale": scales[1]}
+    experts = PreparedExperts(w_up, w_down, max_tokens=T * k, **sc)
+    ws = torch.empty(1 << 20, dtype=torch.uint8, device=device)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    st = torch.cuda.current_stream(device)
+
+    def routing():
+        ids, w = router.route_topk(logits, k)
+        gs, src, inv = router.permute(ids, cfg.E, workspace=ws)
+        xs = router.gather_rows(x, src, k)
+        return router.combine_rows(ys, inv, w), xs, gs
+
+    def layer():
+        ids, w = router.route_topk(logits, k)
+        gs, src, inv = router.permute(ids, cfg.E, workspace=ws)
+        xs = router.gather_rows(x, src, k)
+        return router.combine_rows(experts(xs, gs), inv, w)
+
+    def timed(fn, n):
+        out = []
+        for _ in range(n):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            fn()
+            b.record(st)
+            torch.cuda.synchronize(device)
+            out.append(a.elapsed_time(b))
+        return statistics.median(out)
+
+    for _ in range(args.warmup):
+        routing()
+        layer()
+    torch.cuda.synchronize(device)
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    time.sleep(0.05)
+    t0 = time.perf_counter()
+    r_ms = timed(routing, args.steps)
+    l_ms = timed(layer, args.steps)
+    t1 = time.perf_counter()
+    clocks.stop()
+    if _lib_status():
+        raise RuntimeError("device status set after the layer stage")
+    peaks, peak_src = load_peaks()
+    N = T * k
+    sx = x.element_size()
+    # logits in, ids + weights out; ids read by 2 permutation passes, src + inverse out;
+    # X read once and written in expert order; expert outputs read and per-token Y written.
+    alg = (T * cfg.E * 4 + 2 * N * 4) + (2 * N * 4 + 2 * N * 4) + (T * cfg.D * sx + N * cfg.D * sx) \
+        + (N * cfg.D * 4 + T * cfg.D * 4)
+    hbm = float(peaks["hbm_gbs"])
+    achieved = alg / (r_ms / 1e3) / 1e9
+    # CPU baseline: the oracle's numpy routing + permutation + gather + combine on a sample.
+    from oracle import moe_oracle as orc
+    ns = min(T, 512)
+    lg, xh, ysh = logits[:ns].cpu().numpy(), x[:ns].float().cpu().numpy(), ys[:ns * k].cpu().numpy()
+    c0 = time.perf_counter()
+    reps = 0
+    while True:
+        ids_h, w_h = orc.route_topk(lg, k)
+        gs_h, src_h, inv_h = orc.permute_by_expert(ids_h, cfg.E)
+        orc.gather_rows(xh, src_h, k)
+        orc.combine_rows(ysh, inv_h, w_h, k)
+        reps += 1
+        if time.perf_counter() - c0 > 5.0:
+            break
+    cpu_tps = reps * ns / (time.perf_counter() - c0)
+    return {
+        "metric": "moe_layer_tokens_per_s", "value": T / (l_ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": l_ms, "higher_is_better": True,
+        "dtype": str(tdt).replace("torch.", ""), "data": "synthetic (seeded N(0,1) tokens and router logits)",
+        "config": {"workload": f"{cfg.name}_layer", "tokens": T, "k": k, "E": cfg.E, "D": cfg.D, "F": cfg.F,
+                   "l2": "flushed before every step (256 MiB write)"},
+        "routing": {"ms": r_ms, "tokens_per_s": T / (r_ms / 1e3), "kernels": 6,
+                    "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                                 "frac": achieved / hbm, "algorithmic_bytes": alg,
+                                 "peak_source": f"{peak_src}: hbm_gbs"}},
+        "expert_mlp_ms": l_ms - r_ms,
+        "clocks": clocks.summary(t0, t1),
+        "cpu_baseline": {"value": cpu_tps, "unit": "tokens/s", "cores": 1, "kind": "port",
+                         "sample": f"oracle routing + permutation + gather + combine of {ns} tokens, repeated 5 s"},
+    }
+
+
+def _lib_status() -> int:
+    from src import _lib
+    return _lib.device_status(reset=True)
+
 # --------------------------------------------------------------------- CPU baseline
 def cpu_reference(cfg, budget_s: float, seed: int = 0) -> dict:
     """The reference's unfused path (two ragged dots with tanh-GELU, f32) on
@@ -413,6 +524,9 @@ def main() -> int:
     ap.add_argument("--config", default="c4",
                     help="c1..c5 (default c4: bf16 Mixtral-shaped M=32768 D=4096 F=14336 E=8, top-2)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--stage", default="mlp", choices=["mlp", "layer"],
+                    help="mlp: the expert MLP (the reference's path); layer: routing + permutation + expert MLP "
+                         "+ combine of a whole MoE layer on one GPU (top-k configurations)")
     ap.add_argument("--ref-budget", type=float, default=10.0, help="seconds of CPU baseline timing")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tokens", type=int, default=0, help="override M (routed rows per GPU)")
@@ -460,6 +574,9 @@ def main() -> int:
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    if args.stage == "layer":
+        print(json.dumps(run_layer(args, cfg, device)), flush=True)
+        return 0
     try:
         line = run_ours(args, cfg, rank, world, device)
         if line is not None:
