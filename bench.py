@@ -213,7 +213,7 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
 
         def kern_fn():  # the dominant kernel alone (weights already prepared)
             return experts(x, gs_dev, out=y)
-        launches_per_step = (3 if cfg.dtype == "f32" else 1) if cfg.D <= 256 else 2
+        launches_per_step = (3 if cfg.dtype == "f32" else 1) if cfg.D <= 256 else (3 if cfg.dtype == "fp8" else 2)
 
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)

@@ -1,7 +1,7 @@
 // Persistent grouped GEMM over ragged expert row blocks on CTA pairs
 // (2-SM tcgen05 MMA), sm_100a.  The large-D expert MLP runs as two launches:
 //
-//   up   : H[rows of e, :] = GELU_tanh(X[rows of e, :] @ W_up[e])   (bf16 H)
+//   up   : H[rows of e, :] = GELU_tanh(X[rows of e, :] @ W_up[e])   (bf16 H; f16 with e4m3 weights)
 //   down : Y[rows of e, :] = H[rows of e, :] @ W_down[e]            (f32 Y)
 //
 // A (X or H, row-major, K-major) tiles of 128 rows come from each CTA of the
@@ -21,7 +21,8 @@
 // issuer (leader), warps 2..5 epilogue (one TMEM lane quadrant each; both
 // CTAs), and for e4m3 weights warp 10 streams raw B tiles into a deep ring
 // of their own while warps 6..9 dequantise each raw B tile
-// (e4m3 x 128x128 block scale -> bf16) into the MMA's operand layout.
+// (e4m3 x 128x128 block scale -> f16; X and H are f16 too) into the MMA's
+// operand layout.
 #pragma once
 #include "fused_small.cuh"
 
@@ -42,7 +43,7 @@ struct EpScatter {
 
 struct GemmParams {
   const int32_t* group_sizes;
-  void* out;          // H (bf16, [M, N]) or Y (f32, [M, N])
+  void* out;          // H (bf16 or, for e4m3 weights, f16; [M, N]) or Y (f32, [M, N])
   int M;              // rows of A / out
   int E;
   int N;              // output columns (F for up, D for down)
@@ -58,10 +59,12 @@ struct GemmParams {
 // store_y_block with one destination row pointer per row: lane l of the warp
 // holds the pointer of row l of the 32-row block (null = not stored).
 __device__ __forceinline__ void store_y_rows(uint32_t taddr, float4* stage, uint8_t* row_ptr, int col0,
-                                             uint32_t lane) {
+                                             uint32_t lane, float mul) {
   uint32_t v[32];
   tmem_ld32(taddr, v);
   tmem_ld_wait();
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * mul);
 #pragma unroll
   for (int k = 0; k < 8; ++k)
     stage[lane * 8 + (k ^ (lane & 7))] = make_float4(__uint_as_float(v[4 * k]), __uint_as_float(v[4 * k + 1]),
@@ -79,24 +82,25 @@ __device__ __forceinline__ void store_y_rows(uint32_t taddr, float4* stage, uint
   __syncwarp();
 }
 
-template <int EPI, bool BFP8>  // EPI 0: GELU -> bf16 H, 1: f32 Y; BFP8: e4m3 B dequantised in smem
+template <int EPI, bool BFP8>  // EPI 0: GELU -> H, 1: f32 Y; BFP8: e4m3 B dequantised in smem, f16 operands
 struct GemmCfg {
   static constexpr int BM = 128;   // rows per CTA (256 per pair)
   static constexpr int BN = 256;   // output columns per tile (128 per CTA of B)
-  static constexpr int BK = 64;    // bf16 elements = one 128-byte swizzle row
+  static constexpr int BK = 64;    // 16-bit elements = one 128-byte swizzle row
   static constexpr int A_BYTES = BM * BK * 2;          // 16 KB
-  static constexpr int B_BYTES = (BN / 2) * BK * 2;    // 16 KB (two 64-column atoms, bf16)
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;    // 16 KB (two 64-column atoms, 16-bit)
   static constexpr int B8_BYTES = BFP8 ? (BN / 2) * BK : 0;  // 8 KB raw e4m3 tile
-  static constexpr int STAGE = A_BYTES + B_BYTES;      // operand stage (A + bf16 B)
+  static constexpr int STAGE = A_BYTES + B_BYTES;      // operand stage (A + 16-bit B)
   static constexpr int NS = BFP8 ? 4 : 6;              // operand stages
   static constexpr int NR = BFP8 ? 10 : 0;             // raw e4m3 stages (HBM stream runs ahead)
   static constexpr int EPI_WARPS = 4;
-  static constexpr int CVT_WARPS = BFP8 ? 4 : 0;
+  static constexpr int CVT_WARPS = BFP8 ? 8 : 0;  // two per SM sub-partition
   static constexpr int OUT_STAGE = EPI_WARPS * 32 * 128;  // 4 KB per warp: 32 rows x 128 B
   static constexpr int BAR_BYTES = BFP8 ? 512 : 256;
   static constexpr int SMEM = 1024 + NS * STAGE + NR * B8_BYTES + OUT_STAGE + BAR_BYTES;
   static constexpr int TMEM_COLS = 512;                 // 2 accumulators x 256 columns
-  static constexpr uint32_t IDESC = make_idesc(kFmtBF16, 256, BN, 0, 1);
+  // e4m3 weights run as f16 operands (f16 X, f16 H, f16 dequantised B).
+  static constexpr uint32_t IDESC = make_idesc(BFP8 ? kFmtF16 : kFmtBF16, 256, BN, 0, 1);
   static constexpr uint32_t TX = 2 * (A_BYTES + B_BYTES);  // both CTAs (bf16 B)
   static constexpr uint32_t TX_A = 2 * A_BYTES;            // both CTAs' A (FP8 B arrives converted)
   static constexpr int RAW_WARP = 2 + EPI_WARPS + CVT_WARPS;  // FP8: producer of the raw ring
@@ -105,29 +109,46 @@ struct GemmCfg {
   // was scheduled under it), or of the FP8 block with its extra warps.
   static constexpr int LAUNCH_BOUND = THREADS > 320 ? THREADS : 320;
   static_assert(SMEM <= kMaxSmemPerBlock, "shared memory budget");
+  static_assert(NS % 2 == 0 && NR % 2 == 0, "alternating converter groups keep fixed stage parities");
 };
 
 struct GemmMaps {
-  CUtensorMap a;  // X or H: [M, K] bf16, box {64, 128}
+  CUtensorMap a;  // X or H: [M, K] bf16 (f16 with e4m3 weights), box {64, 128}
   CUtensorMap b;  // W_up / W_down as [E*K, N]: bf16 box {64, 64}, or e4m3 bytes box {128, 64}
 };
 
-// Four e4m3 values (one 32-bit word, lowest byte first) -> f32 x scale ->
-// four bf16 (two bf16x2 words).  e4m3 values are exact in f16, so the only
-// rounding is the final one to bf16 of the dequantised weight.
-__device__ __forceinline__ uint2 e4m3x4_to_bf16x4(uint32_t v, float s) {
+// Four e4m3 values (one 32-bit word, lowest byte first) -> four f16 (two
+// f16x2 words) times the block scale s2 (an f16x2 pair).  e4m3 values are
+// exact in f16, so the multiply's rounding is the only one; decode and
+// multiply are one instruction per pair each.
+__device__ __forceinline__ uint2 e4m3x4_to_f16x4(uint32_t v, uint32_t s2) {
   uint32_t h01, h23;
   asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
       "cvt.rn.f16x2.e4m3x2 %0, lo;\n\tcvt.rn.f16x2.e4m3x2 %1, hi;\n\t}"
       : "=r"(h01), "=r"(h23)
       : "r"(v));
-  float f0, f1, f2, f3;
-  asm("{\n\t.reg .b16 a, b, c, d;\n\tmov.b32 {a, b}, %4;\n\tmov.b32 {c, d}, %5;\n\t"
-      "cvt.f32.f16 %0, a;\n\tcvt.f32.f16 %1, b;\n\tcvt.f32.f16 %2, c;\n\tcvt.f32.f16 %3, d;\n\t}"
-      : "=f"(f0), "=f"(f1), "=f"(f2), "=f"(f3)
-      : "r"(h01), "r"(h23));
-  return make_uint2(pack_bf16x2(f0 * s, f1 * s), pack_bf16x2(f2 * s, f3 * s));
+  asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(h01) : "r"(s2));
+  asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(h23) : "r"(s2));
+  return make_uint2(h01, h23);
 }
+
+// Power-of-two exponent k of an FP8 tile: 2^k brings the largest block scale
+// of the tile's two 128-column blocks (over all of K) into [1, 2), so that the
+// scaled block scales are normal f16 values.  The converters multiply the
+// weights by scale * 2^k; the epilogue multiplies the accumulator by 2^-k
+// (exact).  Every lane of the calling warp returns the same k, in [-100, 100].
+__device__ __forceinline__ int fp8_tile_shift(const float* b_scale, int K, int N, int e, int nb, uint32_t lane) {
+  const int nkb = K / 128, nnb = N / 128;
+  const float* sc = b_scale + (size_t)e * nkb * nnb + (size_t)nb * 2;
+  float m = 0.f;
+  for (int i = (int)lane; i < 2 * nkb; i += 32) m = fmaxf(m, __ldg(sc + (size_t)(i >> 1) * nnb + (i & 1)));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const int ex = (int)((__float_as_uint(m) >> 23) & 0xFFu);
+  const int k = 127 - ex;
+  return k < -100 ? -100 : (k > 100 ? 100 : k);
+}
+__device__ __forceinline__ float exp2i(int k) { return __uint_as_float((uint32_t)(127 + k) << 23); }
 
 // Tile walk: global tile index -> (expert, row block, column block) with
 // grouped rasterisation inside each expert; monotone in the tile index.
@@ -199,13 +220,13 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::NS; ++i) {
       // The leader producer's arrive + both CTAs' TMA bytes; e4m3 B adds one
-      // arrival per converter warp of both CTAs.
-      mbar_init(full + i, BFP8 ? 1 + 2 * C::CVT_WARPS : 1);
+      // arrival per warp of the stage's converter group in both CTAs.
+      mbar_init(full + i, BFP8 ? 1 + 2 * (C::CVT_WARPS / 2) : 1);
       mbar_init(empty + i, 1);
     }
     for (int i = 0; i < C::NR; ++i) {
       mbar_init(raw_full + i, 1);
-      mbar_init(raw_empty + i, C::CVT_WARPS);
+      mbar_init(raw_empty + i, C::CVT_WARPS / 2);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(acc_full + i, 1);
@@ -252,7 +273,7 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
           }
           uint8_t* st = ring + stage * C::STAGE;
           if constexpr (BFP8) {
-            // A of both CTAs lands on the leader's barrier; the bf16 B half
+            // A of both CTAs lands on the leader's barrier; the f16 B half
             // of each CTA comes from its converter warps (raw ring below).
             const uint32_t bar = full_l0 + stage * 8;
             if (rank == 0) mbar_arrive_expect_tx(full + stage, C::TX_A);
@@ -342,18 +363,22 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
       }
     }
   } else if (BFP8 && warp >= 2u + C::EPI_WARPS) {
-    // ------------------------------------------------------------ e4m3 -> bf16 B converters (both CTAs)
-    // Thread t handles k-row r = t % 64 of the 64 x 128 raw tile and half
-    // h = t / 64 of its 128 columns (= one 64-column bf16 atom row, 128
-    // bytes): the 8 threads of a quarter-warp own 8 consecutive rows, so their
-    // swizzled 16-byte accesses fall in 8 distinct bank groups.  A raw tile is
-    // converted as soon as it has landed and its operand stage is free.
-    const int ct = (int)threadIdx.x - 64 - C::EPI_WARPS * 32;  // 0..127
-    const int r = ct & 63, h = ct >> 6;
+    // ------------------------------------------------------------ e4m3 -> f16 B converters (both CTAs)
+    // Two groups of four warps take alternate K steps (K / 64 is even, so a
+    // group keeps its parity across tiles): each group has two stage times
+    // for its stage, and the fixed costs of a stage (barrier checks, fence,
+    // hand-off) of the two groups overlap.  In a group, thread t handles
+    // k-row r = t % 64 of the 64 x 128 raw tile and half h = t / 64 of its
+    // 128 columns (= one 64-column f16 atom row, 128 bytes): the 8 threads of
+    // a quarter-warp own 8 consecutive rows, so their swizzled 16-byte
+    // accesses fall in 8 distinct bank groups.  A raw tile is converted as
+    // soon as it has landed and its operand stage is free.
+    const int ct = (int)threadIdx.x - 64 - C::EPI_WARPS * 32;  // 0..255
+    const int grp = ct >> 7;
+    const int r = ct & 63, h = (ct >> 6) & 1;
     const int nkb_scale = p.K / 128, nnb_scale = p.N / 128;
     TileCursor cur;
-    int stage = 0, rs = 0;
-    uint32_t phase = 0, rph = 0;
+    uint32_t gk = 0;  // K steps of this CTA's earlier tiles
     bool ok = true;
     for (int t = pair; ok; t += npairs) {
       if (!cur.seek(t, p.group_sizes, p.E, p.M, nt)) break;
@@ -366,7 +391,11 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
       // stage, so no stage waits on a global load.
       const float s_lo = (int)lane < nkb_scale ? __ldg(srow + (size_t)lane * nnb_scale) : 0.f;
       const float s_hi = (int)lane + 32 < nkb_scale ? __ldg(srow + (size_t)(lane + 32) * nnb_scale) : 0.f;
-      for (int kb = 0; kb < nk; ++kb) {
+      const float up = exp2i(fp8_tile_shift(p.b_scale, p.K, p.N, cur.e, nb, lane));
+      for (int kb = grp; kb < nk; kb += 2) {
+        const uint32_t g = gk + (uint32_t)kb;
+        const int stage = (int)(g % C::NS), rs = (int)(g % C::NR);
+        const uint32_t phase = (g / C::NS) & 1u, rph = (g / C::NR) & 1u;
         if (!mbar_wait_warp(raw_full + rs, rph, abort_flag, p.status) ||
             !mbar_wait_warp(empty + stage, phase ^ 1u, abort_flag, p.status)) {
           ok = false;
@@ -375,6 +404,7 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
         const int kblk = (kb * C::BK) / 128;
         const float s_reg = __shfl_sync(0xffffffffu, kblk < 32 ? s_lo : s_hi, kblk & 31);
         const float sc = kblk < 64 ? s_reg : __ldg(srow + (size_t)kblk * nnb_scale);
+        const uint32_t s2 = pack_f16x2_sat(sc * up, sc * up);
         const uint8_t* src = rawring + rs * C::B8_BYTES + r * 128;             // 128-byte swizzled raw row
         uint8_t* dst = ring + stage * C::STAGE + C::A_BYTES + h * (64 * 128) + r * 128;  // atom h, row r
         const int rsw = r & 7;
@@ -382,8 +412,8 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
         for (int c = 0; c < 4; ++c) {
           const int chunk = 4 * h + c;  // 16 raw bytes = columns 16*chunk .. +15
           const uint4 v = *reinterpret_cast<const uint4*>(src + ((chunk ^ rsw) << 4));
-          const uint2 b0 = e4m3x4_to_bf16x4(v.x, sc), b1 = e4m3x4_to_bf16x4(v.y, sc);
-          const uint2 b2 = e4m3x4_to_bf16x4(v.z, sc), b3 = e4m3x4_to_bf16x4(v.w, sc);
+          const uint2 b0 = e4m3x4_to_f16x4(v.x, s2), b1 = e4m3x4_to_f16x4(v.y, s2);
+          const uint2 b2 = e4m3x4_to_f16x4(v.z, s2), b3 = e4m3x4_to_f16x4(v.w, s2);
           const int j0 = 2 * c, j1 = 2 * c + 1;  // output 16-byte chunks in the atom row
           *reinterpret_cast<uint4*>(dst + ((j0 ^ rsw) << 4)) = make_uint4(b0.x, b0.y, b1.x, b1.y);
           *reinterpret_cast<uint4*>(dst + ((j1 ^ rsw) << 4)) = make_uint4(b2.x, b2.y, b3.x, b3.y);
@@ -394,15 +424,8 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
           mbar_arrive(raw_empty + rs);
           mbar_arrive_cluster_cta(full_l0 + stage * 8);
         }
-        if (++stage == C::NS) {
-          stage = 0;
-          phase ^= 1u;
-        }
-        if (++rs == C::NR) {
-          rs = 0;
-          rph ^= 1u;
-        }
       }
+      gk += (uint32_t)nk;
     }
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
@@ -440,25 +463,47 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
       if (!mbar_wait_warp(acc_full + ab, use & 1u, abort_flag, p.status)) break;
       tc_fence_after();
       const uint32_t acc = lane_base + ab * C::BN;
+      // FP8 tiles were accumulated with weights scaled by 2^k.
+      const float mul = BFP8 ? exp2i(-fp8_tile_shift(p.b_scale, p.K, p.N, cur.e, nb, lane)) : 1.f;
       if constexpr (EPI == 0) {
-        // 64 columns per step: GELU, pack to bf16, stage 32 rows x 128 B,
-        // store rows as full 128-byte lines.
-        uint16_t* H = reinterpret_cast<uint16_t*>(p.out);  // bf16 bits
+        // 64 columns per step: GELU, pack to bf16 (f16 for FP8 weights),
+        // stage 32 rows x 128 B, store rows as full 128-byte lines.
+        uint16_t* H = reinterpret_cast<uint16_t*>(p.out);  // bf16 / f16 bits
 #pragma unroll 1
         for (int c0 = 0; c0 < C::BN; c0 += 64) {
           uint32_t v[64];
-          tmem_ld32(acc + c0, *reinterpret_cast<uint32_t(*)[32]>(v));
-          tmem_ld32(acc + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
-          tmem_ld_wait();
           uint4* srow = reinterpret_cast<uint4*>(wst) + lane * 8;
+          if constexpr (BFP8) {
+            // Two 32-column halves (fewer live registers: this block has the
+            // converter warps' registers to share).
+#pragma unroll 1
+            for (int hh = 0; hh < 2; ++hh) {
+              tmem_ld32(acc + c0 + 32 * hh, *reinterpret_cast<uint32_t(*)[32]>(v));
+              tmem_ld_wait();
+              auto g = [&](int i) { return gelu_tanh_fast(__uint_as_float(v[i]) * mul); };
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            uint4 w;
-            w.x = pack_bf16x2(gelu_tanh_fast(__uint_as_float(v[8 * k + 0])), gelu_tanh_fast(__uint_as_float(v[8 * k + 1])));
-            w.y = pack_bf16x2(gelu_tanh_fast(__uint_as_float(v[8 * k + 2])), gelu_tanh_fast(__uint_as_float(v[8 * k + 3])));
-            w.z = pack_bf16x2(gelu_tanh_fast(__uint_as_float(v[8 * k + 4])), gelu_tanh_fast(__uint_as_float(v[8 * k + 5])));
-            w.w = pack_bf16x2(gelu_tanh_fast(__uint_as_float(v[8 * k + 6])), gelu_tanh_fast(__uint_as_float(v[8 * k + 7])));
-            srow[k ^ (lane & 7)] = w;
+              for (int k = 0; k < 4; ++k) {
+                uint4 w;
+                w.x = pack_f16x2_sat(g(8 * k + 0), g(8 * k + 1));
+                w.y = pack_f16x2_sat(g(8 * k + 2), g(8 * k + 3));
+                w.z = pack_f16x2_sat(g(8 * k + 4), g(8 * k + 5));
+                w.w = pack_f16x2_sat(g(8 * k + 6), g(8 * k + 7));
+                srow[(4 * hh + k) ^ (lane & 7)] = w;
+              }
+            }
+          } else {
+            tmem_ld32(acc + c0, *reinterpret_cast<uint32_t(*)[32]>(v));
+            tmem_ld32(acc + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+            tmem_ld_wait();
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              uint4 w;
+              w.x = pack_bf16x2(gelu_tanh_fast(__uint_as_float(v[8 * k + 0])), gelu_tanh_fast(__uint_as_float(v[8 * k + 1])));
+              w.y = pack_bf16x2(gelu_tanh_fast(__uint_as_float(v[8 * k + 2])), gelu_tanh_fast(__uint_as_float(v[8 * k + 3])));
+              w.z = pack_bf16x2(gelu_tanh_fast(__uint_as_float(v[8 * k + 4])), gelu_tanh_fast(__uint_as_float(v[8 * k + 5])));
+              w.w = pack_bf16x2(gelu_tanh_fast(__uint_as_float(v[8 * k + 6])), gelu_tanh_fast(__uint_as_float(v[8 * k + 7])));
+              srow[k ^ (lane & 7)] = w;
+            }
           }
           __syncwarp();
           const int gcol = nb * C::BN + c0;
@@ -490,7 +535,15 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
         }
         float4* wst4 = reinterpret_cast<float4*>(wst);
 #pragma unroll 1
-        for (int c0 = 0; c0 < C::BN; c0 += 32) store_y_rows(acc + c0, wst4, row_ptr, nb * C::BN + c0, lane);
+        for (int c0 = 0; c0 < C::BN; c0 += 32) store_y_rows(acc + c0, wst4, row_ptr, nb * C::BN + c0, lane, mul);
+      } else if (BFP8) {
+        // f32 Y rows scaled back by 2^-k, through the same staging as below.
+        float* Y = reinterpret_cast<float*>(p.out);
+        float4* wst4 = reinterpret_cast<float4*>(wst);
+        const int R = wrow0 + (int)lane;
+        uint8_t* row_ptr = R < row_end ? reinterpret_cast<uint8_t*>(Y + (size_t)R * p.N) : nullptr;
+#pragma unroll 1
+        for (int c0 = 0; c0 < C::BN; c0 += 32) store_y_rows(acc + c0, wst4, row_ptr, nb * C::BN + c0, lane, mul);
       } else {
         float* Y = reinterpret_cast<float*>(p.out);
         float4* wst4 = reinterpret_cast<float4*>(wst);

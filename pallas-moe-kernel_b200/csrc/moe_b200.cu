@@ -163,7 +163,26 @@ static bool large_supported(int D, int F, int dtype) {
   if (dtype == MOE_DTYPE_FP8_E4M3_BLK128) return D % 256 == 0 && F % 256 == 0;
   return false;
 }
-static size_t large_ws_bytes(int64_t M, int F) { return (size_t)M * F * 2; }
+static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// Large-D workspace: H (M, F) in 16 bits; with e4m3 weights also X in f16.
+static size_t large_ws_bytes(int64_t M, int D, int F, int dtype) {
+  const size_t h = align256((size_t)M * F * 2);
+  return dtype == MOE_DTYPE_FP8_E4M3_BLK128 ? h + (size_t)M * D * 2 : h;
+}
+
+// bf16 -> f16 (8 values per thread step), saturating at +-65504: the f16
+// operand of the e4m3-weight GEMMs.  Exact for every bf16 value in f16 range
+// (down to f16's subnormals).
+__global__ void bf16_to_f16_kernel(const uint4* __restrict__ x, uint4* __restrict__ out, size_t n8) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (size_t)gridDim.x * blockDim.x) {
+    const uint4 v = x[i];
+    auto cvt = [](uint32_t w) {
+      return pack_f16x2_sat(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+    };
+    out[i] = make_uint4(cvt(v.x), cvt(v.y), cvt(v.z), cvt(v.w));
+  }
+}
 
 template <int EPI, bool BFP8>
 static int launch_gemm(const GemmMaps& maps, const GemmParams& prm, DevInfo* di, cudaStream_t st, int ctas_req) {
@@ -215,7 +234,7 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
   DevInfo* di;
   if (int r = device_info(&dev, &di)) return r;
   const int ctas = opt.ctas > 0 ? opt.ctas : (int)g_tune_ctas;
-  const size_t need = large_ws_bytes(M, F);
+  const size_t need = large_ws_bytes(M, D, F, dtype);
   if (ws_bytes < need) return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", ws_bytes, need);
   if (reinterpret_cast<uintptr_t>(ws) & 255u) return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
   const bool fp8 = dtype == MOE_DTYPE_FP8_E4M3_BLK128;
@@ -224,11 +243,24 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
   int* status = nullptr;
   MOE_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_status));
   const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const auto F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const auto U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  // e4m3 weights: the GEMMs run on f16 operands; X is converted once.
+  const auto A16 = fp8 ? F16 : BF16;
+  const void* xa = x;
+  if (fp8) {
+    if (reinterpret_cast<uintptr_t>(x) & 15u) return fail(MOE_ERR_MISALIGNED, "x must be 16-byte aligned");
+    void* x16 = static_cast<uint8_t*>(ws) + align256((size_t)M * F * 2);
+    const size_t n8 = (size_t)M * D / 8;
+    const int blocks = (int)std::min<size_t>((n8 + 255) / 256, (size_t)di->sms * 8);
+    bf16_to_f16_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint4*>(x), static_cast<uint4*>(x16), n8);
+    MOE_CUDA_TRY(cudaGetLastError());
+    xa = x16;
+  }
   // up: H = GELU(X @ W_up[e])
   GemmMaps m1;
   memset(&m1, 0, sizeof(m1));
-  if (int r = make_map_2d(&m1.a, x, BF16, 2, (uint64_t)M, D, 64, 128)) return r;
+  if (int r = make_map_2d(&m1.a, xa, A16, 2, (uint64_t)M, D, 64, 128)) return r;
   if (fp8) {
     if (int r = make_map_2d(&m1.b, w_up, U8, 1, (uint64_t)E * D, F, 128, 64)) return r;
   } else {
@@ -240,7 +272,7 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
   // down: Y = H @ W_down[e]
   GemmMaps m2;
   memset(&m2, 0, sizeof(m2));
-  if (int r = make_map_2d(&m2.a, ws, BF16, 2, (uint64_t)M, F, 64, 128)) return r;
+  if (int r = make_map_2d(&m2.a, ws, A16, 2, (uint64_t)M, F, 64, 128)) return r;
   if (fp8) {
     if (int r = make_map_2d(&m2.b, w_down, U8, 1, (uint64_t)E * F, D, 128, 64)) return r;
   } else {
@@ -280,7 +312,6 @@ static SmallPlan small_plan(int64_t M, int D, int F, int E, int dtype) {
   return s;
 }
 
-static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 template <int MODE, int D, int BF, bool XR>
 static int launch_small(const FusedMaps& maps, const FusedParams& prm, int ctas, DevInfo* di, cudaStream_t st) {
@@ -585,7 +616,8 @@ static void ep_release(moe_ep_s* ep) {
 static_assert(kEpMaxWorld == 8, "EpScatter holds 8 peer buffers");
 
 static int ep_mlp_launches(const moe_ep_s* ep) {
-  if (!small_supported(ep->D, ep->F, ep->dtype)) return 2;        // up + down grouped GEMMs
+  if (!small_supported(ep->D, ep->F, ep->dtype))                   // (X -> f16 +) up + down grouped GEMMs
+    return ep->dtype == MOE_DTYPE_FP8_E4M3_BLK128 ? 3 : 2;
   return (ep->dtype == MOE_DTYPE_F32 && ep->D == 256) ? 2 : 1;   // (+ X split) fused kernel
 }
 
@@ -641,7 +673,7 @@ int moe_device_status(int reset) {
 size_t moe_fused_mlp_workspace_size(int64_t M, int32_t D, int32_t F, int32_t E, int32_t dtype) {
   if (M < 0 || D <= 0 || F <= 0 || E <= 0) return 0;
   if (small_supported(D, F, dtype)) return align256(small_plan(M, D, F, E, dtype).ws_bytes);
-  if (large_supported(D, F, dtype)) return align256(large_ws_bytes(M, F));
+  if (large_supported(D, F, dtype)) return align256(large_ws_bytes(M, D, F, dtype));
   return 0;
 }
 
@@ -813,7 +845,7 @@ int moe_ep_create(int32_t rank, int32_t world, int32_t num_local_experts, int64_
   ep->abort_word = reinterpret_cast<int*>(ep->tables + t_slices + t_rows + t_gs + 256 + 256);
   if (scatter) ep->recv = reinterpret_cast<int4*>(ep->tables + t_slices + t_rows + t_gs + t_misc);
   ep->ws_bytes = small_supported(D, F, dtype) ? align256(small_plan(cap, D, F, ep->el, dtype).ws_bytes)
-                                              : align256(large_ws_bytes(cap, F));
+                                              : align256(large_ws_bytes(cap, D, F, dtype));
   if (ep->ws_bytes && (e = cudaMalloc(&ep->ws, ep->ws_bytes)) != cudaSuccess) return cuda_fail(e, "cudaMalloc(workspace)");
   if ((e = cudaStreamCreateWithFlags(&ep->comm, cudaStreamNonBlocking)) != cudaSuccess)
     return cuda_fail(e, "cudaStreamCreate");

@@ -286,6 +286,7 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t ab_format, uint32_t m
   return (1u << 4) | (ab_format << 7) | (ab_format << 10) | (a_mn_major << 15) | (b_mn_major << 16) |
          ((n >> 3) << 17) | ((m >> 4) << 24);
 }
+constexpr uint32_t kFmtF16 = 0;
 constexpr uint32_t kFmtBF16 = 1;
 constexpr uint32_t kFmtTF32 = 2;
 
@@ -494,6 +495,12 @@ __device__ __forceinline__ float gelu_tanh_fast(float x) {
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// Two floats -> f16x2, saturating to +-65504 (no infinities from finite input).
+__device__ __forceinline__ uint32_t pack_f16x2_sat(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
 }
 

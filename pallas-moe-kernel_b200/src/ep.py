@@ -78,7 +78,8 @@ class ExpertParallelMLP:
                 sms = torch.cuda.get_device_properties(w_up_local.device).multi_processor_count
                 _lib.set_tuning(2, max(2, sms - self.reserve_sms))    # persistent CTAs per launch
             expert_fn = lambda xr, gs: self._experts(xr, gs)  # noqa: E731
-            self.launches_per_wave = 2 if w_up_local.shape[1] > 256 else 1
+            fp8 = w_up_local.dtype == torch.float8_e4m3fn
+            self.launches_per_wave = (3 if fp8 else 2) if w_up_local.shape[1] > 256 else 1
         else:
             self.launches_per_wave = 0
         self.expert_fn = expert_fn
