@@ -86,6 +86,28 @@ def test_engine_world1_matches_single_gpu(dt, D, F, E, waves):
         layer.close()
 
 
+def test_engine_world1_fp8_matches_single_gpu():
+    """e4m3 block-scaled weights through the engine (combine fused into the
+    down GEMM): bit-identical to moe_fused_mlp on the same rows."""
+    from src.routing import quantize_e4m3_blockwise
+    D, F, E = 512, 1024, 4
+    wu, wd = _weights(E, D, F, "f32")
+    (wq_u, su), (wq_d, sd) = quantize_e4m3_blockwise(wu), quantize_e4m3_blockwise(wd)
+    layer = PeerExpertParallelMLP(wq_u, wq_d, rank=0, world=1, max_tokens=2048, w_up_scale=su, w_down_scale=sd)
+    rng = np.random.default_rng(9)
+    try:
+        for kind, M in [("uniform", 2048), ("zipf", 1000)]:
+            gs = _routing(kind, M, E, rng)
+            x = torch.randn((M, D), device=DEV).to(torch.bfloat16)
+            y = layer(x, torch.from_numpy(gs)).clone()
+            ref = fused_ragged_mlp(x, wq_u, wq_d, torch.from_numpy(gs).to(DEV), w_up_scale=su, w_down_scale=sd)
+            torch.cuda.synchronize()
+            assert torch.equal(y, ref), kind
+        assert _lib.device_status(reset=True) == 0
+    finally:
+        layer.close()
+
+
 def test_engine_world1_clamps_bad_group_sizes_and_empty_batch():
     D, F, E = 128, 512, 4
     wu, wd = _weights(E, D, F, "f32")
