@@ -74,10 +74,20 @@ class ExpertParallelMLP:
             # A rank can receive up to world * max_tokens rows in the worst routing.
             self._experts = PreparedExperts(w_up_local, w_down_local, max_tokens=world * max_tokens,
                                             w_up_scale=w_up_scale, w_down_scale=w_down_scale)
+            ctas = 0
             if self.reserve_sms:
                 sms = torch.cuda.get_device_properties(w_up_local.device).multi_processor_count
-                _lib.set_tuning(2, max(2, sms - self.reserve_sms))    # persistent CTAs per launch
-            expert_fn = lambda xr, gs: self._experts(xr, gs)  # noqa: E731
+                ctas = max(2, sms - self.reserve_sms)
+
+            def expert_fn(xr, gs):
+                # Persistent CTAs per launch capped for this layer's launches only.
+                if not ctas:
+                    return self._experts(xr, gs)
+                _lib.set_tuning(2, ctas)
+                try:
+                    return self._experts(xr, gs)
+                finally:
+                    _lib.set_tuning(2, 0)
             fp8 = w_up_local.dtype == torch.float8_e4m3fn
             self.launches_per_wave = (3 if fp8 else 2) if w_up_local.shape[1] > 256 else 1
         else:
