@@ -6,12 +6,16 @@ A step is one forward of the expert MLP over one batch of synthetic routed
 tokens (seeded; shapes, inits and routing of the named configuration).
 ``value`` is routed tokens/s over the whole job with inputs resident in HBM,
 device-timed with CUDA events, L2 flushed before every step; ``e2e`` is the
-same metric through the public call with the step's inputs copied from
-pinned host memory and the result read back inside the timed region.
+same metric through the public call with every step's inputs copied from
+pinned host memory and its result read back into pinned host memory inside
+the timed region (consecutive steps pipelined over three streams, as a
+serving loop runs them).
 
 At N > 1 (torchrun, one rank per GPU) the expert-parallel layer runs: every
 rank owns E/N experts and its own batch of tokens; tokens travel to their
-expert's rank and back through NCCL all-to-all (weak scaling).
+expert's rank and back through the library's NVLink exchange kernels
+(``--transport peer``, default) or NCCL send/recv (``--transport nccl``);
+weak scaling.
 """
 
 from __future__ import annotations
@@ -256,27 +260,55 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
     if status:
         raise RuntimeError(f"device status {status} after the timed region")
 
-    # e2e: pinned host X -> device, call, Y -> pinned host, every step.
+    # e2e: every step copies its inputs from pinned host memory, runs the
+    # public call and reads Y back into pinned host memory.  Consecutive steps
+    # are pipelined on three streams (copy in, compute, copy out) over two
+    # device and two host buffer slots, as a serving loop runs them: H2D of
+    # step i+1 and D2H of step i-1 overlap the compute of step i.
     xh = x.cpu().pin_memory()
     gsh = torch.from_numpy(gs_np).pin_memory()
-    yh = torch.empty((cfg.M, cfg.D), dtype=torch.float32).pin_memory()
-    xd = torch.empty_like(x)
-    gsd = torch.empty_like(gs_dev)
+    yh = [torch.empty((cfg.M, cfg.D), dtype=torch.float32).pin_memory() for _ in range(2)]
+    xd = [torch.empty_like(x) for _ in range(2)]
+    gsd = [torch.empty_like(gs_dev) for _ in range(2)]
+    yd = [torch.empty((cfg.M, cfg.D), dtype=torch.float32, device=device) for _ in range(2)]
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    ev_in, ev_cmp, ev_out = ([torch.cuda.Event() for _ in range(2)] for _ in range(3))
 
-    def e2e_step():
-        xd.copy_(xh, non_blocking=True)
-        gsd.copy_(gsh, non_blocking=True)
-        if world > 1:
-            out = layer(xd, gsd)
-        else:
-            out = fused_ragged_dot_caller(xd, w_up, w_down, gsd, BM=16, BF=64, max_group_size=cfg.M,
-                                          out=y, workspace=ws, **sc)
-        yh.copy_(out, non_blocking=True)
+    def e2e_run(n):
+        for i in range(n):
+            b = i & 1
+            s_in.wait_event(ev_cmp[b])              # step i-2 no longer reads slot b's inputs
+            with torch.cuda.stream(s_in):
+                xd[b].copy_(xh, non_blocking=True)
+                gsd[b].copy_(gsh, non_blocking=True)
+            ev_in[b].record(s_in)
+            stream.wait_event(ev_in[b])
+            stream.wait_event(ev_out[b])            # step i-2's Y has left slot b
+            if world > 1:
+                out = layer(xd[b], gsd[b], out=yd[b]) if hasattr(layer, "close") else layer(xd[b], gsd[b])
+                if out is not yd[b]:
+                    yd[b].copy_(out)
+            else:
+                fused_ragged_dot_caller(xd[b], w_up, w_down, gsd[b], BM=16, BF=64, max_group_size=cfg.M,
+                                        out=yd[b], workspace=ws, **sc)
+            ev_cmp[b].record(stream)
+            s_out.wait_event(ev_cmp[b])
+            with torch.cuda.stream(s_out):
+                yh[b].copy_(yd[b], non_blocking=True)
+            ev_out[b].record(s_out)
+        stream.wait_event(ev_out[(n - 1) & 1])
 
-    for _ in range(max(1, args.warmup)):
-        e2e_step()
+    e2e_run(max(2, args.warmup))
     torch.cuda.synchronize(device)
-    e2e_ms = float(sum(timed(e2e_step, args.steps)))
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    s_in.wait_event(e0)
+    e2e_run(args.steps)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = e0.elapsed_time(e1)
 
     vals = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=device)
     if world > 1:
@@ -339,7 +371,9 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
     line["clocks"] = clocks.summary(t0, t1)
     h2d = cfg.M * cfg.D * x.element_size() + gs_np.nbytes
     line["e2e"] = {"value": world * cfg.M * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
-                   "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": cfg.M * cfg.D * 4}
+                   "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": cfg.M * cfg.D * 4,
+                   "pipelining": "copy-in, compute and copy-out of consecutive steps on three streams, "
+                                 "two buffer slots"}
     return line
 
 
