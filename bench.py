@@ -484,6 +484,74 @@ def run_layer(args, cfg, device) -> dict:
     }
 
 
+def run_swiglu(args, cfg, device) -> dict:
+    """SwiGLU experts (bf16) on the configuration's shape and routing on one
+    GPU: the up GEMM over the interleaved gate/up weights with the SiLU-gate
+    epilogue, then the down GEMM; inputs resident in HBM, L2 flushed before
+    every step.  FLOPs = 6 M D F; algorithmic bytes = X + the non-empty
+    experts' three weight matrices + Y (H is an intermediate)."""
+    import torch
+    from src import _lib
+    from src.kernel import fused_ragged_swiglu, swiglu_interleave
+    from src.routing import config_group_sizes
+
+    gs = config_group_sizes(cfg, seed=0)
+    g = torch.Generator(device=device)
+    g.manual_seed(1234)
+    x = torch.randn((cfg.M, cfg.D), generator=g, device=device).to(torch.bfloat16)
+    w_gate = (torch.randn((cfg.E, cfg.D, cfg.F), generator=g, device=device) / math.sqrt(cfg.D)).to(torch.bfloat16)
+    w_up = (torch.randn((cfg.E, cfg.D, cfg.F), generator=g, device=device) / math.sqrt(cfg.D)).to(torch.bfloat16)
+    w_down = (torch.randn((cfg.E, cfg.F, cfg.D), generator=g, device=device) / math.sqrt(cfg.F)).to(torch.bfloat16)
+    w_gu = swiglu_interleave(w_gate, w_up)
+    del w_gate, w_up
+    gs_dev = torch.from_numpy(gs).to(device)
+    y = torch.empty((cfg.M, cfg.D), device=device)
+    ws = torch.empty(int(_lib.lib().moe_fused_mlp_swiglu_workspace_size(cfg.M, cfg.D, cfg.F)), dtype=torch.uint8,
+                     device=device)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    st = torch.cuda.current_stream(device)
+    for _ in range(args.warmup):
+        fused_ragged_swiglu(x, w_gu, w_down, gs_dev, out=y, workspace=ws)
+    torch.cuda.synchronize(device)
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    time.sleep(0.05)
+    t0 = time.perf_counter()
+    times = []
+    for _ in range(args.steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        fused_ragged_swiglu(x, w_gu, w_down, gs_dev, out=y, workspace=ws)
+        b.record(st)
+        torch.cuda.synchronize(device)
+        times.append(a.elapsed_time(b))
+    t1 = time.perf_counter()
+    clocks.stop()
+    if _lib_status():
+        raise RuntimeError("device status set after the SwiGLU stage")
+    ms = sum(times) / len(times)
+    peaks, peak_src = load_peaks()
+    peak = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
+    flops = 6 * cfg.M * cfg.D * cfg.F
+    active = int(np.count_nonzero(gs > 0))
+    byts = cfg.M * cfg.D * 2 + active * 3 * cfg.D * cfg.F * 2 + cfg.M * cfg.D * 4
+    achieved = flops / (ms / 1e3) / 1e12
+    return {
+        "metric": "routed_tokens_per_s", "value": cfg.M / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "dtype": "bf16", "data": "synthetic (seeded N(0,1) X, N(0,1/D) / N(0,1/F) weights)",
+        "config": {"workload": f"{cfg.name}_swiglu", "M": cfg.M, "D": cfg.D, "F": cfg.F, "E": cfg.E,
+                   "activation": "swiglu", "l2": "flushed before every step (256 MiB write)"},
+        "gpu_launches": 2 * args.steps,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": None, "algorithmic_flops": flops,
+                     "algorithmic_bytes": byts, "peak_source": f"{peak_src}: bf16_tflops",
+                     "kernels": "up GEMM (SiLU-gate epilogue) + down GEMM, timed together"},
+        "clocks": clocks.summary(t0, t1),
+    }
+
+
 def _lib_status() -> int:
     from src import _lib
     return _lib.device_status(reset=True)
@@ -558,6 +626,9 @@ def main() -> int:
     ap.add_argument("--config", default="c4",
                     help="c1..c5 (default c4: bf16 Mixtral-shaped M=32768 D=4096 F=14336 E=8, top-2)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--act", default="gelu", choices=["gelu", "swiglu"],
+                    help="expert activation: gelu (the reference's GELU-tanh MLP) or swiglu "
+                         "(SiLU-gated experts, bf16, one GPU)")
     ap.add_argument("--stage", default="mlp", choices=["mlp", "layer"],
                     help="mlp: the expert MLP (the reference's path); layer: routing + permutation + expert MLP "
                          "+ combine of a whole MoE layer on one GPU (top-k configurations)")
@@ -608,6 +679,11 @@ def main() -> int:
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    if args.act == "swiglu":
+        if world > 1:
+            raise SystemExit("--act swiglu runs on one GPU")
+        print(json.dumps(run_swiglu(args, cfg, device)), flush=True)
+        return 0
     if args.stage == "layer":
         print(json.dumps(run_layer(args, cfg, device)), flush=True)
         return 0

@@ -222,6 +222,31 @@ int moe_gather_rows(const void* x, const int32_t* sorted_src, int64_t rows, int3
 int moe_combine_rows(const float* y_sorted, const int32_t* inverse, const float* topk_weights, int64_t T, int32_t k,
                      int32_t D, float* y, void* stream);
 
+/*
+ * SwiGLU experts: Y = ragged_dot(SiLU(ragged_dot(X, W_gate)) * ragged_dot(X,
+ * W_up), W_down), the expert MLP of Mixtral / DeepSeek-style layers.  No
+ * counterpart in the reference, whose expert MLP is GELU-tanh only
+ * (src/kernel.py:46-63); the ragged layout, group_sizes semantics, rows past
+ * sum(group_sizes) (zeros) and the error codes are those of moe_fused_mlp.
+ * bf16 only; D a multiple of 256, F a multiple of 128.
+ *
+ * moe_swiglu_interleave  w_gate, w_up (E, D, F) bf16 -> w_gate_up (E, D, 2F):
+ *                  columns interleaved every 128 (gate 0..127, up 0..127,
+ *                  gate 128..255, ...), the operand layout of the up GEMM.
+ *                  Run once per set of weights.
+ * moe_fused_mlp_swiglu   x (M, D) bf16, w_gate_up (E, D, 2F) bf16 from
+ *                  moe_swiglu_interleave, w_down (E, F, D) bf16 -> y (M, D)
+ *                  f32.  H = SiLU(gate) * up goes through the workspace as
+ *                  bf16 (M, F): moe_fused_mlp_swiglu_workspace_size bytes,
+ *                  256-byte aligned.
+ */
+int moe_swiglu_interleave(const void* w_gate, const void* w_up, void* w_gate_up, int32_t E, int32_t D, int32_t F,
+                          void* stream);
+size_t moe_fused_mlp_swiglu_workspace_size(int64_t M, int32_t D, int32_t F);
+int moe_fused_mlp_swiglu(const void* x, const void* w_gate_up, const void* w_down, const int32_t* group_sizes,
+                         float* y, int64_t M, int32_t D, int32_t F, int32_t E, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
 /* Text of the calling thread's last error ("" when none). */
 const char* moe_last_error(void);
 

@@ -256,3 +256,31 @@ def combine_rows(y_sorted: np.ndarray, inverse: np.ndarray, weights: np.ndarray,
         ok = inv[:, j] >= 0
         y[ok] += w[ok, j:j + 1] * ys[inv[ok, j]]
     return y
+
+
+# ----------------------------------------------------------------------------- SwiGLU experts
+# The reference's expert MLP is GELU-tanh only (src/kernel.py:46-63).  The
+# SwiGLU variant keeps its ragged layout and group_sizes semantics and swaps
+# the activation for the gated one of Mixtral / DeepSeek-style experts.
+
+def silu(x: np.ndarray) -> np.ndarray:
+    """x * sigmoid(x), in the input's precision."""
+    return x / (1.0 + np.exp(-x))
+
+
+def ref_ragged_swiglu(x: np.ndarray, w_gate: np.ndarray, w_up: np.ndarray, w_down: np.ndarray,
+                      group_sizes: Sequence[int], acc_dtype=np.float64) -> np.ndarray:
+    """Y = ragged_dot(silu(ragged_dot(X, W_gate)) * ragged_dot(X, W_up), W_down);
+    rows past sum(group_sizes) are zero, as in ``ref_ragged_mlp``."""
+    g = ragged_dot(x, w_gate, group_sizes, acc_dtype)
+    u = ragged_dot(x, w_up, group_sizes, acc_dtype)
+    return ragged_dot(silu(g) * u, w_down, group_sizes, acc_dtype)
+
+
+def swiglu_interleave(w_gate: np.ndarray, w_up: np.ndarray, period: int = 128) -> np.ndarray:
+    """(E, D, F) gate and up -> (E, D, 2F) with blocks of ``period`` columns
+    alternating gate, up, gate, up, ..."""
+    E, D, F = w_gate.shape
+    g = w_gate.reshape(E, D, F // period, 1, period)
+    u = w_up.reshape(E, D, F // period, 1, period)
+    return np.concatenate([g, u], axis=3).reshape(E, D, 2 * F)

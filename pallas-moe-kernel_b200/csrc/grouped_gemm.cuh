@@ -82,7 +82,10 @@ __device__ __forceinline__ void store_y_rows(uint32_t taddr, float4* stage, uint
   __syncwarp();
 }
 
-template <int EPI, bool BFP8>  // EPI 0: GELU -> H, 1: f32 Y; BFP8: e4m3 B dequantised in smem, f16 operands
+// EPI 0: GELU -> H, 1: f32 Y, 2: SwiGLU -> H (B holds gate and up weights
+// interleaved every 128 columns; H has half the columns); BFP8: e4m3 B
+// dequantised in smem, f16 operands.
+template <int EPI, bool BFP8>
 struct GemmCfg {
   static constexpr int BM = 128;   // rows per CTA (256 per pair)
   static constexpr int BN = 256;   // output columns per tile (128 per CTA of B)
@@ -515,6 +518,45 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
             const int row = wrow0 + r;
             if (row < row_end)
               *reinterpret_cast<uint4*>(H + (size_t)row * p.N + gcol + 8 * k) = val;
+          }
+          __syncwarp();
+        }
+      } else if constexpr (EPI == 2) {
+        // SwiGLU: columns [0, 128) of the tile are gate, [128, 256) up;
+        // H[:, 128 nb + c] = SiLU(gate_c) * up_c, 64 columns per step through
+        // the same 32-row x 128-byte staging as the GELU epilogue.
+        uint16_t* H = reinterpret_cast<uint16_t*>(p.out);  // bf16 bits
+        const int ldh = p.N / 2;
+#pragma unroll 1
+        for (int c0 = 0; c0 < C::BN / 2; c0 += 64) {
+          uint4* srow = reinterpret_cast<uint4*>(wst) + lane * 8;
+#pragma unroll 1
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t g[32], u[32];
+            tmem_ld32(acc + c0 + 32 * hh, g);
+            tmem_ld32(acc + C::BN / 2 + c0 + 32 * hh, u);
+            tmem_ld_wait();
+            auto h = [&](int i) { return silu_fast(__uint_as_float(g[i])) * __uint_as_float(u[i]); };
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              uint4 w;
+              w.x = pack_bf16x2(h(8 * k + 0), h(8 * k + 1));
+              w.y = pack_bf16x2(h(8 * k + 2), h(8 * k + 3));
+              w.z = pack_bf16x2(h(8 * k + 4), h(8 * k + 5));
+              w.w = pack_bf16x2(h(8 * k + 6), h(8 * k + 7));
+              srow[(4 * hh + k) ^ (lane & 7)] = w;
+            }
+          }
+          __syncwarp();
+          const int gcol = nb * (C::BN / 2) + c0;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = 4 * i + (int)(lane >> 3);
+            const int k = (int)(lane & 7);
+            const uint4 val = reinterpret_cast<const uint4*>(wst)[r * 8 + (k ^ (r & 7))];
+            const int row = wrow0 + r;
+            if (row < row_end)
+              *reinterpret_cast<uint4*>(H + (size_t)row * ldh + gcol + 8 * k) = val;
           }
           __syncwarp();
         }

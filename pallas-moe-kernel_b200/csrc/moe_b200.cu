@@ -84,7 +84,7 @@ static int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType d
 struct DevInfo {
   int sms = 0;
   bool attr_set[32] = {};
-  int pairs[8] = {};  // co-resident CTA pairs per pair-kernel variant (0 = not queried)
+  int pairs[16] = {};  // co-resident CTA pairs per pair-kernel variant (0 = not queried)
 };
 static DevInfo g_dev[64];
 static std::mutex g_dev_mu;
@@ -188,8 +188,9 @@ template <int EPI, bool BFP8>
 static int launch_gemm(const GemmMaps& maps, const GemmParams& prm, DevInfo* di, cudaStream_t st, int ctas_req) {
   using Cfg = GemmCfg<EPI, BFP8>;
   auto kern = grouped_gemm_pair_kernel<EPI, BFP8>;
-  constexpr int slot = 24 + EPI + (BFP8 ? 2 : 0);
-  constexpr int pslot = 4 + EPI + (BFP8 ? 2 : 0);
+  constexpr int slot = 24 + 2 * EPI + (BFP8 ? 1 : 0);
+  constexpr int pslot = 8 + 2 * EPI + (BFP8 ? 1 : 0);
+  static_assert(slot < 32 && pslot < 16, "attribute slot");
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -281,6 +282,54 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
   GemmParams p2{gs, y, (int)M, E, D, F, F, 8, status, w_down_scale, opt.skip_tail ? 1 : 0};
   if (opt.scatter) p2.scatter = *opt.scatter;
   return fp8 ? launch_gemm<1, true>(m2, p2, di, st, ctas) : launch_gemm<1, false>(m2, p2, di, st, ctas);
+}
+
+// ------------------------------------------------------------------ SwiGLU experts
+// (E, D, F) gate and up weights -> (E, D, 2F) with columns interleaved every
+// 128: [gate 0..127 | up 0..127 | gate 128..255 | up 128..255 | ...], so that
+// every 256-column tile of the up GEMM holds matching gate and up columns.
+// One thread per 16-byte vector (8 bf16).
+__global__ void swiglu_interleave_kernel(const uint4* __restrict__ gate, const uint4* __restrict__ up,
+                                         uint4* __restrict__ out, size_t rows, int F) {
+  const int vin = F / 8, vout = 2 * vin;
+  const size_t n = rows * (size_t)vout;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / vout;
+    const int v = (int)(i - r * vout);
+    const int j = v / 32, w = v % 32;   // 32 vectors = 256 columns per interleave period
+    const uint4* src = w < 16 ? gate : up;
+    out[i] = src[r * vin + (size_t)j * 16 + (w & 15)];
+  }
+}
+
+static bool swiglu_supported(int D, int F) { return D >= 256 && D % 256 == 0 && F % 128 == 0; }
+
+static int run_swiglu(const void* x, const void* w_gu, const void* w_down, const int32_t* gs, float* y, int64_t M,
+                      int D, int F, int E, void* ws, size_t ws_bytes, cudaStream_t st) {
+  int dev;
+  DevInfo* di;
+  if (int r = device_info(&dev, &di)) return r;
+  const size_t need = align256((size_t)M * F * 2);
+  if (ws_bytes < need) return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", ws_bytes, need);
+  if (reinterpret_cast<uintptr_t>(ws) & 255u) return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+  int* status = nullptr;
+  MOE_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_status));
+  const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int ctas = (int)g_tune_ctas;
+  // up: H = SiLU(X @ W_gate[e]) * (X @ W_up[e]) over the interleaved (E*D, 2F) weights
+  GemmMaps m1;
+  memset(&m1, 0, sizeof(m1));
+  if (int r = make_map_2d(&m1.a, x, BF16, 2, (uint64_t)M, D, 64, 128)) return r;
+  if (int r = make_map_2d(&m1.b, w_gu, BF16, 2, (uint64_t)E * D, 2 * F, 64, 64)) return r;
+  GemmParams p1{gs, ws, (int)M, E, 2 * F, D, D, 8, status, nullptr, 0};
+  if (int r = launch_gemm<2, false>(m1, p1, di, st, ctas)) return r;
+  // down: Y = H @ W_down[e]
+  GemmMaps m2;
+  memset(&m2, 0, sizeof(m2));
+  if (int r = make_map_2d(&m2.a, ws, BF16, 2, (uint64_t)M, F, 64, 128)) return r;
+  if (int r = make_map_2d(&m2.b, w_down, BF16, 2, (uint64_t)E * F, D, 64, 64)) return r;
+  GemmParams p2{gs, y, (int)M, E, D, F, F, 8, status, nullptr, 0};
+  return launch_gemm<1, false>(m2, p2, di, st, ctas);
 }
 
 // ------------------------------------------------------------------ small-D dispatch
@@ -1203,6 +1252,47 @@ int moe_combine_rows(const float* y_sorted, const int32_t* inverse, const float*
   combine_rows_kernel<<<blocks, 512, 0, static_cast<cudaStream_t>(stream)>>>(y_sorted, inverse, weights, T, k, D, y);
   MOE_CUDA_TRY(cudaGetLastError());
   return 0;
+}
+
+// ------------------------------------------------------------------ SwiGLU experts
+int moe_swiglu_interleave(const void* w_gate, const void* w_up, void* w_gate_up, int32_t E, int32_t D, int32_t F,
+                          void* stream) {
+  t_err[0] = 0;
+  if (E <= 0 || D <= 0 || F <= 0 || F % 128) return fail(MOE_ERR_INVALID_ARG, "E=%d D=%d F=%d (F %% 128 == 0)", E, D, F);
+  if (!w_gate || !w_up || !w_gate_up) return fail(MOE_ERR_INVALID_ARG, "null pointer");
+  if ((reinterpret_cast<uintptr_t>(w_gate) | reinterpret_cast<uintptr_t>(w_up) |
+       reinterpret_cast<uintptr_t>(w_gate_up)) & 15u)
+    return fail(MOE_ERR_MISALIGNED, "weights must be 16-byte aligned");
+  int dev;
+  DevInfo* di;
+  if (int r = device_info(&dev, &di)) return r;
+  const size_t rows = (size_t)E * D, n = rows * (size_t)(F / 4);
+  const int blocks = (int)std::min<size_t>((n + 255) / 256, (size_t)di->sms * 8);
+  swiglu_interleave_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(w_gate), static_cast<const uint4*>(w_up), static_cast<uint4*>(w_gate_up), rows, F);
+  MOE_CUDA_TRY(cudaGetLastError());
+  return 0;
+}
+
+size_t moe_fused_mlp_swiglu_workspace_size(int64_t M, int32_t D, int32_t F) {
+  if (M < 0 || !swiglu_supported(D, F)) return 0;
+  return align256((size_t)M * F * 2);
+}
+
+int moe_fused_mlp_swiglu(const void* x, const void* w_gate_up, const void* w_down, const int32_t* group_sizes,
+                         float* y, int64_t M, int32_t D, int32_t F, int32_t E, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  t_err[0] = 0;
+  if (M < 0 || D <= 0 || F <= 0 || E <= 0)
+    return fail(MOE_ERR_INVALID_ARG, "bad sizes M=%lld D=%d F=%d E=%d", (long long)M, D, F, E);
+  if (M > (int64_t)0x7fffffff) return fail(MOE_ERR_UNSUPPORTED_SHAPE, "M=%lld exceeds 2^31-1", (long long)M);
+  if (!swiglu_supported(D, F))
+    return fail(MOE_ERR_UNSUPPORTED_SHAPE, "SwiGLU experts need D %% 256 == 0 (D >= 256) and F %% 128 == 0");
+  if (M == 0) return 0;
+  if (!x || !w_gate_up || !w_down || !group_sizes || !y) return fail(MOE_ERR_INVALID_ARG, "null operand pointer");
+  if (reinterpret_cast<uintptr_t>(y) & 15u) return fail(MOE_ERR_MISALIGNED, "y must be 16-byte aligned");
+  return run_swiglu(x, w_gate_up, w_down, group_sizes, y, M, D, F, E, workspace, workspace_bytes,
+                    static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

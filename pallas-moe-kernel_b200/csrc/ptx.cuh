@@ -492,6 +492,12 @@ __device__ __forceinline__ float gelu_tanh_fast(float x) {
   return fmaf(hx, tanh_approx(u), hx);
 }
 
+// SiLU(x) = x / (1 + e^-x) = x / (1 + 2^(-x log2 e)), with the approximate
+// exp2 and reciprocal (relative error ~1e-7, far below bf16 rounding).
+__device__ __forceinline__ float silu_fast(float x) {
+  return x * rcp_approx(1.0f + ex2_approx(-1.4426950408889634f * x));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));

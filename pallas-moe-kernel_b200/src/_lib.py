@@ -87,6 +87,12 @@ def lib() -> ctypes.CDLL:
     L.moe_gather_rows.restype = ctypes.c_int
     L.moe_combine_rows.argtypes = [vp, vp, vp, i64, i32, i32, vp, vp]
     L.moe_combine_rows.restype = ctypes.c_int
+    L.moe_swiglu_interleave.argtypes = [vp, vp, vp, i32, i32, i32, vp]
+    L.moe_swiglu_interleave.restype = ctypes.c_int
+    L.moe_fused_mlp_swiglu_workspace_size.argtypes = [i64, i32, i32]
+    L.moe_fused_mlp_swiglu_workspace_size.restype = sz
+    L.moe_fused_mlp_swiglu.argtypes = [vp, vp, vp, vp, vp, i64, i32, i32, i32, vp, sz, vp]
+    L.moe_fused_mlp_swiglu.restype = ctypes.c_int
     L.moe_ep_destroy.argtypes = [vp]
     L.moe_ep_destroy.restype = ctypes.c_int
     _lib = L

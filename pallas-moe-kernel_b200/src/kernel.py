@@ -128,6 +128,71 @@ def fused_ragged_mlp(x: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor, 
     return out
 
 
+def swiglu_interleave(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
+    """(E, D, F) bf16 gate and up weights -> the (E, D, 2F) operand of
+    ``fused_ragged_swiglu``: blocks of 128 columns alternating gate, up."""
+    if w_gate.shape != w_up.shape or w_gate.dim() != 3:
+        raise ValueError(f"w_gate {tuple(w_gate.shape)} and w_up {tuple(w_up.shape)} must be the same (E, D, F)")
+    if w_gate.dtype != torch.bfloat16 or w_up.dtype != torch.bfloat16:
+        raise TypeError("SwiGLU weights are bf16")
+    if not (w_gate.is_cuda and w_up.device == w_gate.device):
+        raise ValueError("w_gate and w_up must be on one CUDA device")
+    E, D, F = w_gate.shape
+    w_gate, w_up = w_gate.contiguous(), w_up.contiguous()
+    out = torch.empty((E, D, 2 * F), device=w_gate.device, dtype=torch.bfloat16)
+    with torch.cuda.device(w_gate.device):
+        rc = _lib.lib().moe_swiglu_interleave(
+            ctypes.c_void_p(w_gate.data_ptr()), ctypes.c_void_p(w_up.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+            E, D, F, ctypes.c_void_p(torch.cuda.current_stream(w_gate.device).cuda_stream))
+    _lib.check(rc)
+    return out
+
+
+def fused_ragged_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor, group_sizes,
+                        *, out: Optional[torch.Tensor] = None,
+                        workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """SwiGLU experts: ``Y = ragged_dot(silu(X W_gate) * (X W_up), W_down)``.
+
+    x (M, D) bf16, w_gate_up (E, D, 2F) bf16 from ``swiglu_interleave``,
+    w_down (E, F, D) bf16, group_sizes (E,) -> y (M, D) f32.  Same ragged
+    semantics as ``fused_ragged_mlp``; D a multiple of 256, F of 128.
+    """
+    if not x.is_cuda:
+        raise ValueError("fused_ragged_swiglu runs on CUDA tensors only (no CPU path)")
+    M, D = x.shape
+    E, D2, F2 = w_gate_up.shape
+    F = F2 // 2
+    if D != D2 or F2 % 2 or tuple(w_down.shape) != (E, F, D):
+        raise ValueError(f"shape mismatch x={tuple(x.shape)} w_gate_up={tuple(w_gate_up.shape)} "
+                         f"w_down={tuple(w_down.shape)}")
+    for t in (x, w_gate_up, w_down):
+        if t.dtype != torch.bfloat16:
+            raise TypeError("SwiGLU experts take bf16 operands")
+        if t.device != x.device:
+            raise ValueError("all operands must be on the same device")
+    dev = x.device
+    x, w_gate_up, w_down = x.contiguous(), w_gate_up.contiguous(), w_down.contiguous()
+    gs = _as_device_group_sizes(group_sizes, dev)
+    if gs.numel() != E:
+        raise ValueError(f"group_sizes has {gs.numel()} entries, expected E={E}")
+    if out is None:
+        out = torch.empty((M, D), device=dev, dtype=torch.float32)
+    elif out.shape != (M, D) or out.dtype != torch.float32 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous (M, D) float32 tensor")
+    L = _lib.lib()
+    ws_bytes = int(L.moe_fused_mlp_swiglu_workspace_size(M, D, F))
+    if ws_bytes and (workspace is None or workspace.numel() * workspace.element_size() < ws_bytes):
+        workspace = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    with torch.cuda.device(dev):
+        rc = L.moe_fused_mlp_swiglu(
+            ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(w_gate_up.data_ptr()),
+            ctypes.c_void_p(w_down.data_ptr()), ctypes.c_void_p(gs.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+            M, D, F, E, ctypes.c_void_p(workspace.data_ptr() if ws_bytes else 0), ws_bytes,
+            ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream))
+    _lib.check(rc)
+    return out
+
+
 class PreparedExperts:
     """Expert weights with their kernel-side operand layout built once
     (``moe_prepare_weights``), for repeated calls with fixed weights.
