@@ -484,6 +484,88 @@ def run_layer(args, cfg, device) -> dict:
     }
 
 
+def run_train(args, cfg, device) -> dict:
+    """Training step of the expert MLP (bf16) on one GPU: forward with the
+    pre-activation saved, then the backward (dX, dW_up, dW_down) for a given
+    dY; inputs resident in HBM, L2 flushed before every step.  FLOPs = 12 M D F
+    (forward 4, backward 8); launches per step: 2 forward + 5 backward."""
+    import torch
+    from src import _lib
+    from src.train import backward, forward_train
+
+    if cfg.dtype != "bf16":
+        cfg = with_shape_dtype(cfg, "bf16")
+    x, w_up, w_down, gs, _ = make_workload(cfg, device)
+    gs_dev = torch.from_numpy(gs).to(device)
+    g = torch.Generator(device=device)
+    g.manual_seed(4321)
+    dy = torch.randn((cfg.M, cfg.D), generator=g, device=device)
+    y = torch.empty((cfg.M, cfg.D), device=device)
+    a = torch.empty((cfg.M, cfg.F), device=device, dtype=torch.bfloat16)
+    L = _lib.lib()
+    ws_f = torch.empty(int(L.moe_fused_mlp_forward_train_workspace_size(cfg.M, cfg.D, cfg.F, cfg.E)),
+                       dtype=torch.uint8, device=device)
+    ws_b = torch.empty(int(L.moe_fused_mlp_backward_workspace_size(cfg.M, cfg.D, cfg.F, cfg.E)),
+                       dtype=torch.uint8, device=device)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    st = torch.cuda.current_stream(device)
+
+    def step():
+        forward_train(x, w_up, w_down, gs_dev, out=y, a_save=a, workspace=ws_f)
+        return backward(x, w_up, w_down, gs_dev, a, dy, workspace=ws_b)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    time.sleep(0.05)
+    t0 = time.perf_counter()
+    fwd, tot = [], []
+    for _ in range(args.steps):
+        flush.zero_()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record(st)
+        forward_train(x, w_up, w_down, gs_dev, out=y, a_save=a, workspace=ws_f)
+        ev[1].record(st)
+        backward(x, w_up, w_down, gs_dev, a, dy, workspace=ws_b)
+        ev[2].record(st)
+        torch.cuda.synchronize(device)
+        fwd.append(ev[0].elapsed_time(ev[1]))
+        tot.append(ev[0].elapsed_time(ev[2]))
+    t1 = time.perf_counter()
+    clocks.stop()
+    if _lib_status():
+        raise RuntimeError("device status set after the training stage")
+    ms = sum(tot) / len(tot)
+    f_ms = sum(fwd) / len(fwd)
+    peaks, peak_src = load_peaks()
+    peak = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
+    mdf = cfg.M * cfg.D * cfg.F
+    achieved = 12 * mdf / (ms / 1e3) / 1e12
+    return {
+        "metric": "routed_tokens_per_s", "value": cfg.M / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "dtype": "bf16", "data": "synthetic (seeded N(0,1) X and dY, N(0,1/D) / N(0,1/F) weights)",
+        "config": {"workload": f"{cfg.name}_train", "M": cfg.M, "D": cfg.D, "F": cfg.F, "E": cfg.E,
+                   "step": "forward (pre-activation saved) + backward (dX, dW_up, dW_down f32)",
+                   "l2": "flushed before every step (256 MiB write)"},
+        "gpu_launches": 7 * args.steps,
+        "forward_ms": f_ms, "backward_ms": ms - f_ms,
+        "backward_tflops": 8 * mdf / ((ms - f_ms) / 1e3) / 1e12,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": None, "algorithmic_flops": 12 * mdf,
+                     "peak_source": f"{peak_src}: bf16_tflops",
+                     "kernels": "forward 2 grouped GEMMs + backward pad + 4 grouped GEMMs, timed together"},
+        "clocks": clocks.summary(t0, t1),
+    }
+
+
+def with_shape_dtype(cfg, dtype):
+    from src.routing import with_shape
+    return with_shape(cfg, dtype=dtype, name=f"{cfg.name}_as_{dtype}")
+
+
 def run_swiglu(args, cfg, device) -> dict:
     """SwiGLU experts (bf16) on the configuration's shape and routing on one
     GPU: the up GEMM over the interleaved gate/up weights with the SiLU-gate
@@ -629,9 +711,10 @@ def main() -> int:
     ap.add_argument("--act", default="gelu", choices=["gelu", "swiglu"],
                     help="expert activation: gelu (the reference's GELU-tanh MLP) or swiglu "
                          "(SiLU-gated experts, bf16, one GPU)")
-    ap.add_argument("--stage", default="mlp", choices=["mlp", "layer"],
+    ap.add_argument("--stage", default="mlp", choices=["mlp", "layer", "train"],
                     help="mlp: the expert MLP (the reference's path); layer: routing + permutation + expert MLP "
-                         "+ combine of a whole MoE layer on one GPU (top-k configurations)")
+                         "+ combine of a whole MoE layer on one GPU (top-k configurations); train: forward with "
+                         "the pre-activation saved + backward of the expert MLP (bf16, one GPU)")
     ap.add_argument("--ref-budget", type=float, default=10.0, help="seconds of CPU baseline timing")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tokens", type=int, default=0, help="override M (routed rows per GPU)")
@@ -686,6 +769,11 @@ def main() -> int:
         return 0
     if args.stage == "layer":
         print(json.dumps(run_layer(args, cfg, device)), flush=True)
+        return 0
+    if args.stage == "train":
+        if world > 1:
+            raise SystemExit("--stage train runs on one GPU")
+        print(json.dumps(run_train(args, cfg, device)), flush=True)
         return 0
     try:
         line = run_ours(args, cfg, rank, world, device)

@@ -247,6 +247,40 @@ int moe_fused_mlp_swiglu(const void* x, const void* w_gate_up, const void* w_dow
                          float* y, int64_t M, int32_t D, int32_t F, int32_t E, void* workspace,
                          size_t workspace_bytes, void* stream);
 
+/*
+ * Training: forward with the pre-activation saved, and the backward.  No
+ * counterpart in the reference, which has no backward pass (its kernel is
+ * forward-only, src/kernel.py:9-123); the forward math, ragged layout and
+ * group_sizes semantics are those of moe_fused_mlp.  bf16 operands, f32
+ * accumulation; D and F multiples of 256; E <= 4096.
+ *
+ * moe_fused_mlp_forward_train  as moe_fused_mlp with MOE_DTYPE_BF16 (always
+ *                  on the two grouped GEMMs), plus a_save (M, F) bf16 = the
+ *                  pre-activation X W_up[e] of every routed row (rows past
+ *                  sum(group_sizes) untouched).  Workspace:
+ *                  moe_fused_mlp_forward_train_workspace_size bytes.
+ * moe_fused_mlp_backward  given dy (M, D) (dy_dtype MOE_DTYPE_F32 or
+ *                  MOE_DTYPE_BF16) and the forward's a_saved:
+ *                    dx      (M, D) f32 = (dy W_down[e]^T * GELU'(A)) W_up[e]^T,
+ *                            rows past sum(group_sizes) zero;
+ *                    dw_up   (E, D, F) f32 = X_e^T (dy_e W_down[e]^T * GELU'(A_e));
+ *                    dw_down (E, F, D) f32 = GELU(A_e)^T dy_e;
+ *                  experts without rows get zero weight gradients.  dy and
+ *                  the intermediate dA and GELU(A) are rounded to bf16 for
+ *                  the tensor cores.  Workspace:
+ *                  moe_fused_mlp_backward_workspace_size bytes (256-byte
+ *                  aligned; padded copies of X, dy, dA and GELU(A)).
+ */
+size_t moe_fused_mlp_forward_train_workspace_size(int64_t M, int32_t D, int32_t F, int32_t E);
+int moe_fused_mlp_forward_train(const void* x, const void* w_up, const void* w_down, const int32_t* group_sizes,
+                                float* y, void* a_save, int64_t M, int32_t D, int32_t F, int32_t E, void* workspace,
+                                size_t workspace_bytes, void* stream);
+size_t moe_fused_mlp_backward_workspace_size(int64_t M, int32_t D, int32_t F, int32_t E);
+int moe_fused_mlp_backward(const void* x, const void* w_up, const void* w_down, const int32_t* group_sizes,
+                           const void* a_saved, const void* dy, int32_t dy_dtype, float* dx, float* dw_up,
+                           float* dw_down, int64_t M, int32_t D, int32_t F, int32_t E, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
 /* Text of the calling thread's last error ("" when none). */
 const char* moe_last_error(void);
 

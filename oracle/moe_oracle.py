@@ -284,3 +284,46 @@ def swiglu_interleave(w_gate: np.ndarray, w_up: np.ndarray, period: int = 128) -
     g = w_gate.reshape(E, D, F // period, 1, period)
     u = w_up.reshape(E, D, F // period, 1, period)
     return np.concatenate([g, u], axis=3).reshape(E, D, 2 * F)
+
+
+# ----------------------------------------------------------------------------- backward
+# The reference is forward-only (src/kernel.py:9-123).  The gradients of its
+# expert MLP, Y = ragged_dot(gelu_tanh(ragged_dot(X, W_up)), W_down), follow
+# from the chain rule per expert; rows past sum(group_sizes) take no part.
+
+def gelu_tanh_grad(x: np.ndarray) -> np.ndarray:
+    """d/dx of ``gelu_tanh``: 0.5 (1 + t) + 0.5 x (1 - t^2) k0 (1 + 3 k1 x^2),
+    t = tanh(k0 (x + k1 x^3))."""
+    k0 = np.sqrt(2.0 / np.pi)
+    k1 = 0.044715
+    t = np.tanh(k0 * (x + k1 * x ** 3))
+    return 0.5 * (1.0 + t) + 0.5 * x * (1.0 - t * t) * k0 * (1.0 + 3.0 * k1 * x * x)
+
+
+def ref_ragged_mlp_backward(x: np.ndarray, w_up: np.ndarray, w_down: np.ndarray, group_sizes: Sequence[int],
+                            dy: np.ndarray, acc_dtype=np.float64):
+    """(dX (M, D), dW_up (E, D, F), dW_down (E, F, D)) of ``ref_ragged_mlp``
+    for the upstream gradient dy (M, D): per expert e with rows R,
+    A = X_R W_up[e], dA = (dy_R W_down[e]^T) * gelu'(A), dX_R = dA W_up[e]^T,
+    dW_up[e] = X_R^T dA, dW_down[e] = gelu(A)^T dy_R.  Rows past
+    sum(group_sizes) get dX = 0; experts without rows get zero dW."""
+    M, D = x.shape
+    E, _, F = w_up.shape
+    dx = np.zeros((M, D), acc_dtype)
+    dwu = np.zeros((E, D, F), acc_dtype)
+    dwd = np.zeros((E, F, D), acc_dtype)
+    offs = np.minimum(group_sizes_to_offsets(np.maximum(np.asarray(group_sizes), 0)), M)
+    for e in range(E):
+        a, b = int(offs[e]), int(offs[e + 1])
+        if b <= a:
+            continue
+        xe = x[a:b].astype(acc_dtype)
+        ye = dy[a:b].astype(acc_dtype)
+        wu = w_up[e].astype(acc_dtype)
+        wd = w_down[e].astype(acc_dtype)
+        pre = xe @ wu
+        da = (ye @ wd.T) * gelu_tanh_grad(pre)
+        dx[a:b] = da @ wu.T
+        dwu[e] = xe.T @ da
+        dwd[e] = gelu_tanh(pre).T @ ye
+    return dx, dwu, dwd

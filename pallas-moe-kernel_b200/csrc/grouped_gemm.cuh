@@ -54,6 +54,7 @@ struct GemmParams {
   const float* b_scale;  // FP8 weights: (E, K/128, N/128) f32 block scales, else null
   int skip_tail;         // 1: leave rows at or past sum(group_sizes) unwritten (Y only)
   EpScatter scatter;     // Y only: rows go to their source ranks (expert parallelism)
+  void* out2;            // EPI 3: the pre-activation X W_up (bf16, [M, N]) saved for the backward
 };
 
 // store_y_block with one destination row pointer per row: lane l of the warp
@@ -83,8 +84,9 @@ __device__ __forceinline__ void store_y_rows(uint32_t taddr, float4* stage, uint
 }
 
 // EPI 0: GELU -> H, 1: f32 Y, 2: SwiGLU -> H (B holds gate and up weights
-// interleaved every 128 columns; H has half the columns); BFP8: e4m3 B
-// dequantised in smem, f16 operands.
+// interleaved every 128 columns; H has half the columns), 3: GELU -> H plus
+// the pre-activation (bf16) to out2; BFP8: e4m3 B dequantised in smem, f16
+// operands.
 template <int EPI, bool BFP8>
 struct GemmCfg {
   static constexpr int BM = 128;   // rows per CTA (256 per pair)
@@ -397,8 +399,9 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
       const float up = exp2i(fp8_tile_shift(p.b_scale, p.K, p.N, cur.e, nb, lane));
       for (int kb = grp; kb < nk; kb += 2) {
         const uint32_t g = gk + (uint32_t)kb;
-        const int stage = (int)(g % C::NS), rs = (int)(g % C::NR);
-        const uint32_t phase = (g / C::NS) & 1u, rph = (g / C::NR) & 1u;
+        constexpr uint32_t kNR = C::NR > 0 ? C::NR : 1;  // this branch only runs with e4m3 weights
+        const int stage = (int)(g % C::NS), rs = (int)(g % kNR);
+        const uint32_t phase = (g / C::NS) & 1u, rph = (g / kNR) & 1u;
         if (!mbar_wait_warp(raw_full + rs, rph, abort_flag, p.status) ||
             !mbar_wait_warp(empty + stage, phase ^ 1u, abort_flag, p.status)) {
           ok = false;
@@ -468,7 +471,7 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
       const uint32_t acc = lane_base + ab * C::BN;
       // FP8 tiles were accumulated with weights scaled by 2^k.
       const float mul = BFP8 ? exp2i(-fp8_tile_shift(p.b_scale, p.K, p.N, cur.e, nb, lane)) : 1.f;
-      if constexpr (EPI == 0) {
+      if constexpr (EPI == 0 || EPI == 3) {
         // 64 columns per step: GELU, pack to bf16 (f16 for FP8 weights),
         // stage 32 rows x 128 B, store rows as full 128-byte lines.
         uint16_t* H = reinterpret_cast<uint16_t*>(p.out);  // bf16 / f16 bits
@@ -520,6 +523,30 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
               *reinterpret_cast<uint4*>(H + (size_t)row * p.N + gcol + 8 * k) = val;
           }
           __syncwarp();
+          if constexpr (EPI == 3 && !BFP8) {
+            // The same 64 columns before the activation, for the backward.
+            uint16_t* A = reinterpret_cast<uint16_t*>(p.out2);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              uint4 w;
+              w.x = pack_bf16x2(__uint_as_float(v[8 * k + 0]), __uint_as_float(v[8 * k + 1]));
+              w.y = pack_bf16x2(__uint_as_float(v[8 * k + 2]), __uint_as_float(v[8 * k + 3]));
+              w.z = pack_bf16x2(__uint_as_float(v[8 * k + 4]), __uint_as_float(v[8 * k + 5]));
+              w.w = pack_bf16x2(__uint_as_float(v[8 * k + 6]), __uint_as_float(v[8 * k + 7]));
+              srow[k ^ (lane & 7)] = w;
+            }
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int r = 4 * i + (int)(lane >> 3);
+              const int k = (int)(lane & 7);
+              const uint4 val = reinterpret_cast<const uint4*>(wst)[r * 8 + (k ^ (r & 7))];
+              const int row = wrow0 + r;
+              if (row < row_end)
+                *reinterpret_cast<uint4*>(A + (size_t)row * p.N + gcol + 8 * k) = val;
+            }
+            __syncwarp();
+          }
         }
       } else if constexpr (EPI == 2) {
         // SwiGLU: columns [0, 128) of the tile are gate, [128, 256) up;

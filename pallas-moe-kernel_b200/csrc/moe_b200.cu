@@ -14,6 +14,7 @@
 #include "router.cuh"
 #include "fused_pair.cuh"
 #include "grouped_gemm.cuh"
+#include "grouped_gemm_bwd.cuh"
 
 namespace moe {
 __device__ int g_status = 0;
@@ -83,8 +84,8 @@ static int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType d
 // ------------------------------------------------------------------ device info
 struct DevInfo {
   int sms = 0;
-  bool attr_set[32] = {};
-  int pairs[16] = {};  // co-resident CTA pairs per pair-kernel variant (0 = not queried)
+  bool attr_set[40] = {};
+  int pairs[24] = {};  // co-resident CTA pairs per pair-kernel variant (0 = not queried)
 };
 static DevInfo g_dev[64];
 static std::mutex g_dev_mu;
@@ -282,6 +283,134 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
   GemmParams p2{gs, y, (int)M, E, D, F, F, 8, status, w_down_scale, opt.skip_tail ? 1 : 0};
   if (opt.scatter) p2.scatter = *opt.scatter;
   return fp8 ? launch_gemm<1, true>(m2, p2, di, st, ctas) : launch_gemm<1, false>(m2, p2, di, st, ctas);
+}
+
+// ------------------------------------------------------------------ training: forward with saved pre-activation, backward
+template <int MODE>
+static int launch_bwd(const GemmMaps& maps, const BwdParams& prm, DevInfo* di, cudaStream_t st, int ctas_req) {
+  using Cfg = BwdCfg<MODE>;
+  auto kern = grouped_bwd_pair_kernel<MODE>;
+  constexpr int slot = 32 + MODE;
+  constexpr int pslot = 16 + MODE;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!di->attr_set[slot]) {
+    MOE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    cfg.gridDim = dim3(2 * (di->sms / 2));
+    int clusters = 0;
+    MOE_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg));
+    if (clusters < 1) return fail(MOE_ERR_CUDA, "no CTA pair fits on this device");
+    di->pairs[pslot] = clusters;
+    di->attr_set[slot] = true;
+  }
+  int pairs = di->pairs[pslot];
+  if (ctas_req > 0 && ctas_req / 2 < pairs) pairs = ctas_req / 2 > 0 ? ctas_req / 2 : 1;
+  cfg.gridDim = dim3(2 * pairs);
+  MOE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, maps, prm));
+  return 0;
+}
+
+static bool train_supported(int D, int F) { return D >= 256 && D % 256 == 0 && F >= 256 && F % 256 == 0; }
+
+// Padded rows of the backward's row-layout buffers: every expert's rows
+// rounded up to 64, at most 63 extra rows per expert.
+static int64_t bwd_padded_rows(int64_t M, int E) { return M + 64 * (int64_t)E; }
+
+static size_t bwd_ws_bytes(int64_t M, int D, int F, int E) {
+  const int64_t mp = bwd_padded_rows(M, E);
+  return 2 * align256((size_t)mp * D * 2) + 2 * align256((size_t)mp * F * 2);
+}
+
+// Forward of the bf16 expert MLP on the grouped GEMMs, saving A = X W_up.
+static int run_train_forward(const void* x, const void* w_up, const void* w_down, const int32_t* gs, float* y,
+                             void* a_save, int64_t M, int D, int F, int E, void* ws, size_t ws_bytes,
+                             cudaStream_t st) {
+  int dev;
+  DevInfo* di;
+  if (int r = device_info(&dev, &di)) return r;
+  const size_t need = large_ws_bytes(M, D, F, MOE_DTYPE_BF16);
+  if (ws_bytes < need) return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", ws_bytes, need);
+  if (reinterpret_cast<uintptr_t>(ws) & 255u) return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+  int* status = nullptr;
+  MOE_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_status));
+  const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int ctas = (int)g_tune_ctas;
+  GemmMaps m1;
+  memset(&m1, 0, sizeof(m1));
+  if (int r = make_map_2d(&m1.a, x, BF16, 2, (uint64_t)M, D, 64, 128)) return r;
+  if (int r = make_map_2d(&m1.b, w_up, BF16, 2, (uint64_t)E * D, F, 64, 64)) return r;
+  GemmParams p1{gs, ws, (int)M, E, F, D, D, 8, status, nullptr, 0};
+  p1.out2 = a_save;
+  if (int r = launch_gemm<3, false>(m1, p1, di, st, ctas)) return r;
+  GemmMaps m2;
+  memset(&m2, 0, sizeof(m2));
+  if (int r = make_map_2d(&m2.a, ws, BF16, 2, (uint64_t)M, F, 64, 128)) return r;
+  if (int r = make_map_2d(&m2.b, w_down, BF16, 2, (uint64_t)E * F, D, 64, 64)) return r;
+  GemmParams p2{gs, y, (int)M, E, D, F, F, 8, status, nullptr, 0};
+  return launch_gemm<1, false>(m2, p2, di, st, ctas);
+}
+
+static int run_backward(const void* x, const void* w_up, const void* w_down, const int32_t* gs, const void* a_saved,
+                        const void* dy, int dy_dtype, float* dx, float* dw_up, float* dw_down, int64_t M, int D,
+                        int F, int E, void* ws, size_t ws_bytes, cudaStream_t st) {
+  int dev;
+  DevInfo* di;
+  if (int r = device_info(&dev, &di)) return r;
+  const size_t need = bwd_ws_bytes(M, D, F, E);
+  if (ws_bytes < need) return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", ws_bytes, need);
+  if (reinterpret_cast<uintptr_t>(ws) & 255u) return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+  int* status = nullptr;
+  MOE_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_status));
+  const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int ctas = (int)g_tune_ctas;
+  const int64_t mp = bwd_padded_rows(M, E);
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  uint16_t* x_pad = reinterpret_cast<uint16_t*>(w);
+  uint16_t* dy_pad = reinterpret_cast<uint16_t*>(w + align256((size_t)mp * D * 2));
+  uint16_t* da_pad = reinterpret_cast<uint16_t*>(w + 2 * align256((size_t)mp * D * 2));
+  uint16_t* h_pad = reinterpret_cast<uint16_t*>(w + 2 * align256((size_t)mp * D * 2) + align256((size_t)mp * F * 2));
+  // 1. X and dY in the padded row layout.
+  {
+    const int blocks = (int)std::min<int64_t>((mp + 7) / 8, (int64_t)di->sms * 8);
+    bwd_pad_rows_kernel<<<blocks, 256, 8 * (E + 1), st>>>(static_cast<const uint16_t*>(x), dy,
+                                                           dy_dtype == MOE_DTYPE_F32 ? 1 : 0, gs, E, (int)M, D,
+                                                           x_pad, dy_pad);
+    MOE_CUDA_TRY(cudaGetLastError());
+  }
+  GemmMaps m;
+  // 2. dH = dY W_down^T -> dA = dH GELU'(A), H = GELU(A) (padded rows).
+  memset(&m, 0, sizeof(m));
+  if (int r = make_map_2d(&m.a, dy_pad, BF16, 2, (uint64_t)mp, D, 64, 128)) return r;
+  if (int r = make_map_2d(&m.b, w_down, BF16, 2, (uint64_t)E * F, D, 64, 128)) return r;
+  BwdParams p{gs, (int)M, E, F, D, 0, 8, status, static_cast<const uint16_t*>(a_saved), da_pad, h_pad};
+  if (int r = launch_bwd<kBwdDH>(m, p, di, st, ctas)) return r;
+  // 3. dX = dA W_up^T (natural rows).
+  memset(&m, 0, sizeof(m));
+  if (int r = make_map_2d(&m.a, da_pad, BF16, 2, (uint64_t)mp, F, 64, 128)) return r;
+  if (int r = make_map_2d(&m.b, w_up, BF16, 2, (uint64_t)E * D, F, 64, 128)) return r;
+  p = BwdParams{gs, (int)M, E, D, F, 0, 8, status, nullptr, dx, nullptr};
+  if (int r = launch_bwd<kBwdDX>(m, p, di, st, ctas)) return r;
+  // 4. dW_up[e] = X_e^T dA_e  (E, D, F).
+  memset(&m, 0, sizeof(m));
+  if (int r = make_map_2d(&m.a, x_pad, BF16, 2, (uint64_t)mp, D, 64, 64)) return r;
+  if (int r = make_map_2d(&m.b, da_pad, BF16, 2, (uint64_t)mp, F, 64, 64)) return r;
+  p = BwdParams{gs, (int)M, E, F, 0, D, 8, status, nullptr, dw_up, nullptr};
+  if (int r = launch_bwd<kBwdDW>(m, p, di, st, ctas)) return r;
+  // 5. dW_down[e] = H_e^T dY_e  (E, F, D).
+  memset(&m, 0, sizeof(m));
+  if (int r = make_map_2d(&m.a, h_pad, BF16, 2, (uint64_t)mp, F, 64, 64)) return r;
+  if (int r = make_map_2d(&m.b, dy_pad, BF16, 2, (uint64_t)mp, D, 64, 64)) return r;
+  p = BwdParams{gs, (int)M, E, D, 0, F, 8, status, nullptr, dw_down, nullptr};
+  return launch_bwd<kBwdDW>(m, p, di, st, ctas);
 }
 
 // ------------------------------------------------------------------ SwiGLU experts
@@ -1293,6 +1422,58 @@ int moe_fused_mlp_swiglu(const void* x, const void* w_gate_up, const void* w_dow
   if (reinterpret_cast<uintptr_t>(y) & 15u) return fail(MOE_ERR_MISALIGNED, "y must be 16-byte aligned");
   return run_swiglu(x, w_gate_up, w_down, group_sizes, y, M, D, F, E, workspace, workspace_bytes,
                     static_cast<cudaStream_t>(stream));
+}
+
+// ------------------------------------------------------------------ training
+static int check_train_args(int64_t M, int32_t D, int32_t F, int32_t E) {
+  if (M < 0 || D <= 0 || F <= 0 || E <= 0)
+    return fail(MOE_ERR_INVALID_ARG, "bad sizes M=%lld D=%d F=%d E=%d", (long long)M, D, F, E);
+  if (E > 4096) return fail(MOE_ERR_UNSUPPORTED_SHAPE, "E=%d exceeds 4096", E);
+  if (M + 64LL * E > (int64_t)0x7fffffff) return fail(MOE_ERR_UNSUPPORTED_SHAPE, "M=%lld too large", (long long)M);
+  if (!train_supported(D, F))
+    return fail(MOE_ERR_UNSUPPORTED_SHAPE, "training entry points need D and F multiples of 256 (got D=%d F=%d)", D, F);
+  return 0;
+}
+
+size_t moe_fused_mlp_forward_train_workspace_size(int64_t M, int32_t D, int32_t F, int32_t E) {
+  if (M < 0 || E <= 0 || !train_supported(D, F)) return 0;
+  return large_ws_bytes(M, D, F, MOE_DTYPE_BF16);
+}
+
+int moe_fused_mlp_forward_train(const void* x, const void* w_up, const void* w_down, const int32_t* group_sizes,
+                                float* y, void* a_save, int64_t M, int32_t D, int32_t F, int32_t E, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  t_err[0] = 0;
+  if (int r = check_train_args(M, D, F, E)) return r;
+  if (M == 0) return 0;
+  if (!x || !w_up || !w_down || !group_sizes || !y || !a_save) return fail(MOE_ERR_INVALID_ARG, "null operand pointer");
+  if ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(a_save)) & 15u)
+    return fail(MOE_ERR_MISALIGNED, "y and a_save must be 16-byte aligned");
+  return run_train_forward(x, w_up, w_down, group_sizes, y, a_save, M, D, F, E, workspace, workspace_bytes,
+                           static_cast<cudaStream_t>(stream));
+}
+
+size_t moe_fused_mlp_backward_workspace_size(int64_t M, int32_t D, int32_t F, int32_t E) {
+  if (M < 0 || E <= 0 || E > 4096 || !train_supported(D, F)) return 0;
+  return bwd_ws_bytes(M, D, F, E);
+}
+
+int moe_fused_mlp_backward(const void* x, const void* w_up, const void* w_down, const int32_t* group_sizes,
+                           const void* a_saved, const void* dy, int32_t dy_dtype, float* dx, float* dw_up,
+                           float* dw_down, int64_t M, int32_t D, int32_t F, int32_t E, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  t_err[0] = 0;
+  if (int r = check_train_args(M, D, F, E)) return r;
+  if (dy_dtype != MOE_DTYPE_F32 && dy_dtype != MOE_DTYPE_BF16)
+    return fail(MOE_ERR_UNSUPPORTED_DTYPE, "dy_dtype %d (f32 or bf16)", dy_dtype);
+  if (!x || !w_up || !w_down || !group_sizes || !a_saved || !dy || !dx || !dw_up || !dw_down)
+    return fail(MOE_ERR_INVALID_ARG, "null operand pointer");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(a_saved) | reinterpret_cast<uintptr_t>(dy) |
+       reinterpret_cast<uintptr_t>(dx) | reinterpret_cast<uintptr_t>(dw_up) | reinterpret_cast<uintptr_t>(dw_down)) &
+      15u)
+    return fail(MOE_ERR_MISALIGNED, "operands must be 16-byte aligned");
+  return run_backward(x, w_up, w_down, group_sizes, a_saved, dy, dy_dtype, dx, dw_up, dw_down, M, D, F, E, workspace,
+                      workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"
