@@ -60,14 +60,43 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// Encoded maps of recent calls, per host thread: a map is a pure function of
+// (base, type, shape, box), so a hit skips the driver call.  Weights,
+// workspaces and reused activation buffers hit on repeated calls.
+struct MapKey {
+  const void* base;
+  uint64_t rows, cols;
+  uint32_t box_cols, box_rows;
+  int dt;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && rows == o.rows && cols == o.cols && box_cols == o.box_cols &&
+           box_rows == o.box_rows && dt == o.dt;
+  }
+};
+struct MapCacheEntry {
+  MapKey key;
+  CUtensorMap map;
+  bool valid;
+};
+constexpr int kMapCacheSlots = 64;
+static thread_local MapCacheEntry t_maps[kMapCacheSlots];
+
 // 2-D row-major tensor [rows, cols] with a {box_cols, box_rows} box and the
 // 128-byte swizzle; out-of-range elements read as zero.
 static int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int esz, uint64_t rows,
                        uint64_t cols, uint32_t box_cols, uint32_t box_rows) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
     return fail(MOE_ERR_MISALIGNED, "operand base %p is not 16-byte aligned", base);
+  const MapKey key{base, rows, cols, box_cols, box_rows, (int)dt};
+  const uint64_t h = (reinterpret_cast<uintptr_t>(base) >> 8) * 0x9E3779B97F4A7C15ull ^ rows * 0xC2B2AE3D27D4EB4Full ^
+                     cols * 0x165667B19E3779F9ull ^ ((uint64_t)box_cols << 20 | (uint64_t)box_rows << 8 | (uint64_t)dt);
+  MapCacheEntry& slot = t_maps[(h >> 40) % kMapCacheSlots];
+  if (slot.valid && slot.key == key) {
+    *map = slot.map;
+    return 0;
+  }
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {cols * (uint64_t)esz};
   cuuint32_t box[2] = {box_cols, box_rows};
@@ -78,12 +107,16 @@ static int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType d
   if (r != CUDA_SUCCESS)
     return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) rows=%llu cols=%llu box=%ux%u", (int)r,
                 (unsigned long long)rows, (unsigned long long)cols, box_cols, box_rows);
+  slot.key = key;
+  slot.map = *map;
+  slot.valid = true;
   return 0;
 }
 
 // ------------------------------------------------------------------ device info
 struct DevInfo {
   int sms = 0;
+  int* status = nullptr;  // device address of g_status on this device
   bool attr_set[40] = {};
   int pairs[24] = {};  // co-resident CTA pairs per pair-kernel variant (0 = not queried)
 };
@@ -104,6 +137,9 @@ static int device_info(int* dev_out, DevInfo** info) {
     if (major != 10 || minor != 0)
       return fail(MOE_ERR_CUDA, "device %d is sm_%d%d; this library is built for sm_100a only", dev, major,
                   minor);
+    int* status = nullptr;
+    MOE_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_status));
+    g_dev[dev].status = status;
     g_dev[dev].sms = sms;
   }
   *dev_out = dev;
@@ -115,23 +151,23 @@ static int device_info(int* dev_out, DevInfo** info) {
 // W (E, R, C) f32 -> hi/lo planes of W^T (E, C, R): hi = W rounded toward
 // zero to tf32, lo = W - hi.  32x32 tiles through shared memory so both the
 // read and the write are coalesced.
-__global__ void __launch_bounds__(256) split_transpose_kernel(const float* __restrict__ w, float* __restrict__ hi,
-                                                              float* __restrict__ lo, int R, int C) {
-  __shared__ float tile[32][33];
-  const int e = blockIdx.z;
-  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+// One 32x32 tile (rows r0.., columns c0.. of expert e) by 256 threads laid
+// out 32 x 8 (tx = column lane, ty = row group).
+__device__ __forceinline__ void split_transpose_tile(const float* __restrict__ w, float* __restrict__ hi,
+                                                     float* __restrict__ lo, int R, int C, int e, int c0, int r0,
+                                                     int tx, int ty, float (*tile)[33]) {
   const float* src = w + (size_t)e * R * C;
-  for (int i = threadIdx.y; i < 32; i += 8) {
-    const int r = r0 + i, c = c0 + threadIdx.x;
-    tile[i][threadIdx.x] = (r < R && c < C) ? src[(size_t)r * C + c] : 0.f;
+  for (int i = ty; i < 32; i += 8) {
+    const int r = r0 + i, c = c0 + tx;
+    tile[i][tx] = (r < R && c < C) ? src[(size_t)r * C + c] : 0.f;
   }
   __syncthreads();
   float* dh = hi + (size_t)e * R * C;
   float* dl = lo + (size_t)e * R * C;
-  for (int i = threadIdx.y; i < 32; i += 8) {
-    const int c = c0 + i, r = r0 + threadIdx.x;
+  for (int i = ty; i < 32; i += 8) {
+    const int c = c0 + i, r = r0 + tx;
     if (r < R && c < C) {
-      const float v = tile[threadIdx.x][i];
+      const float v = tile[tx][i];
       const float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
       dh[(size_t)c * R + r] = h;
       dl[(size_t)c * R + r] = v - h;
@@ -139,23 +175,67 @@ __global__ void __launch_bounds__(256) split_transpose_kernel(const float* __res
   }
 }
 
-// X (n floats) -> hi/lo planes, same layout.
-__global__ void __launch_bounds__(256) split_kernel(const float4* __restrict__ x, float4* __restrict__ hi,
-                                                    float4* __restrict__ lo, size_t n4) {
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
-    const float4 v = x[i];
-    float4 h, l;
-    h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-    h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-    h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-    h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
-    l.x = v.x - h.x;
-    l.y = v.y - h.y;
-    l.z = v.z - h.z;
-    l.w = v.w - h.w;
-    hi[i] = h;
-    lo[i] = l;
+__global__ void __launch_bounds__(256) split_transpose_kernel(const float* __restrict__ w, float* __restrict__ hi,
+                                                              float* __restrict__ lo, int R, int C) {
+  __shared__ float tile[32][33];
+  split_transpose_tile(w, hi, lo, R, C, blockIdx.z, blockIdx.x * 32, blockIdx.y * 32, threadIdx.x, threadIdx.y,
+                       tile);
+}
+
+__device__ __forceinline__ float4 tf32_hi4(float4 v) {
+  return make_float4(__uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u),
+                     __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u),
+                     __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u),
+                     __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u));
+}
+
+// Everything a small-D call does before the fused kernel, in one launch:
+// blocks [0, 2 w_blocks) split W_up and W_down into their tf32 planes (one
+// 32x32 tile each), the next x_blocks split X, the last y_blocks zero Y (for
+// the F-split grid, whose CTAs add into Y).  Unused segments have 0 blocks.
+struct PrepArgs {
+  const float* wu;
+  float *wu_hi, *wu_lo;  // W_up (E, D, F) -> planes (E, F, D)
+  const float* wd;
+  float *wd_hi, *wd_lo;  // W_down (E, F, D) -> planes (E, D, F)
+  int D, F, E;
+  int w_blocks;          // tiles per weight matrix
+  const float4* x;
+  float4 *x_hi, *x_lo;
+  size_t x_n4;
+  int x_blocks;
+  float4* y;
+  size_t y_n4;
+  int y_blocks;
+};
+
+__global__ void __launch_bounds__(256) small_prep_kernel(const PrepArgs a) {
+  __shared__ float tile[32][33];
+  int b = (int)blockIdx.x;
+  const int t = (int)threadIdx.x;
+  if (b < 2 * a.w_blocks) {
+    const bool down = b >= a.w_blocks;
+    if (down) b -= a.w_blocks;
+    const int R = down ? a.F : a.D, C = down ? a.D : a.F;
+    const int tc = (C + 31) / 32, tr = (R + 31) / 32;
+    const int e = b / (tr * tc), rem = b % (tr * tc);
+    split_transpose_tile(down ? a.wd : a.wu, down ? a.wd_hi : a.wu_hi, down ? a.wd_lo : a.wu_lo, R, C, e,
+                         (rem % tc) * 32, (rem / tc) * 32, t & 31, t >> 5, tile);
+    return;
   }
+  b -= 2 * a.w_blocks;
+  if (b < a.x_blocks) {
+    for (size_t i = (size_t)b * 256 + t; i < a.x_n4; i += (size_t)a.x_blocks * 256) {
+      const float4 v = a.x[i];
+      const float4 h = tf32_hi4(v);
+      a.x_hi[i] = h;
+      a.x_lo[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+    }
+    return;
+  }
+  b -= a.x_blocks;
+  for (size_t i = (size_t)b * 256 + t; i < a.y_n4; i += (size_t)a.y_blocks * 256)
+    a.y[i] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 // ------------------------------------------------------------------ large-D dispatch (two grouped GEMMs)
@@ -242,8 +322,7 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
   const bool fp8 = dtype == MOE_DTYPE_FP8_E4M3_BLK128;
   if (fp8 && (!w_up_scale || !w_down_scale))
     return fail(MOE_ERR_INVALID_ARG, "FP8 weights need w_up_scale and w_down_scale");
-  int* status = nullptr;
-  MOE_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_status));
+  int* status = di->status;
   const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const auto F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const auto U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
@@ -340,8 +419,7 @@ static int run_train_forward(const void* x, const void* w_up, const void* w_down
   const size_t need = large_ws_bytes(M, D, F, MOE_DTYPE_BF16);
   if (ws_bytes < need) return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", ws_bytes, need);
   if (reinterpret_cast<uintptr_t>(ws) & 255u) return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
-  int* status = nullptr;
-  MOE_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_status));
+  int* status = di->status;
   const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int ctas = (int)g_tune_ctas;
   GemmMaps m1;
@@ -368,8 +446,7 @@ static int run_backward(const void* x, const void* w_up, const void* w_down, con
   const size_t need = bwd_ws_bytes(M, D, F, E);
   if (ws_bytes < need) return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", ws_bytes, need);
   if (reinterpret_cast<uintptr_t>(ws) & 255u) return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
-  int* status = nullptr;
-  MOE_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_status));
+  int* status = di->status;
   const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int ctas = (int)g_tune_ctas;
   const int64_t mp = bwd_padded_rows(M, E);
@@ -441,8 +518,7 @@ static int run_swiglu(const void* x, const void* w_gu, const void* w_down, const
   const size_t need = align256((size_t)M * F * 2);
   if (ws_bytes < need) return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", ws_bytes, need);
   if (reinterpret_cast<uintptr_t>(ws) & 255u) return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
-  int* status = nullptr;
-  MOE_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_status));
+  int* status = di->status;
   const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int ctas = (int)g_tune_ctas;
   // up: H = SiLU(X @ W_gate[e]) * (X @ W_up[e]) over the interleaved (E*D, 2F) weights
@@ -577,9 +653,11 @@ static int launch_pair(const FusedMaps& maps, const FusedParams& prm, int pairs_
   return 0;
 }
 
+// `split_weights`: the 3xTF32 weight planes are built by this call's
+// preparation launch (raw f32 weights); otherwise they are already in `ws`.
 static int run_small(const void* x, const void* w_up, const void* w_down, const int32_t* gs, float* y, int64_t M,
                      int D, int F, int E, int dtype, void* ws, size_t ws_bytes, cudaStream_t st,
-                     RunOpts opt = RunOpts()) {
+                     RunOpts opt = RunOpts(), bool split_weights = false) {
   int dev;
   DevInfo* di;
   if (int r = device_info(&dev, &di)) return r;
@@ -608,8 +686,7 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
   const int ctas_req = opt.ctas > 0 ? opt.ctas : (int)g_tune_ctas;
   int ctas = ctas_req > 0 && ctas_req < di->sms ? ctas_req : di->sms;
 
-  int* status = nullptr;
-  MOE_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_status));
+  int* status = di->status;
 
   FusedParams prm{};
   prm.group_sizes = gs;
@@ -626,7 +703,48 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
 
   FusedMaps maps;
   memset(&maps, 0, sizeof(maps));
-  if (splits > 1) MOE_CUDA_TRY(cudaMemsetAsync(y, 0, (size_t)M * D * sizeof(float), st));
+  const size_t wsz = (size_t)E * D * F;
+  float* wu_hi = static_cast<float*>(ws);
+  float* wu_lo = wu_hi + wsz;
+  float* wd_hi = wu_lo + wsz;
+  float* wd_lo = wd_hi + wsz;
+  float* x_hi = wd_lo + wsz;
+  float* x_lo = x_hi + (size_t)M * D;
+  const bool f32 = dtype == MOE_DTYPE_F32;
+  {
+    // One preparation launch for what this call needs before the fused kernel.
+    PrepArgs pa{};
+    const int cap = di->sms * 4;
+    if (f32 && split_weights) {
+      pa.wu = static_cast<const float*>(w_up);
+      pa.wd = static_cast<const float*>(w_down);
+      pa.wu_hi = wu_hi;
+      pa.wu_lo = wu_lo;
+      pa.wd_hi = wd_hi;
+      pa.wd_lo = wd_lo;
+      pa.D = D;
+      pa.F = F;
+      pa.E = E;
+      pa.w_blocks = E * ((D + 31) / 32) * ((F + 31) / 32);
+    }
+    if (f32 && !pair && !plan.x_res) {
+      pa.x = static_cast<const float4*>(x);
+      pa.x_hi = reinterpret_cast<float4*>(x_hi);
+      pa.x_lo = reinterpret_cast<float4*>(x_lo);
+      pa.x_n4 = (size_t)M * D / 4;
+      pa.x_blocks = (int)std::min<size_t>((pa.x_n4 + 255) / 256, (size_t)cap);
+    }
+    if (splits > 1) {
+      pa.y = reinterpret_cast<float4*>(y);
+      pa.y_n4 = (size_t)M * D / 4;
+      pa.y_blocks = (int)std::min<size_t>((pa.y_n4 + 255) / 256, (size_t)cap);
+    }
+    const int blocks = 2 * pa.w_blocks + pa.x_blocks + pa.y_blocks;
+    if (blocks > 0) {
+      small_prep_kernel<<<blocks, 256, 0, st>>>(pa);
+      MOE_CUDA_TRY(cudaGetLastError());
+    }
+  }
 
   if (dtype == MOE_DTYPE_BF16) {
     const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -647,11 +765,6 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
   }
 
   const auto F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-  const size_t wsz = (size_t)E * D * F;
-  float* wu_hi = static_cast<float*>(ws);
-  float* wu_lo = wu_hi + wsz;
-  float* wd_hi = wu_lo + wsz;
-  float* wd_lo = wd_hi + wsz;
   if (int r = make_map_2d(&maps.wu[0], wu_hi, F32, 4, (uint64_t)E * F, D, 32, plan.bf)) return r;
   if (int r = make_map_2d(&maps.wu[1], wu_lo, F32, 4, (uint64_t)E * F, D, 32, plan.bf)) return r;
   const uint32_t wd_box_rows = pair ? D / 2 : D;
@@ -666,13 +779,6 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
   if (plan.x_res) {
     if (int r = make_map_2d(&maps.x[0], x, F32, 4, (uint64_t)M, D, 32, 128)) return r;
   } else {
-    float* x_hi = wd_lo + wsz;
-    float* x_lo = x_hi + (size_t)M * D;
-    const size_t n4 = (size_t)M * D / 4;
-    const int blocks = (int)std::min<size_t>((n4 + 255) / 256, (size_t)di->sms * 8);
-    split_kernel<<<blocks, 256, 0, st>>>(static_cast<const float4*>(x), reinterpret_cast<float4*>(x_hi),
-                                         reinterpret_cast<float4*>(x_lo), n4);
-    MOE_CUDA_TRY(cudaGetLastError());
     if (int r = make_map_2d(&maps.x[0], x_hi, F32, 4, (uint64_t)M, D, 32, 128)) return r;
     if (int r = make_map_2d(&maps.x[1], x_lo, F32, 4, (uint64_t)M, D, 32, 128)) return r;
   }
@@ -910,8 +1016,8 @@ int moe_fused_mlp(const void* x, const void* w_up, const void* w_down, const int
   if (!small_supported(D, F, dtype))
     return run_large(x, w_up, w_down, group_sizes, w_up_scale, w_down_scale, y, M, D, F, E, dtype, workspace,
                      workspace_bytes, st);
-  if (int r = prepare_small(w_up, w_down, D, F, E, dtype, workspace, workspace_bytes, st)) return r;
-  return run_small(x, w_up, w_down, group_sizes, y, M, D, F, E, dtype, workspace, workspace_bytes, st);
+  return run_small(x, w_up, w_down, group_sizes, y, M, D, F, E, dtype, workspace, workspace_bytes, st, RunOpts(),
+                   true);
 }
 
 int moe_fused_mlp_noalloc(const float* x, const float* w_up, const float* w_down, const int32_t* group_sizes,
@@ -932,8 +1038,8 @@ int moe_fused_mlp_noalloc(const float* x, const float* w_up, const float* w_down
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // Every scratch byte the fused kernel reads is written by the weight split
   // earlier in this same call, so nothing needs clearing between calls.
-  if (int r = prepare_small(w_up, w_down, D, F, E, MOE_DTYPE_F32, scratch, kNoAllocScratchBytes, st)) return r;
-  return run_small(x, w_up, w_down, group_sizes, y, M, D, F, E, MOE_DTYPE_F32, scratch, kNoAllocScratchBytes, st);
+  return run_small(x, w_up, w_down, group_sizes, y, M, D, F, E, MOE_DTYPE_F32, scratch, kNoAllocScratchBytes, st,
+                   RunOpts(), true);
 }
 
 // ------------------------------------------------------------------ expert-parallel engine
@@ -1322,12 +1428,11 @@ int moe_permute(const int32_t* expert_ids, int64_t N, int32_t E, int32_t* group_
   const size_t need = moe_permute_workspace_size(N, E);
   if (workspace_bytes < need || !workspace)
     return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", workspace_bytes, need);
-  int* status = nullptr;
-  MOE_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_status));
   static bool attr_done[64] = {};
   int dev;
   DevInfo* di;
   if (int r = device_info(&dev, &di)) return r;
+  int* status = di->status;
   const size_t smem_scatter = (size_t)(kPermBlock / 32) * E * sizeof(int);
   if (!attr_done[dev]) {
     MOE_CUDA_TRY(cudaFuncSetAttribute(perm_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

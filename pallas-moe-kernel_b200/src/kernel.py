@@ -64,10 +64,45 @@ def workspace_size(M: int, D: int, F: int, E: int, dtype_code: int) -> int:
 
 
 def _as_device_group_sizes(group_sizes, device) -> torch.Tensor:
+    if (isinstance(group_sizes, torch.Tensor) and group_sizes.dtype == torch.int32
+            and group_sizes.device == device and group_sizes.is_contiguous()):
+        return group_sizes
     if not isinstance(group_sizes, torch.Tensor):
         group_sizes = torch.as_tensor(group_sizes)
     gs = group_sizes.to(device=device, dtype=torch.int32, non_blocking=True)
     return gs.contiguous()
+
+
+_WORKSPACES: dict = {}
+_WS_SIZES: dict = {}
+
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _stream_handle(dev: torch.device) -> int:
+    """cudaStream_t of torch's current stream on ``dev``."""
+    if _raw_stream is not None:
+        return _raw_stream(dev.index)
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+_WORKSPACE_CACHE_MAX = 64 << 20
+
+
+def _stream_workspace(dev: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    """A workspace of at least ``nbytes`` shared by the calls on one stream
+    (they run in stream order, so none overlaps another's use of it); small
+    calls are dominated by host time, and this saves an allocation each.
+    Workspaces above 64 MiB, and every call while a CUDA graph is being
+    captured (the graph's memory pool), get a fresh allocation."""
+    if nbytes > _WORKSPACE_CACHE_MAX or torch.cuda.is_current_stream_capturing():
+        return torch.empty(nbytes, device=dev, dtype=torch.uint8)
+    key = (dev.index, stream)
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(nbytes, device=dev, dtype=torch.uint8)
+        _WORKSPACES[key] = ws
+    return ws
 
 
 def fused_ragged_mlp(x: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor, group_sizes,
@@ -111,19 +146,25 @@ def fused_ragged_mlp(x: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor, 
         out = torch.empty((M, D), device=dev, dtype=torch.float32)
     elif out.shape != (M, D) or out.dtype != torch.float32 or not out.is_contiguous():
         raise ValueError("out must be a contiguous (M, D) float32 tensor")
-    ws_bytes = workspace_size(M, D, F, E, code)
+    L = _lib.lib()
+    key = (M, D, F, E, code)
+    ws_bytes = _WS_SIZES.get(key)
+    if ws_bytes is None:
+        if len(_WS_SIZES) > 4096:
+            _WS_SIZES.clear()
+        ws_bytes = _WS_SIZES.setdefault(key, int(L.moe_fused_mlp_workspace_size(M, D, F, E, code)))
+    stream = _stream_handle(dev)
     if ws_bytes and (workspace is None or workspace.numel() * workspace.element_size() < ws_bytes):
-        workspace = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
-    stream = torch.cuda.current_stream(dev).cuda_stream
-    with torch.cuda.device(dev):
-        rc = _lib.lib().moe_fused_mlp(
-            ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(w_up.data_ptr()),
-            ctypes.c_void_p(w_down.data_ptr()), ctypes.c_void_p(gs.data_ptr()),
-            ctypes.c_void_p(w_up_scale.data_ptr() if w_up_scale is not None else 0),
-            ctypes.c_void_p(w_down_scale.data_ptr() if w_down_scale is not None else 0),
-            ctypes.c_void_p(out.data_ptr()), M, D, F, E, code,
-            ctypes.c_void_p(workspace.data_ptr() if ws_bytes else 0), ws_bytes,
-            ctypes.c_void_p(stream))
+        workspace = _stream_workspace(dev, stream, ws_bytes)
+    args = (x.data_ptr(), w_up.data_ptr(), w_down.data_ptr(), gs.data_ptr(),
+            w_up_scale.data_ptr() if w_up_scale is not None else None,
+            w_down_scale.data_ptr() if w_down_scale is not None else None,
+            out.data_ptr(), M, D, F, E, code, workspace.data_ptr() if ws_bytes else None, ws_bytes, stream)
+    if dev.index == torch.cuda.current_device():
+        rc = L.moe_fused_mlp(*args)
+    else:
+        with torch.cuda.device(dev):
+            rc = L.moe_fused_mlp(*args)
     _lib.check(rc)
     return out
 
@@ -232,15 +273,17 @@ class PreparedExperts:
         gs = _as_device_group_sizes(group_sizes, dev)
         if out is None:
             out = torch.empty((M, D), device=dev, dtype=torch.float32)
-        stream = torch.cuda.current_stream(dev).cuda_stream
-        with torch.cuda.device(dev):
-            rc = _lib.lib().moe_fused_mlp_prepared(
-                ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(self.w_up.data_ptr()),
-                ctypes.c_void_p(self.w_down.data_ptr()), ctypes.c_void_p(gs.data_ptr()),
-                ctypes.c_void_p(self.w_up_scale.data_ptr() if self.w_up_scale is not None else 0),
-                ctypes.c_void_p(self.w_down_scale.data_ptr() if self.w_down_scale is not None else 0),
-                ctypes.c_void_p(out.data_ptr()), M, self.D, self.F, self.E, self.dtype_code,
-                ctypes.c_void_p(self.workspace.data_ptr()), self.ws_bytes, ctypes.c_void_p(stream))
+        stream = _stream_handle(dev)
+        args = (x.data_ptr(), self.w_up.data_ptr(), self.w_down.data_ptr(), gs.data_ptr(),
+                self.w_up_scale.data_ptr() if self.w_up_scale is not None else None,
+                self.w_down_scale.data_ptr() if self.w_down_scale is not None else None,
+                out.data_ptr(), M, self.D, self.F, self.E, self.dtype_code, self.workspace.data_ptr(),
+                self.ws_bytes, stream)
+        if dev.index == torch.cuda.current_device():
+            rc = _lib.lib().moe_fused_mlp_prepared(*args)
+        else:
+            with torch.cuda.device(dev):
+                rc = _lib.lib().moe_fused_mlp_prepared(*args)
         _lib.check(rc)
         return out
 
