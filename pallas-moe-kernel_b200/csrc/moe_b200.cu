@@ -677,11 +677,17 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
     if (nch_total % splits != 0)
       return fail(MOE_ERR_INVALID_ARG, "tuning splits=%d does not divide %d chunks", splits, nch_total);
   } else {
-    // Enough units for every SM (or SM pair) while each unit keeps >= 1 chunk.
+    // The most F-splits that still fit the (expert, row-block) units in one
+    // wave of SMs (or SM pairs): a second wave of shorter units costs more
+    // than it balances (measured on B200 over M = 128 ... 131072, D = 64 ...
+    // 256, E = 4 ... 16, f32 and bf16).  Row blocks are estimated from M; at
+    // small M every expert is taken to hold a partial block of its own.
     const int rows_per_unit = pair ? 256 : 128;
     const int64_t workers = pair ? di->sms / 2 : di->sms;
-    const int64_t blocks_est = (M + rows_per_unit - 1) / rows_per_unit;
-    while (blocks_est * splits < workers && nch_total % (splits * 2) == 0 && splits * 2 <= nch_total) splits *= 2;
+    const int64_t blocks_est =
+        std::max<int64_t>((M + rows_per_unit - 1) / rows_per_unit, std::min<int64_t>(E, (M + 15) / 16));
+    while (blocks_est * splits * 2 <= workers && nch_total % (splits * 2) == 0 && splits * 2 <= nch_total)
+      splits *= 2;
   }
   const int ctas_req = opt.ctas > 0 ? opt.ctas : (int)g_tune_ctas;
   int ctas = ctas_req > 0 && ctas_req < di->sms ? ctas_req : di->sms;
