@@ -104,6 +104,25 @@ struct EpArgs {
   int* status;
 };
 
+// Scatter mode with the dispatch fused into the up GEMM: the GEMM's dispatch
+// warps store this rank's rows of the other owners' experts into their X
+// landing regions (the owner's own rows are copied before the GEMM), and its
+// TMA producer waits, per tile, for the sources whose rows the tile reads.
+struct EpDispatch {
+  uint8_t* base[kEpMaxWorld];  // every rank's symmetric buffer
+  const uint8_t* x;            // this rank's X (rows sorted by global expert)
+  size_t off_x;                // byte offset of the X landing region (wave 0)
+  const EpSlice* slices;       // [E] this rank's slices (wave 0)
+  const int* wave_rows;        // [E + 1] row prefix of the slices
+  const int4* recv;            // [el][world] {first region row, rows, first source row, source}
+  const uint32_t* data_flags;  // this rank's flags data[0][s]
+  unsigned* push_ctr;          // CTAs of the GEMM done with their dispatch rows
+  int* abort_word;
+  int E, rank, world, row_bytes;
+  uint32_t epoch;
+  int on;
+};
+
 // ---------------------------------------------------------------- primitives
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
@@ -301,11 +320,15 @@ __global__ void __launch_bounds__(1024) ep_counts_kernel(const __grid_constant__
     }
   }
   __syncthreads();
-  // This rank's slices: inside the owner's region, sources in rank order.
+  // This rank's slices: inside the owner's region, sources in rank order
+  // starting at the owner itself (owner o: o, o + 1, ..., o - 1 mod world),
+  // so that an owner's own rows lead each of its experts -- the up GEMM can
+  // start on them before any peer's rows have landed.
   for (int i = tid; i < V * E; i += blockDim.x) {
     const int v = i / E, g = i - v * E;
+    const int o = g / EL;
     int before = 0;
-    for (int s = 0; s < a.rank; ++s) {
+    for (int k = 0, s = o; s != a.rank; ++k, s = (s + 1 == W ? 0 : s + 1)) {
       const int c = s_cnt[s * E + g];
       before += wave_cut(c, v + 1, V) - wave_cut(c, v, V);
     }
@@ -331,7 +354,7 @@ __global__ void __launch_bounds__(1024) ep_counts_kernel(const __grid_constant__
       const int g = a.rank * EL + e;
       int start = 0;
       for (int e2 = 0; e2 < e; ++e2) start += a.local_gs[e2];
-      for (int s2 = 0; s2 < sr; ++s2) start += s_cnt[s2 * E + g];
+      for (int s2 = a.rank; s2 != sr; s2 = (s2 + 1 == W ? 0 : s2 + 1)) start += s_cnt[s2 * E + g];
       int n = s_cnt[sr * E + g];
       if (start + n > a.region_cap) n = max(0, a.region_cap - start);
       a.recv[i] = make_int4(start, n, s_src[sr * E + g], sr);
@@ -360,7 +383,9 @@ __device__ __forceinline__ int ep_find_slice(const int* wr, int E, int row) {
 }
 
 // Stores this rank's rows of wave v into the owners' X landing regions.
-__global__ void __launch_bounds__(1024) ep_push_kernel(const __grid_constant__ EpArgs a, int v) {
+// `local_only`: copy only the slices this rank owns itself and raise no
+// flags (the rest is pushed by the up GEMM's dispatch warps).
+__global__ void __launch_bounds__(1024) ep_push_kernel(const __grid_constant__ EpArgs a, int v, int local_only) {
   __shared__ int s_wr[kEpMaxExperts + 1];
   __shared__ bool s_last;
   const int E = a.E;
@@ -375,12 +400,14 @@ __global__ void __launch_bounds__(1024) ep_push_kernel(const __grid_constant__ E
     for (int row = (int)(blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)); row < rows; row += warps) {
       const int g = ep_find_slice(s_wr, E, row);
       const EpSlice sl = a.slices[(size_t)v * E + g];
+      if (local_only && sl.owner != a.rank) continue;
       const int r = row - s_wr[g];
       const uint8_t* src = a.x + (size_t)(sl.src_row + r) * a.row_bytes_x;
       uint8_t* dst = a.base[sl.owner] + a.off_x + (size_t)v * a.region_x_bytes + (size_t)(sl.dst_row + r) * a.row_bytes_x;
       warp_copy_row(dst, src, a.row_bytes_x, lane);
     }
   }
+  if (local_only) return;
   __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {

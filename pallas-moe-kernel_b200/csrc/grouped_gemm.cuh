@@ -24,6 +24,7 @@
 // (e4m3 x 128x128 block scale -> f16; X and H are f16 too) into the MMA's
 // operand layout.
 #pragma once
+#include "ep_exchange.cuh"
 #include "fused_small.cuh"
 
 namespace moe {
@@ -55,6 +56,7 @@ struct GemmParams {
   int skip_tail;         // 1: leave rows at or past sum(group_sizes) unwritten (Y only)
   EpScatter scatter;     // Y only: rows go to their source ranks (expert parallelism)
   void* out2;            // EPI 3: the pre-activation X W_up (bf16, [M, N]) saved for the backward
+  EpDispatch dispatch;   // EPI 0, bf16: expert-parallel dispatch fused into the up GEMM
 };
 
 // store_y_block with one destination row pointer per row: lane l of the warp
@@ -102,14 +104,18 @@ struct GemmCfg {
   static constexpr int CVT_WARPS = BFP8 ? 8 : 0;  // two per SM sub-partition
   static constexpr int OUT_STAGE = EPI_WARPS * 32 * 128;  // 4 KB per warp: 32 rows x 128 B
   static constexpr int BAR_BYTES = BFP8 ? 512 : 256;
-  static constexpr int SMEM = 1024 + NS * STAGE + NR * B8_BYTES + OUT_STAGE + BAR_BYTES;
+  // bf16 up GEMM: four warps that run the expert-parallel dispatch (idle
+  // otherwise), with the slice row prefix in shared memory.
+  static constexpr int PUSH_WARPS = (EPI == 0 && !BFP8) ? 4 : 0;
+  static constexpr int PUSH_SMEM = PUSH_WARPS ? (kEpMaxExperts + 1) * 4 : 0;
+  static constexpr int SMEM = 1024 + NS * STAGE + NR * B8_BYTES + OUT_STAGE + BAR_BYTES + PUSH_SMEM;
   static constexpr int TMEM_COLS = 512;                 // 2 accumulators x 256 columns
   // e4m3 weights run as f16 operands (f16 X, f16 H, f16 dequantised B).
   static constexpr uint32_t IDESC = make_idesc(BFP8 ? kFmtF16 : kFmtBF16, 256, BN, 0, 1);
   static constexpr uint32_t TX = 2 * (A_BYTES + B_BYTES);  // both CTAs (bf16 B)
   static constexpr uint32_t TX_A = 2 * A_BYTES;            // both CTAs' A (FP8 B arrives converted)
   static constexpr int RAW_WARP = 2 + EPI_WARPS + CVT_WARPS;  // FP8: producer of the raw ring
-  static constexpr int THREADS = 64 + (EPI_WARPS + CVT_WARPS) * 32 + (BFP8 ? 32 : 0);
+  static constexpr int THREADS = 64 + (EPI_WARPS + CVT_WARPS + PUSH_WARPS) * 32 + (BFP8 ? 32 : 0);
   // Register cap: that of a 320-thread block at least (the bf16 epilogue
   // was scheduled under it), or of the FP8 block with its extra warps.
   static constexpr int LAUNCH_BOUND = THREADS > 320 ? THREADS : 320;
@@ -212,6 +218,7 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
   uint64_t* raw_empty = raw_full + C::NR; // [NR] local: converters done with the raw tile
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(raw_empty + C::NR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* push_wr = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);  // PUSH_WARPS only
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -263,6 +270,7 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
       uint32_t phase = 0;
       const uint64_t pol_a = l2_policy_evict_last();
       const uint64_t pol_b = l2_policy_evict_last();
+      uint32_t arrived = 0;  // dispatch: sources whose rows have landed here
       for (int t = pair;; t += npairs) {
         if (!cur.seek(t, p.group_sizes, p.E, p.M, nt)) break;
         int mb, nb;
@@ -271,6 +279,34 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
         const int n0 = nb * C::BN + (int)rank * (C::BN / 2);
         const int brow0 = cur.e * p.k_rows_per_e;
         bool ok = true;
+        if (C::PUSH_WARPS > 0 && p.dispatch.on) {
+          // Wait for every peer whose rows of this expert meet this CTA's 128
+          // rows (a peer's flag covers all its rows of this step), then order
+          // the TMA reads after the peer's stores.
+          const EpDispatch& d = p.dispatch;
+          for (int s = 0; s < d.world && ok; ++s) {
+            if (s == d.rank || (arrived >> s) & 1u) continue;
+            const int4 rc = d.recv[cur.e * d.world + s];
+            if (rc.y <= 0 || rc.x >= row0 + C::BM || rc.x + rc.y <= row0) continue;
+            const uint64_t t0 = global_timer_ns();
+            while (!epoch_reached(ld_acquire_sys(d.data_flags + s), d.epoch)) {
+              if (*reinterpret_cast<volatile int*>(d.abort_word) || *abort_flag) {
+                ok = false;
+                break;
+              }
+              if (global_timer_ns() - t0 > kEpWaitLimitNs) {
+                atomicOr(p.status, kStatusPeerTimeout);
+                atomicExch(d.abort_word, 1);
+                *abort_flag = 1;
+                ok = false;
+                break;
+              }
+            }
+            arrived |= 1u << s;
+          }
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          if (!ok) break;
+        }
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(empty + stage, phase ^ 1u, abort_flag, p.status)) {
             ok = false;
@@ -432,6 +468,48 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
         }
       }
       gk += (uint32_t)nk;
+    }
+  } else if (C::PUSH_WARPS > 0 && warp >= 2u + C::EPI_WARPS) {
+    // ------------------------------------------------------------ expert-parallel dispatch (both CTAs)
+    // This rank's rows of the other owners' experts go straight into their
+    // X landing regions while the tensor cores work on the rows already here.
+    if (p.dispatch.on) {
+      const EpDispatch& d = p.dispatch;
+      const int pt = (int)threadIdx.x - 64 - C::EPI_WARPS * 32;  // 0 .. 32 * PUSH_WARPS - 1
+      constexpr int kPushThreads = C::PUSH_WARPS * 32;
+      for (int g = pt; g <= d.E; g += kPushThreads) push_wr[g] = d.wave_rows[g];
+      asm volatile("bar.sync 1, %0;" ::"n"(kPushThreads) : "memory");
+      const int gw = (int)blockIdx.x * C::PUSH_WARPS + (pt >> 5);
+      const int nw = (int)gridDim.x * C::PUSH_WARPS;
+      const int rows = push_wr[d.E];
+      if (*reinterpret_cast<volatile int*>(d.abort_word) == 0) {
+        for (int row = gw; row < rows; row += nw) {
+          const int g = ep_find_slice(push_wr, d.E, row);
+          const EpSlice sl = d.slices[g];
+          if (sl.owner == d.rank) continue;
+          const int r = row - push_wr[g];
+          warp_copy_row(d.base[sl.owner] + d.off_x + (size_t)(sl.dst_row + r) * d.row_bytes,
+                        d.x + (size_t)(sl.src_row + r) * d.row_bytes, d.row_bytes, (int)lane);
+        }
+      }
+      __threadfence_system();
+      asm volatile("bar.sync 1, %0;" ::"n"(kPushThreads) : "memory");
+      if (pt == 0) {
+        unsigned prev;
+        asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(d.push_ctr) : "memory");
+        if (prev == gridDim.x - 1) {
+          // Last CTA: every row of this rank has left; tell the owners (an
+          // aborted engine tells nobody, so its peers time out instead).
+          *d.push_ctr = 0;
+          __threadfence_system();
+          if (*reinterpret_cast<volatile int*>(d.abort_word) == 0)
+            for (int s = 0; s < d.world; ++s)
+              if (s != d.rank)
+                st_release_sys(reinterpret_cast<uint32_t*>(d.base[s]) +
+                                   (d.data_flags - reinterpret_cast<const uint32_t*>(d.base[d.rank])) + d.rank,
+                               d.epoch);
+        }
+      }
     }
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)

@@ -307,6 +307,7 @@ struct RunOpts {
   int ctas = 0;
   bool skip_tail = false;
   const EpScatter* scatter = nullptr;  // large-D path: rows of Y go to their source ranks
+  const EpDispatch* dispatch = nullptr;  // large-D bf16 path: the token dispatch runs inside the up GEMM
 };
 
 static int run_large(const void* x, const void* w_up, const void* w_down, const int32_t* gs,
@@ -348,6 +349,7 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
     if (int r = make_map_2d(&m1.b, w_up, BF16, 2, (uint64_t)E * D, F, 64, 64)) return r;
   }
   GemmParams p1{gs, ws, (int)M, E, F, D, D, 8, status, w_up_scale, 0};
+  if (opt.dispatch && !fp8) p1.dispatch = *opt.dispatch;
   if (int r = fp8 ? launch_gemm<0, true>(m1, p1, di, st, ctas) : launch_gemm<0, false>(m1, p1, di, st, ctas))
     return r;
   // down: Y = H @ W_down[e]
@@ -1303,6 +1305,58 @@ int moe_ep_forward(moe_ep_t ep, const void* x, const int32_t* group_sizes, float
   MOE_CUDA_TRY(cudaStreamWaitEvent(ep->comm, ep->ev_start, 0));
   ep_counts_kernel<<<1, 1024, ep_counts_smem(ep->world, ep->E, ep->waves), ep->comm>>>(a);
   MOE_CUDA_TRY(cudaGetLastError());
+  RunOpts opt;
+  opt.ctas = ep->mlp_ctas;
+  opt.skip_tail = true;
+  if (ep->scatter && ep->dtype == MOE_DTYPE_BF16) {
+    // bf16 two-GEMM experts: the owner's own rows are copied into its landing
+    // region first (they lead every expert's rows), then the up GEMM starts at
+    // once: its dispatch warps push this rank's rows to the other owners while
+    // its producer waits, tile by tile, only for the peers whose rows the tile
+    // reads.  The down GEMM stores each Y row into its source's landing area.
+    int dev;
+    DevInfo* di;
+    if (int r = device_info(&dev, &di)) return r;
+    MOE_CUDA_TRY(cudaEventRecord(ep->ev_push[0], ep->comm));
+    MOE_CUDA_TRY(cudaStreamWaitEvent(st, ep->ev_push[0], 0));
+    ep_push_kernel<<<di->sms, 1024, 0, st>>>(a, 0, 1);
+    MOE_CUDA_TRY(cudaGetLastError());
+    EpDispatch dp;
+    memset(&dp, 0, sizeof(dp));
+    for (int s2 = 0; s2 < ep->world; ++s2) dp.base[s2] = ep->peer[s2];
+    dp.x = static_cast<const uint8_t*>(x);
+    dp.off_x = ep->off_x;
+    dp.slices = ep->slices;
+    dp.wave_rows = ep->wave_rows;
+    dp.recv = ep->recv;
+    dp.data_flags = reinterpret_cast<EpFlags*>(ep->buf)->data[0];
+    dp.push_ctr = ep->push_ctr;
+    dp.abort_word = ep->abort_word;
+    dp.E = ep->E;
+    dp.rank = ep->rank;
+    dp.world = ep->world;
+    dp.row_bytes = a.row_bytes_x;
+    dp.epoch = a.epoch;
+    dp.on = 1;
+    opt.dispatch = &dp;
+    EpScatter sc;
+    memset(&sc, 0, sizeof(sc));
+    for (int s2 = 0; s2 < ep->world; ++s2) sc.base[s2] = ep->peer[s2];
+    sc.off = ep->off_yl;
+    sc.recv = ep->recv;
+    sc.world = ep->world;
+    sc.on = 1;
+    opt.scatter = &sc;
+    float* yl = reinterpret_cast<float*>(ep->buf + ep->off_yl);
+    if (int r = run_large(ep->buf + ep->off_x, ep->w_up, ep->w_down, ep->local_gs, ep->w_up_scale, ep->w_down_scale,
+                          yl, ep->region_cap, ep->D, ep->F, ep->el, ep->dtype, ep->ws, ep->ws_bytes, st, opt))
+      return r;
+    ep_ydone_kernel<<<1, 32, 0, st>>>(a);
+    MOE_CUDA_TRY(cudaGetLastError());
+    ep_finish_kernel<<<di->sms, 1024, 0, st>>>(a);
+    MOE_CUDA_TRY(cudaGetLastError());
+    return 0;
+  }
   // In scatter mode the push runs before the experts, alone: it gets every SM.
   int push_ctas = ep->comm_ctas;
   if (ep->scatter) {
@@ -1312,13 +1366,10 @@ int moe_ep_forward(moe_ep_t ep, const void* x, const int32_t* group_sizes, float
     push_ctas = di->sms;
   }
   for (int v = 0; v < ep->waves; ++v) {
-    ep_push_kernel<<<push_ctas, 1024, 0, ep->comm>>>(a, v);
+    ep_push_kernel<<<push_ctas, 1024, 0, ep->comm>>>(a, v, 0);
     MOE_CUDA_TRY(cudaGetLastError());
     MOE_CUDA_TRY(cudaEventRecord(ep->ev_push[v], ep->comm));
   }
-  RunOpts opt;
-  opt.ctas = ep->mlp_ctas;
-  opt.skip_tail = true;
   if (ep->scatter) {
     // One wave: land every row, run both GEMMs on every SM with the down
     // GEMM storing each Y row straight into its source's landing area, tell
@@ -1374,6 +1425,8 @@ int moe_ep_forward(moe_ep_t ep, const void* x, const int32_t* group_sizes, float
 
 int moe_ep_launches_per_forward(moe_ep_t ep) {
   if (!ep) return fail(MOE_ERR_INVALID_ARG, "null engine");
+  if (ep->scatter && ep->dtype == MOE_DTYPE_BF16)
+    return 2 + ep_mlp_launches(ep) + 2;  // counts, local copy, GEMMs (dispatch inside the up GEMM), ydone, finish
   if (ep->scatter) return 3 + ep_mlp_launches(ep) + 2;  // counts, push, wait, GEMMs, ydone, finish
   return 1 + ep->waves * (3 + ep_mlp_launches(ep));
 }
