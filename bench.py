@@ -217,7 +217,8 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
 
         def kern_fn():  # the dominant kernel alone (weights already prepared)
             return experts(x, gs_dev, out=y)
-        launches_per_step = (3 if cfg.dtype == "f32" else 1) if cfg.D <= 256 else (3 if cfg.dtype == "fp8" else 2)
+        code = {"f32": _lib.MOE_DTYPE_F32, "bf16": _lib.MOE_DTYPE_BF16, "fp8": _lib.MOE_DTYPE_FP8_E4M3_BLK128}[cfg.dtype]
+        launches_per_step = _lib.lib().moe_fused_mlp_launch_count(cfg.M, cfg.D, cfg.F, cfg.E, code)
 
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)

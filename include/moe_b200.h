@@ -76,6 +76,10 @@ int moe_fused_mlp(const void* x, const void* w_up, const void* w_down, const int
 
 /* Scratch bytes moe_fused_mlp needs for this problem (0 when none). */
 size_t moe_fused_mlp_workspace_size(int64_t M, int32_t D, int32_t F, int32_t E, int32_t dtype);
+/* Number of kernel launches one moe_fused_mlp call with these arguments makes
+ * on the current device under the current tuning (0 for M == 0), or a
+ * negative MOE_ERR_* code.  Host-side: launches nothing. */
+int moe_fused_mlp_launch_count(int64_t M, int32_t D, int32_t F, int32_t E, int32_t dtype);
 
 /*
  * Two-stage form of moe_fused_mlp for weights that stay fixed across calls

@@ -655,6 +655,23 @@ static int launch_pair(const FusedMaps& maps, const FusedParams& prm, int pairs_
   return 0;
 }
 
+// F-splits of a small-D call: the tuning value if set, else the most splits
+// that still fit the (expert, row-block) units in one wave of SMs (or SM
+// pairs) -- a second wave of shorter units costs more than it balances
+// (measured on B200 over M = 128 ... 131072, D = 64 ... 256, E = 4 ... 16,
+// f32 and bf16).  Row blocks are estimated from M; at small M every expert is
+// taken to hold a partial block of its own.
+static int small_splits(int64_t M, int E, int nch_total, bool pair, const DevInfo* di) {
+  if (g_tune_splits > 0) return (int)g_tune_splits;
+  const int rows_per_unit = pair ? 256 : 128;
+  const int64_t workers = pair ? di->sms / 2 : di->sms;
+  const int64_t blocks_est =
+      std::max<int64_t>((M + rows_per_unit - 1) / rows_per_unit, std::min<int64_t>(E, (M + 15) / 16));
+  int splits = 1;
+  while (blocks_est * splits * 2 <= workers && nch_total % (splits * 2) == 0 && splits * 2 <= nch_total) splits *= 2;
+  return splits;
+}
+
 // `split_weights`: the 3xTF32 weight planes are built by this call's
 // preparation launch (raw f32 weights); otherwise they are already in `ws`.
 static int run_small(const void* x, const void* w_up, const void* w_down, const int32_t* gs, float* y, int64_t M,
@@ -673,24 +690,9 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
   const bool pair = g_tune_pair == 2;
   if (pair && !pair_supported(D, dtype))
     return fail(MOE_ERR_INVALID_ARG, "CTA-pair kernel not available for D=%d dtype=%d", D, dtype);
-  int splits = 1;
-  if (g_tune_splits > 0) {
-    splits = (int)g_tune_splits;
-    if (nch_total % splits != 0)
-      return fail(MOE_ERR_INVALID_ARG, "tuning splits=%d does not divide %d chunks", splits, nch_total);
-  } else {
-    // The most F-splits that still fit the (expert, row-block) units in one
-    // wave of SMs (or SM pairs): a second wave of shorter units costs more
-    // than it balances (measured on B200 over M = 128 ... 131072, D = 64 ...
-    // 256, E = 4 ... 16, f32 and bf16).  Row blocks are estimated from M; at
-    // small M every expert is taken to hold a partial block of its own.
-    const int rows_per_unit = pair ? 256 : 128;
-    const int64_t workers = pair ? di->sms / 2 : di->sms;
-    const int64_t blocks_est =
-        std::max<int64_t>((M + rows_per_unit - 1) / rows_per_unit, std::min<int64_t>(E, (M + 15) / 16));
-    while (blocks_est * splits * 2 <= workers && nch_total % (splits * 2) == 0 && splits * 2 <= nch_total)
-      splits *= 2;
-  }
+  if (g_tune_splits > 0 && nch_total % g_tune_splits != 0)
+    return fail(MOE_ERR_INVALID_ARG, "tuning splits=%d does not divide %d chunks", (int)g_tune_splits, nch_total);
+  const int splits = small_splits(M, E, nch_total, pair, di);
   const int ctas_req = opt.ctas > 0 ? opt.ctas : (int)g_tune_ctas;
   int ctas = ctas_req > 0 && ctas_req < di->sms ? ctas_req : di->sms;
 
@@ -1586,6 +1588,25 @@ int moe_fused_mlp_swiglu(const void* x, const void* w_gate_up, const void* w_dow
   if (reinterpret_cast<uintptr_t>(y) & 15u) return fail(MOE_ERR_MISALIGNED, "y must be 16-byte aligned");
   return run_swiglu(x, w_gate_up, w_down, group_sizes, y, M, D, F, E, workspace, workspace_bytes,
                     static_cast<cudaStream_t>(stream));
+}
+
+int moe_fused_mlp_launch_count(int64_t M, int32_t D, int32_t F, int32_t E, int32_t dtype) {
+  t_err[0] = 0;
+  if (M < 0 || D <= 0 || F <= 0 || E <= 0 || dtype < 0 || dtype > 2)
+    return fail(MOE_ERR_INVALID_ARG, "bad arguments M=%lld D=%d F=%d E=%d dtype=%d", (long long)M, D, F, E, dtype);
+  if (M == 0) return 0;
+  if (!small_supported(D, F, dtype)) {
+    if (!large_supported(D, F, dtype)) return fail(MOE_ERR_UNSUPPORTED_SHAPE, "D=%d F=%d dtype=%d", D, F, dtype);
+    return dtype == MOE_DTYPE_FP8_E4M3_BLK128 ? 3 : 2;  // (X -> f16,) up GEMM, down GEMM
+  }
+  int dev;
+  DevInfo* di;
+  if (int r = device_info(&dev, &di)) return r;
+  const SmallPlan plan = small_plan(M, D, F, E, dtype);
+  const int splits = small_splits(M, E, F / plan.bf, g_tune_pair == 2, di);
+  // One preparation launch (weight planes, X planes, Y zeroing) when any of
+  // them is needed, then the fused kernel.
+  return (dtype == MOE_DTYPE_F32 || splits > 1 ? 1 : 0) + 1;
 }
 
 // ------------------------------------------------------------------ training

@@ -55,6 +55,8 @@ def lib() -> ctypes.CDLL:
     L.moe_prepare_weights.restype = ctypes.c_int
     L.moe_fused_mlp_workspace_size.argtypes = [i64, i32, i32, i32, i32]
     L.moe_fused_mlp_workspace_size.restype = sz
+    L.moe_fused_mlp_launch_count.argtypes = [i64, i32, i32, i32, i32]
+    L.moe_fused_mlp_launch_count.restype = ctypes.c_int
     L.moe_last_error.argtypes = []
     L.moe_last_error.restype = ctypes.c_char_p
     L.moe_device_status.argtypes = [ctypes.c_int]

@@ -185,3 +185,14 @@ def test_ep_engine_validates_arguments_before_any_device_work():
     assert h.value is None
     assert L.moe_ep_forward(None, None, None, None, 0, None) == -1
     assert L.moe_ep_launches_per_forward(None) == -1
+
+
+def test_launch_count_host_side():
+    L = _lib.lib()
+    assert L.moe_fused_mlp_launch_count(0, 128, 512, 8, 0) == 0
+    assert L.moe_fused_mlp_launch_count(-1, 128, 512, 8, 0) == -1
+    assert L.moe_fused_mlp_launch_count(16, 128, 512, 8, 9) == -1
+    # Two grouped GEMMs for bf16 large D, plus the X conversion for e4m3 weights.
+    assert L.moe_fused_mlp_launch_count(32768, 4096, 14336, 8, 1) == 2
+    assert L.moe_fused_mlp_launch_count(65536, 7168, 2048, 256, 2) == 3
+    assert L.moe_fused_mlp_launch_count(16, 384, 512, 8, 1) == -2
