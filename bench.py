@@ -492,28 +492,44 @@ def run_train(args, cfg, device) -> dict:
     (forward 4, backward 8); launches per step: 2 forward + 5 backward."""
     import torch
     from src import _lib
-    from src.train import backward, forward_train
+    from src.train import backward, forward_train, swiglu_backward, swiglu_forward_train
 
     if cfg.dtype != "bf16":
         cfg = with_shape_dtype(cfg, "bf16")
     x, w_up, w_down, gs, _ = make_workload(cfg, device)
     gs_dev = torch.from_numpy(gs).to(device)
+    swiglu = args.act == "swiglu"
+    if swiglu:  # gate and up weights, interleaved for the up GEMM
+        from src.kernel import swiglu_interleave
+        g0 = torch.Generator(device=device)
+        g0.manual_seed(777)
+        w_gate = (torch.randn(w_up.shape, generator=g0, device=device) / math.sqrt(cfg.D)).to(torch.bfloat16)
+        w_up = swiglu_interleave(w_gate, w_up)
+        del w_gate
     g = torch.Generator(device=device)
     g.manual_seed(4321)
     dy = torch.randn((cfg.M, cfg.D), generator=g, device=device)
     y = torch.empty((cfg.M, cfg.D), device=device)
-    a = torch.empty((cfg.M, cfg.F), device=device, dtype=torch.bfloat16)
+    a = torch.empty((cfg.M, 2 * cfg.F if swiglu else cfg.F), device=device, dtype=torch.bfloat16)
     L = _lib.lib()
-    ws_f = torch.empty(int(L.moe_fused_mlp_forward_train_workspace_size(cfg.M, cfg.D, cfg.F, cfg.E)),
-                       dtype=torch.uint8, device=device)
-    ws_b = torch.empty(int(L.moe_fused_mlp_backward_workspace_size(cfg.M, cfg.D, cfg.F, cfg.E)),
-                       dtype=torch.uint8, device=device)
+    if swiglu:
+        f_bytes = L.moe_fused_mlp_swiglu_forward_train_workspace_size(cfg.M, cfg.D, cfg.F, cfg.E)
+        b_bytes = L.moe_fused_mlp_swiglu_backward_workspace_size(cfg.M, cfg.D, cfg.F, cfg.E)
+        fwd_fn = lambda ws: swiglu_forward_train(x, w_up, w_down, gs_dev, out=y, gu_save=a, workspace=ws)  # noqa: E731
+        bwd_fn = lambda ws: swiglu_backward(x, w_up, w_down, gs_dev, a, dy, workspace=ws)  # noqa: E731
+    else:
+        f_bytes = L.moe_fused_mlp_forward_train_workspace_size(cfg.M, cfg.D, cfg.F, cfg.E)
+        b_bytes = L.moe_fused_mlp_backward_workspace_size(cfg.M, cfg.D, cfg.F, cfg.E)
+        fwd_fn = lambda ws: forward_train(x, w_up, w_down, gs_dev, out=y, a_save=a, workspace=ws)  # noqa: E731
+        bwd_fn = lambda ws: backward(x, w_up, w_down, gs_dev, a, dy, workspace=ws)  # noqa: E731
+    ws_f = torch.empty(int(f_bytes), dtype=torch.uint8, device=device)
+    ws_b = torch.empty(int(b_bytes), dtype=torch.uint8, device=device)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     st = torch.cuda.current_stream(device)
 
     def step():
-        forward_train(x, w_up, w_down, gs_dev, out=y, a_save=a, workspace=ws_f)
-        return backward(x, w_up, w_down, gs_dev, a, dy, workspace=ws_b)
+        fwd_fn(ws_f)
+        return bwd_fn(ws_b)
 
     for _ in range(args.warmup):
         step()
@@ -527,9 +543,9 @@ def run_train(args, cfg, device) -> dict:
         flush.zero_()
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         ev[0].record(st)
-        forward_train(x, w_up, w_down, gs_dev, out=y, a_save=a, workspace=ws_f)
+        fwd_fn(ws_f)
         ev[1].record(st)
-        backward(x, w_up, w_down, gs_dev, a, dy, workspace=ws_b)
+        bwd_fn(ws_b)
         ev[2].record(st)
         torch.cuda.synchronize(device)
         fwd.append(ev[0].elapsed_time(ev[1]))
@@ -543,19 +559,21 @@ def run_train(args, cfg, device) -> dict:
     peaks, peak_src = load_peaks()
     peak = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
     mdf = cfg.M * cfg.D * cfg.F
-    achieved = 12 * mdf / (ms / 1e3) / 1e12
+    f_fl, b_fl = (6, 12) if swiglu else (4, 8)  # forward / backward FLOPs in units of M D F
+    achieved = (f_fl + b_fl) * mdf / (ms / 1e3) / 1e12
     return {
         "metric": "routed_tokens_per_s", "value": cfg.M / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "dtype": "bf16", "data": "synthetic (seeded N(0,1) X and dY, N(0,1/D) / N(0,1/F) weights)",
-        "config": {"workload": f"{cfg.name}_train", "M": cfg.M, "D": cfg.D, "F": cfg.F, "E": cfg.E,
-                   "step": "forward (pre-activation saved) + backward (dX, dW_up, dW_down f32)",
+        "config": {"workload": f"{cfg.name}_train" + ("_swiglu" if swiglu else ""), "M": cfg.M, "D": cfg.D,
+                   "F": cfg.F, "E": cfg.E, "activation": args.act,
+                   "step": "forward (pre-activation saved) + backward (dX and the weight gradients, f32)",
                    "l2": "flushed before every step (256 MiB write)"},
         "gpu_launches": 7 * args.steps,
         "forward_ms": f_ms, "backward_ms": ms - f_ms,
-        "backward_tflops": 8 * mdf / ((ms - f_ms) / 1e3) / 1e12,
+        "backward_tflops": b_fl * mdf / ((ms - f_ms) / 1e3) / 1e12,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "traffic": None, "algorithmic_flops": 12 * mdf,
+                     "frac": achieved / peak, "traffic": None, "algorithmic_flops": (f_fl + b_fl) * mdf,
                      "peak_source": f"{peak_src}: bf16_tflops",
                      "kernels": "forward 2 grouped GEMMs + backward pad + 4 grouped GEMMs, timed together"},
         "clocks": clocks.summary(t0, t1),
@@ -763,7 +781,7 @@ def main() -> int:
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
-    if args.act == "swiglu":
+    if args.act == "swiglu" and args.stage != "train":
         if world > 1:
             raise SystemExit("--act swiglu runs on one GPU")
         print(json.dumps(run_swiglu(args, cfg, device)), flush=True)

@@ -285,6 +285,30 @@ int moe_fused_mlp_backward(const void* x, const void* w_up, const void* w_down, 
                            float* dw_down, int64_t M, int32_t D, int32_t F, int32_t E, void* workspace,
                            size_t workspace_bytes, void* stream);
 
+/*
+ * SwiGLU training (bf16; D and F multiples of 256; E <= 4096).  Weights as for
+ * moe_fused_mlp_swiglu: w_gate_up (E, D, 2F) interleaved every 128 columns.
+ *
+ * moe_fused_mlp_swiglu_forward_train  as moe_fused_mlp_swiglu, plus gu_save
+ *                  (M, 2F) bf16 = the raw gate and up columns X W_gate_up[e]
+ *                  of every routed row, in the weights' interleave.
+ * moe_fused_mlp_swiglu_backward  given dy (f32 or bf16) and gu_saved:
+ *                    dx         (M, D) f32, rows past sum(group_sizes) zero;
+ *                    dw_gate_up (E, D, 2F) f32, interleaved like w_gate_up;
+ *                    dw_down    (E, F, D) f32;
+ *                  with s = sigmoid(gate): dGate = (dy W_down^T) up s (1 +
+ *                  gate (1 - s)), dUp = (dy W_down^T) gate s, H = gate s up.
+ */
+size_t moe_fused_mlp_swiglu_forward_train_workspace_size(int64_t M, int32_t D, int32_t F, int32_t E);
+int moe_fused_mlp_swiglu_forward_train(const void* x, const void* w_gate_up, const void* w_down,
+                                       const int32_t* group_sizes, float* y, void* gu_save, int64_t M, int32_t D,
+                                       int32_t F, int32_t E, void* workspace, size_t workspace_bytes, void* stream);
+size_t moe_fused_mlp_swiglu_backward_workspace_size(int64_t M, int32_t D, int32_t F, int32_t E);
+int moe_fused_mlp_swiglu_backward(const void* x, const void* w_gate_up, const void* w_down,
+                                  const int32_t* group_sizes, const void* gu_saved, const void* dy, int32_t dy_dtype,
+                                  float* dx, float* dw_gate_up, float* dw_down, int64_t M, int32_t D, int32_t F,
+                                  int32_t E, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Text of the calling thread's last error ("" when none). */
 const char* moe_last_error(void);
 

@@ -327,3 +327,37 @@ def ref_ragged_mlp_backward(x: np.ndarray, w_up: np.ndarray, w_down: np.ndarray,
         dwu[e] = xe.T @ da
         dwd[e] = gelu_tanh(pre).T @ ye
     return dx, dwu, dwd
+
+
+def ref_ragged_swiglu_backward(x: np.ndarray, w_gate: np.ndarray, w_up: np.ndarray, w_down: np.ndarray,
+                               group_sizes: Sequence[int], dy: np.ndarray, acc_dtype=np.float64):
+    """(dX, dW_gate, dW_up, dW_down) of ``ref_ragged_swiglu`` for the upstream
+    gradient dy: per expert e with rows R, G = X_R W_gate[e], U = X_R W_up[e],
+    s = sigmoid(G), dH = dy_R W_down[e]^T, dG = dH U s (1 + G (1 - s)),
+    dU = dH G s, dX_R = dG W_gate[e]^T + dU W_up[e]^T, dW_gate[e] = X_R^T dG,
+    dW_up[e] = X_R^T dU, dW_down[e] = (G s U)^T dy_R."""
+    M, D = x.shape
+    E, _, F = w_gate.shape
+    dx = np.zeros((M, D), acc_dtype)
+    dwg = np.zeros((E, D, F), acc_dtype)
+    dwu = np.zeros((E, D, F), acc_dtype)
+    dwd = np.zeros((E, F, D), acc_dtype)
+    offs = np.minimum(group_sizes_to_offsets(np.maximum(np.asarray(group_sizes), 0)), M)
+    for e in range(E):
+        a, b = int(offs[e]), int(offs[e + 1])
+        if b <= a:
+            continue
+        xe = x[a:b].astype(acc_dtype)
+        ye = dy[a:b].astype(acc_dtype)
+        wg, wu, wd = (w[e].astype(acc_dtype) for w in (w_gate, w_up, w_down))
+        g = xe @ wg
+        u = xe @ wu
+        s = 1.0 / (1.0 + np.exp(-g))
+        dh = ye @ wd.T
+        dg = dh * u * s * (1.0 + g * (1.0 - s))
+        du = dh * g * s
+        dx[a:b] = dg @ wg.T + du @ wu.T
+        dwg[e] = xe.T @ dg
+        dwu[e] = xe.T @ du
+        dwd[e] = (g * s * u).T @ ye
+    return dx, dwg, dwu, dwd

@@ -87,8 +87,8 @@ __device__ __forceinline__ void store_y_rows(uint32_t taddr, float4* stage, uint
 
 // EPI 0: GELU -> H, 1: f32 Y, 2: SwiGLU -> H (B holds gate and up weights
 // interleaved every 128 columns; H has half the columns), 3: GELU -> H plus
-// the pre-activation (bf16) to out2; BFP8: e4m3 B dequantised in smem, f16
-// operands.
+// the pre-activation (bf16) to out2, 4: SwiGLU plus the raw gate/up columns
+// (bf16) to out2; BFP8: e4m3 B dequantised in smem, f16 operands.
 template <int EPI, bool BFP8>
 struct GemmCfg {
   static constexpr int BM = 128;   // rows per CTA (256 per pair)
@@ -626,7 +626,7 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
             __syncwarp();
           }
         }
-      } else if constexpr (EPI == 2) {
+      } else if constexpr (EPI == 2 || EPI == 4) {
         // SwiGLU: columns [0, 128) of the tile are gate, [128, 256) up;
         // H[:, 128 nb + c] = SiLU(gate_c) * up_c, 64 columns per step through
         // the same 32-row x 128-byte staging as the GELU epilogue.
@@ -664,6 +664,42 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
               *reinterpret_cast<uint4*>(H + (size_t)row * ldh + gcol + 8 * k) = val;
           }
           __syncwarp();
+        }
+        if constexpr (EPI == 4) {
+          // The tile's raw gate and up columns (bf16, same interleave as the
+          // weights), saved for the backward.
+          uint16_t* GU = reinterpret_cast<uint16_t*>(p.out2);
+#pragma unroll 1
+          for (int c0 = 0; c0 < C::BN; c0 += 64) {
+            uint4* srow = reinterpret_cast<uint4*>(wst) + lane * 8;
+#pragma unroll 1
+            for (int hh = 0; hh < 2; ++hh) {
+              uint32_t v[32];
+              tmem_ld32(acc + c0 + 32 * hh, v);
+              tmem_ld_wait();
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                uint4 w;
+                w.x = pack_bf16x2(__uint_as_float(v[8 * k + 0]), __uint_as_float(v[8 * k + 1]));
+                w.y = pack_bf16x2(__uint_as_float(v[8 * k + 2]), __uint_as_float(v[8 * k + 3]));
+                w.z = pack_bf16x2(__uint_as_float(v[8 * k + 4]), __uint_as_float(v[8 * k + 5]));
+                w.w = pack_bf16x2(__uint_as_float(v[8 * k + 6]), __uint_as_float(v[8 * k + 7]));
+                srow[(4 * hh + k) ^ (lane & 7)] = w;
+              }
+            }
+            __syncwarp();
+            const int gcol = nb * C::BN + c0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int r = 4 * i + (int)(lane >> 3);
+              const int k = (int)(lane & 7);
+              const uint4 val = reinterpret_cast<const uint4*>(wst)[r * 8 + (k ^ (r & 7))];
+              const int row = wrow0 + r;
+              if (row < row_end)
+                *reinterpret_cast<uint4*>(GU + (size_t)row * p.N + gcol + 8 * k) = val;
+            }
+            __syncwarp();
+          }
         }
       } else if (p.scatter.on) {
         // Destination of row wrow0 + lane: the source rank whose rows of

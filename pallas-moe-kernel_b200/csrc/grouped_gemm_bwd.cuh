@@ -35,7 +35,7 @@
 
 namespace moe {
 
-enum : int { kBwdDH = 0, kBwdDX = 1, kBwdDW = 2 };
+enum : int { kBwdDH = 0, kBwdDX = 1, kBwdDW = 2, kBwdDHSwiGLU = 3 };
 
 __host__ __device__ __forceinline__ int pad64(int g) { return (g + 63) & ~63; }
 
@@ -48,9 +48,11 @@ struct BwdParams {
   int m_out;          // DW: output rows per expert (D for dW_up, F for dW_down)
   int group_m;        // tile rasterisation group (row blocks)
   int* status;
-  const uint16_t* a_saved;  // DH: pre-activation (M, N) bf16, natural rows
-  void* out;          // DH: dA (Mp, N) bf16, padded rows; DX: dX (M, N) f32; DW: dW (E, m_out, N) f32
-  void* out2;         // DH: H = GELU(A) (Mp, N) bf16, padded rows
+  const uint16_t* a_saved;  // DH: pre-activation (M, N) bf16; DH SwiGLU: gate/up pre-activations
+                            // (M, 2N) bf16 interleaved every 128 columns; natural rows
+  void* out;          // DH: dA (Mp, N) bf16, padded rows; DH SwiGLU: dGate/dUp (Mp, 2N) interleaved;
+                      // DX: dX (M, N) f32; DW: dW (E, m_out, N) f32
+  void* out2;         // DH: H = GELU(A), DH SwiGLU: H = SiLU(gate) * up; (Mp, N) bf16, padded rows
 };
 
 template <int MODE>
@@ -139,6 +141,17 @@ __device__ __forceinline__ void gelu_tanh_and_grad(float x, float& g, float& gp)
   const float hx = 0.5f * x;
   g = fmaf(hx, t, hx);
   gp = fmaf(0.5f, t, 0.5f) + hx * sech2 * k0 * fmaf(3.0f * k1, x2, 1.0f);
+}
+
+// SwiGLU backward of one element: from dH, gate g and up u,
+//   s = sigmoid(g), H = g s u, dGate = dH u s (1 + g (1 - s)), dUp = dH g s.
+// s = 1 / (1 + 2^(-g log2 e)) with the approximate exp2 and reciprocal.
+__device__ __forceinline__ void swiglu_grad(float dh, float g, float u, float& dg, float& du, float& h) {
+  const float s = rcp_approx(1.0f + ex2_approx(-1.4426950408889634f * g));
+  const float silu = g * s;
+  h = silu * u;
+  du = dh * silu;
+  dg = dh * u * s * fmaf(g, 1.0f - s, 1.0f);
 }
 
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
@@ -404,6 +417,91 @@ __global__ void __launch_bounds__(BwdCfg<MODE>::THREADS, 1)
 #pragma unroll 1
         for (int c0 = 0; c0 < C::BN; c0 += 32)
           store_y_block<0>(acc + c0, wst4, Y, tl.row_begin + lr0, tl.row_begin + tl.rows, c0, lane, false, p.N);
+      } else if constexpr (MODE == kBwdDHSwiGLU) {
+        // 32 dH columns per step (inside one 128-column gate/up period): the
+        // saved gate and up columns come in through the staging tile as one
+        // 128-byte line per row (64 B gate | 64 B up); dGate|dUp leave the
+        // same way, H as 64-byte row segments.
+        uint16_t* dGU = reinterpret_cast<uint16_t*>(p.out);
+        uint16_t* Hp = reinterpret_cast<uint16_t*>(p.out2);
+        const int ld2 = 2 * p.N;
+        const int prow_end = pad64(tl.rows);
+#pragma unroll 1
+        for (int c0 = 0; c0 < C::BN; c0 += 32) {
+          const int fcol = tl.nb * C::BN + c0;              // first dH / H column
+          const int gcol = 256 * (fcol >> 7) + (fcol & 127);  // its gate column; up is 128 further
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = 4 * i + (int)(lane >> 3);
+            const int k = (int)(lane & 7);
+            const int lr = lr0 + r;
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (lr < tl.rows)
+              v = __ldg(reinterpret_cast<const uint4*>(p.a_saved + (size_t)(tl.row_begin + lr) * ld2 + gcol +
+                                                       (k < 4 ? 8 * k : 128 + 8 * (k - 4))));
+            stg[r * 8 + (k ^ (r & 7))] = v;
+          }
+          __syncwarp();
+          uint32_t g[16], u[16];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 a = stg[lane * 8 + (j ^ (lane & 7))];
+            const uint4 b = stg[lane * 8 + ((4 + j) ^ (lane & 7))];
+            g[4 * j] = a.x;
+            g[4 * j + 1] = a.y;
+            g[4 * j + 2] = a.z;
+            g[4 * j + 3] = a.w;
+            u[4 * j] = b.x;
+            u[4 * j + 1] = b.y;
+            u[4 * j + 2] = b.z;
+            u[4 * j + 3] = b.w;
+          }
+          __syncwarp();
+          uint32_t v[32];
+          tmem_ld32(acc + c0, v);
+          tmem_ld_wait();
+          uint32_t dg[16], du[16], hv[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float dg0, du0, h0, dg1, du1, h1;
+            swiglu_grad(__uint_as_float(v[2 * j]), bf16_lo(g[j]), bf16_lo(u[j]), dg0, du0, h0);
+            swiglu_grad(__uint_as_float(v[2 * j + 1]), bf16_hi(g[j]), bf16_hi(u[j]), dg1, du1, h1);
+            dg[j] = pack_bf16x2(dg0, dg1);
+            du[j] = pack_bf16x2(du0, du1);
+            hv[j] = pack_bf16x2(h0, h1);
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            stg[lane * 8 + (j ^ (lane & 7))] = make_uint4(dg[4 * j], dg[4 * j + 1], dg[4 * j + 2], dg[4 * j + 3]);
+            stg[lane * 8 + ((4 + j) ^ (lane & 7))] =
+                make_uint4(du[4 * j], du[4 * j + 1], du[4 * j + 2], du[4 * j + 3]);
+          }
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = 4 * i + (int)(lane >> 3);
+            const int k = (int)(lane & 7);
+            const int lr = lr0 + r;
+            if (lr < prow_end)
+              *reinterpret_cast<uint4*>(dGU + (size_t)(tl.prow_begin + lr) * ld2 + gcol +
+                                        (k < 4 ? 8 * k : 128 + 8 * (k - 4))) = stg[r * 8 + (k ^ (r & 7))];
+          }
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            stg[lane * 8 + (j ^ (lane & 7))] = make_uint4(hv[4 * j], hv[4 * j + 1], hv[4 * j + 2], hv[4 * j + 3]);
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = 4 * i + (int)(lane >> 3);
+            const int k = (int)(lane & 7);
+            const int lr = lr0 + r;
+            if (k < 4 && lr < prow_end)
+              *reinterpret_cast<uint4*>(Hp + (size_t)(tl.prow_begin + lr) * p.N + fcol + 8 * k) =
+                  stg[r * 8 + (k ^ (r & 7))];
+          }
+          __syncwarp();
+        }
       } else {
         // dA = dH * GELU'(A) and H = GELU(A), 64 columns per step.  The saved
         // A rows come in through the staging tile (coalesced 128-byte row

@@ -271,7 +271,7 @@ static int launch_gemm(const GemmMaps& maps, const GemmParams& prm, DevInfo* di,
   auto kern = grouped_gemm_pair_kernel<EPI, BFP8>;
   constexpr int slot = 24 + 2 * EPI + (BFP8 ? 1 : 0);
   constexpr int pslot = 8 + 2 * EPI + (BFP8 ? 1 : 0);
-  static_assert(slot < 32 && pslot < 16, "attribute slot");
+  static_assert(slot < 36 && pslot < 18, "attribute slot");
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -371,8 +371,9 @@ template <int MODE>
 static int launch_bwd(const GemmMaps& maps, const BwdParams& prm, DevInfo* di, cudaStream_t st, int ctas_req) {
   using Cfg = BwdCfg<MODE>;
   auto kern = grouped_bwd_pair_kernel<MODE>;
-  constexpr int slot = 32 + MODE;
-  constexpr int pslot = 16 + MODE;
+  constexpr int slot = 36 + MODE;
+  constexpr int pslot = 18 + MODE;
+  static_assert(slot < 40 && pslot < 24, "attribute slot");
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -485,6 +486,93 @@ static int run_backward(const void* x, const void* w_up, const void* w_down, con
   p = BwdParams{gs, (int)M, E, F, 0, D, 8, status, nullptr, dw_up, nullptr};
   if (int r = launch_bwd<kBwdDW>(m, p, di, st, ctas)) return r;
   // 5. dW_down[e] = H_e^T dY_e  (E, F, D).
+  memset(&m, 0, sizeof(m));
+  if (int r = make_map_2d(&m.a, h_pad, BF16, 2, (uint64_t)mp, F, 64, 64)) return r;
+  if (int r = make_map_2d(&m.b, dy_pad, BF16, 2, (uint64_t)mp, D, 64, 64)) return r;
+  p = BwdParams{gs, (int)M, E, D, 0, F, 8, status, nullptr, dw_down, nullptr};
+  return launch_bwd<kBwdDW>(m, p, di, st, ctas);
+}
+
+// SwiGLU training: forward saving the raw gate/up columns, and its backward.
+static size_t swiglu_bwd_ws_bytes(int64_t M, int D, int F, int E) {
+  const int64_t mp = bwd_padded_rows(M, E);
+  return 2 * align256((size_t)mp * D * 2) + align256((size_t)mp * 2 * F * 2) + align256((size_t)mp * F * 2);
+}
+
+static int run_swiglu_train_forward(const void* x, const void* w_gu, const void* w_down, const int32_t* gs, float* y,
+                                    void* gu_save, int64_t M, int D, int F, int E, void* ws, size_t ws_bytes,
+                                    cudaStream_t st) {
+  int dev;
+  DevInfo* di;
+  if (int r = device_info(&dev, &di)) return r;
+  const size_t need = align256((size_t)M * F * 2);
+  if (ws_bytes < need) return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", ws_bytes, need);
+  if (reinterpret_cast<uintptr_t>(ws) & 255u) return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+  int* status = di->status;
+  const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int ctas = (int)g_tune_ctas;
+  GemmMaps m1;
+  memset(&m1, 0, sizeof(m1));
+  if (int r = make_map_2d(&m1.a, x, BF16, 2, (uint64_t)M, D, 64, 128)) return r;
+  if (int r = make_map_2d(&m1.b, w_gu, BF16, 2, (uint64_t)E * D, 2 * F, 64, 64)) return r;
+  GemmParams p1{gs, ws, (int)M, E, 2 * F, D, D, 8, status, nullptr, 0};
+  p1.out2 = gu_save;
+  if (int r = launch_gemm<4, false>(m1, p1, di, st, ctas)) return r;
+  GemmMaps m2;
+  memset(&m2, 0, sizeof(m2));
+  if (int r = make_map_2d(&m2.a, ws, BF16, 2, (uint64_t)M, F, 64, 128)) return r;
+  if (int r = make_map_2d(&m2.b, w_down, BF16, 2, (uint64_t)E * F, D, 64, 64)) return r;
+  GemmParams p2{gs, y, (int)M, E, D, F, F, 8, status, nullptr, 0};
+  return launch_gemm<1, false>(m2, p2, di, st, ctas);
+}
+
+static int run_swiglu_backward(const void* x, const void* w_gu, const void* w_down, const int32_t* gs,
+                               const void* gu_saved, const void* dy, int dy_dtype, float* dx, float* dw_gu,
+                               float* dw_down, int64_t M, int D, int F, int E, void* ws, size_t ws_bytes,
+                               cudaStream_t st) {
+  int dev;
+  DevInfo* di;
+  if (int r = device_info(&dev, &di)) return r;
+  const size_t need = swiglu_bwd_ws_bytes(M, D, F, E);
+  if (ws_bytes < need) return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", ws_bytes, need);
+  if (reinterpret_cast<uintptr_t>(ws) & 255u) return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+  int* status = di->status;
+  const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int ctas = (int)g_tune_ctas;
+  const int64_t mp = bwd_padded_rows(M, E);
+  const size_t sx = align256((size_t)mp * D * 2);
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  uint16_t* x_pad = reinterpret_cast<uint16_t*>(w);
+  uint16_t* dy_pad = reinterpret_cast<uint16_t*>(w + sx);
+  uint16_t* dgu_pad = reinterpret_cast<uint16_t*>(w + 2 * sx);
+  uint16_t* h_pad = reinterpret_cast<uint16_t*>(w + 2 * sx + align256((size_t)mp * 2 * F * 2));
+  {
+    const int blocks = (int)std::min<int64_t>((mp + 7) / 8, (int64_t)di->sms * 8);
+    bwd_pad_rows_kernel<<<blocks, 256, 8 * (E + 1), st>>>(static_cast<const uint16_t*>(x), dy,
+                                                           dy_dtype == MOE_DTYPE_F32 ? 1 : 0, gs, E, (int)M, D,
+                                                           x_pad, dy_pad);
+    MOE_CUDA_TRY(cudaGetLastError());
+  }
+  GemmMaps m;
+  // dH = dY W_down^T -> dGate, dUp (interleaved like the weights), H (padded rows).
+  memset(&m, 0, sizeof(m));
+  if (int r = make_map_2d(&m.a, dy_pad, BF16, 2, (uint64_t)mp, D, 64, 128)) return r;
+  if (int r = make_map_2d(&m.b, w_down, BF16, 2, (uint64_t)E * F, D, 64, 128)) return r;
+  BwdParams p{gs, (int)M, E, F, D, 0, 8, status, static_cast<const uint16_t*>(gu_saved), dgu_pad, h_pad};
+  if (int r = launch_bwd<kBwdDHSwiGLU>(m, p, di, st, ctas)) return r;
+  // dX = [dGate | dUp] W_gate_up^T (K = 2F).
+  memset(&m, 0, sizeof(m));
+  if (int r = make_map_2d(&m.a, dgu_pad, BF16, 2, (uint64_t)mp, 2 * F, 64, 128)) return r;
+  if (int r = make_map_2d(&m.b, w_gu, BF16, 2, (uint64_t)E * D, 2 * F, 64, 128)) return r;
+  p = BwdParams{gs, (int)M, E, D, 2 * F, 0, 8, status, nullptr, dx, nullptr};
+  if (int r = launch_bwd<kBwdDX>(m, p, di, st, ctas)) return r;
+  // dW_gate_up[e] = X_e^T [dGate | dUp]_e  (E, D, 2F), interleaved like the weights.
+  memset(&m, 0, sizeof(m));
+  if (int r = make_map_2d(&m.a, x_pad, BF16, 2, (uint64_t)mp, D, 64, 64)) return r;
+  if (int r = make_map_2d(&m.b, dgu_pad, BF16, 2, (uint64_t)mp, 2 * F, 64, 64)) return r;
+  p = BwdParams{gs, (int)M, E, 2 * F, 0, D, 8, status, nullptr, dw_gu, nullptr};
+  if (int r = launch_bwd<kBwdDW>(m, p, di, st, ctas)) return r;
+  // dW_down[e] = H_e^T dY_e  (E, F, D).
   memset(&m, 0, sizeof(m));
   if (int r = make_map_2d(&m.a, h_pad, BF16, 2, (uint64_t)mp, F, 64, 64)) return r;
   if (int r = make_map_2d(&m.b, dy_pad, BF16, 2, (uint64_t)mp, D, 64, 64)) return r;
@@ -1659,6 +1747,48 @@ int moe_fused_mlp_backward(const void* x, const void* w_up, const void* w_down, 
     return fail(MOE_ERR_MISALIGNED, "operands must be 16-byte aligned");
   return run_backward(x, w_up, w_down, group_sizes, a_saved, dy, dy_dtype, dx, dw_up, dw_down, M, D, F, E, workspace,
                       workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+size_t moe_fused_mlp_swiglu_forward_train_workspace_size(int64_t M, int32_t D, int32_t F, int32_t E) {
+  if (M < 0 || E <= 0 || !train_supported(D, F)) return 0;
+  return align256((size_t)M * F * 2);
+}
+
+int moe_fused_mlp_swiglu_forward_train(const void* x, const void* w_gate_up, const void* w_down,
+                                       const int32_t* group_sizes, float* y, void* gu_save, int64_t M, int32_t D,
+                                       int32_t F, int32_t E, void* workspace, size_t workspace_bytes, void* stream) {
+  t_err[0] = 0;
+  if (int r = check_train_args(M, D, F, E)) return r;
+  if (M == 0) return 0;
+  if (!x || !w_gate_up || !w_down || !group_sizes || !y || !gu_save)
+    return fail(MOE_ERR_INVALID_ARG, "null operand pointer");
+  if ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(gu_save)) & 15u)
+    return fail(MOE_ERR_MISALIGNED, "y and gu_save must be 16-byte aligned");
+  return run_swiglu_train_forward(x, w_gate_up, w_down, group_sizes, y, gu_save, M, D, F, E, workspace,
+                                  workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+size_t moe_fused_mlp_swiglu_backward_workspace_size(int64_t M, int32_t D, int32_t F, int32_t E) {
+  if (M < 0 || E <= 0 || E > 4096 || !train_supported(D, F)) return 0;
+  return swiglu_bwd_ws_bytes(M, D, F, E);
+}
+
+int moe_fused_mlp_swiglu_backward(const void* x, const void* w_gate_up, const void* w_down,
+                                  const int32_t* group_sizes, const void* gu_saved, const void* dy, int32_t dy_dtype,
+                                  float* dx, float* dw_gate_up, float* dw_down, int64_t M, int32_t D, int32_t F,
+                                  int32_t E, void* workspace, size_t workspace_bytes, void* stream) {
+  t_err[0] = 0;
+  if (int r = check_train_args(M, D, F, E)) return r;
+  if (dy_dtype != MOE_DTYPE_F32 && dy_dtype != MOE_DTYPE_BF16)
+    return fail(MOE_ERR_UNSUPPORTED_DTYPE, "dy_dtype %d (f32 or bf16)", dy_dtype);
+  if (!x || !w_gate_up || !w_down || !group_sizes || !gu_saved || !dy || !dx || !dw_gate_up || !dw_down)
+    return fail(MOE_ERR_INVALID_ARG, "null operand pointer");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(gu_saved) | reinterpret_cast<uintptr_t>(dy) |
+       reinterpret_cast<uintptr_t>(dx) | reinterpret_cast<uintptr_t>(dw_gate_up) |
+       reinterpret_cast<uintptr_t>(dw_down)) & 15u)
+    return fail(MOE_ERR_MISALIGNED, "operands must be 16-byte aligned");
+  return run_swiglu_backward(x, w_gate_up, w_down, group_sizes, gu_saved, dy, dy_dtype, dx, dw_gate_up, dw_down, M, D,
+                             F, E, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -72,3 +72,38 @@ def test_training_workspace_sizes():
     mp = M + 64 * E
     assert L.moe_fused_mlp_backward_workspace_size(M, D, F, E) == 2 * mp * D * 2 + 2 * mp * F * 2
     assert L.moe_fused_mlp_backward_workspace_size(M, 128, F, E) == 0
+
+
+@pytest.mark.parametrize("gs", [[7, 0, 12], [20, 3, 9], [0, 0, 0]])
+def test_swiglu_backward_oracle_matches_autograd(gs):
+    rng = np.random.default_rng(50 + sum(gs))
+    M, D, F, E = 32, 6, 10, 3
+    x = rng.standard_normal((M, D))
+    wg, wu = rng.standard_normal((E, D, F)) / 2, rng.standard_normal((E, D, F)) / 2
+    wd = rng.standard_normal((E, F, D)) / 3
+    dy = rng.standard_normal((M, D))
+    dx, dwg, dwu, dwd = orc.ref_ragged_swiglu_backward(x, wg, wu, wd, gs, dy)
+    xt, wgt, wut, wdt = (torch.tensor(a, dtype=torch.float64, requires_grad=True) for a in (x, wg, wu, wd))
+    offs = np.concatenate([[0], np.cumsum(gs)])
+    parts = [(torch.nn.functional.silu(xt[offs[e]:offs[e + 1]] @ wgt[e]) * (xt[offs[e]:offs[e + 1]] @ wut[e])) @ wdt[e]
+             for e in range(E)]
+    y = torch.cat(parts + [torch.zeros((M - int(offs[-1]), D), dtype=torch.float64)])
+    y.backward(torch.tensor(dy))
+    for got, ref in ((dx, xt.grad), (dwg, wgt.grad), (dwu, wut.grad), (dwd, wdt.grad)):
+        np.testing.assert_allclose(got, ref.numpy(), rtol=1e-12, atol=1e-12)
+
+
+def test_swiglu_training_abi_checks_before_device_work():
+    L = _lib.lib()
+    vp = ctypes.c_void_p
+    n, s = vp(0), vp(16)
+    assert L.moe_fused_mlp_swiglu_forward_train(n, n, n, n, n, n, -1, 512, 512, 4, n, 0, n) == -1
+    assert L.moe_fused_mlp_swiglu_forward_train(s, s, s, s, s, s, 16, 512, 384, 4, n, 0, n) == -2
+    assert L.moe_fused_mlp_swiglu_forward_train(n, n, n, n, n, n, 0, 512, 512, 4, n, 0, n) == 0
+    args = [s, s, s, s, s, s, 0, s, s, s, 16, 512, 512, 4, n, 0, n]
+    assert L.moe_fused_mlp_swiglu_backward(*args[:6], 2, *args[7:]) == -3
+    assert L.moe_fused_mlp_swiglu_backward(*args[:5], n, 0, *args[7:]) == -1
+    M, D, F, E = 32768, 4096, 14336, 8
+    mp = M + 64 * E
+    assert L.moe_fused_mlp_swiglu_backward_workspace_size(M, D, F, E) == 2 * mp * D * 2 + mp * 2 * F * 2 + mp * F * 2
+    assert L.moe_fused_mlp_swiglu_forward_train_workspace_size(M, D, F, E) == M * F * 2

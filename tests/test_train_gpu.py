@@ -170,3 +170,78 @@ def test_backward_mixtral_shape_sampled():
         got_w += [dwu[e][:, cols].cpu().numpy(), dwd[e][cols, :].cpu().numpy().T]
     assert _rel(np.concatenate(ref_x), np.concatenate(got_x)) <= TOL
     assert _rel(np.concatenate(ref_w), np.concatenate(got_w)) <= TOL
+
+
+# ----------------------------------------------------------------------------- SwiGLU experts
+from src.kernel import fused_ragged_swiglu, swiglu_interleave  # noqa: E402
+from src.train import fused_ragged_swiglu_train, swiglu_backward, swiglu_forward_train  # noqa: E402
+
+
+def _swiglu_inputs(M, D, F, E, seed):
+    g = torch.Generator(device=DEV)
+    g.manual_seed(seed)
+    x = torch.randn((M, D), generator=g, device=DEV).to(torch.bfloat16)
+    wg = (torch.randn((E, D, F), generator=g, device=DEV) / D ** 0.5).to(torch.bfloat16)
+    wu = (torch.randn((E, D, F), generator=g, device=DEV) / D ** 0.5).to(torch.bfloat16)
+    wd = (torch.randn((E, F, D), generator=g, device=DEV) / F ** 0.5).to(torch.bfloat16)
+    dy = torch.randn((M, D), generator=g, device=DEV)
+    return x, wg, wu, wd, dy
+
+
+def test_swiglu_forward_train_matches_forward_and_saves_gate_up():
+    M, D, F, E = 2048, 512, 512, 4
+    gs = make_group_sizes(M - 64, E)
+    x, wg, wu, wd, _ = _swiglu_inputs(M, D, F, E, seed=3)
+    wgu = swiglu_interleave(wg, wu)
+    gst = torch.from_numpy(gs).to(DEV)
+    y, gu = swiglu_forward_train(x, wgu, wd, gst)
+    y_ref = fused_ragged_swiglu(x, wgu, wd, gst)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y_ref)
+    n = int(gs.sum())
+    pre = orc.ragged_dot(_np(x), orc.swiglu_interleave(_np(wg), _np(wu)), gs, np.float64)
+    assert _rel(pre[:n], _np(gu[:n])) <= 4e-3
+
+
+@pytest.mark.parametrize("M,D,F,E,gs", [
+    (2048, 512, 512, 4, None),
+    (1536, 768, 256, 3, None),
+    (1024, 512, 512, 4, [0, 700, 0, 5]),
+    (1024, 512, 512, 4, [300, 0, 0, 0]),
+])
+def test_swiglu_backward_full_oracle(M, D, F, E, gs):
+    gs = make_group_sizes(M, E) if gs is None else np.asarray(gs, np.int32)
+    x, wg, wu, wd, dy = _swiglu_inputs(M, D, F, E, seed=M + F)
+    wgu = swiglu_interleave(wg, wu)
+    gst = torch.from_numpy(gs).to(DEV)
+    _, gu = swiglu_forward_train(x, wgu, wd, gst)
+    dx, dwgu, dwd = swiglu_backward(x, wgu, wd, gst, gu, dy)
+    torch.cuda.synchronize()
+    rx, rwg, rwu, rwd = orc.ref_ragged_swiglu_backward(_np(x), _np(wg), _np(wu), _np(wd), gs, _np(dy))
+    n = int(gs.sum())
+    dx = dx.cpu().numpy()
+    assert np.all(dx[n:] == 0.0)
+    for e, g in enumerate(gs):
+        if g == 0:
+            assert torch.all(dwgu[e] == 0) and torch.all(dwd[e] == 0)
+    assert _rel(rx, dx) <= TOL
+    assert _rel(orc.swiglu_interleave(rwg, rwu), dwgu.cpu().numpy()) <= TOL
+    assert _rel(rwd, dwd.cpu().numpy()) <= TOL
+
+
+def test_swiglu_autograd_matches_torch_autograd():
+    M, D, F, E = 1024, 256, 256, 3
+    gs = make_group_sizes(M - 40, E)
+    x, wg, wu, wd, dy = _swiglu_inputs(M, D, F, E, seed=21)
+    wgu = swiglu_interleave(wg, wu)
+    xs, wgus, wds = (t.clone().requires_grad_(True) for t in (x, wgu, wd))
+    fused_ragged_swiglu_train(xs, wgus, wds, torch.from_numpy(gs).to(DEV)).backward(dy)
+    xr, wgr, wur, wdr = (t.float().clone().requires_grad_(True) for t in (x, wg, wu, wd))
+    offs = np.concatenate([[0], np.cumsum(gs)])
+    parts = [(torch.nn.functional.silu(xr[offs[e]:offs[e + 1]] @ wgr[e]) * (xr[offs[e]:offs[e + 1]] @ wur[e])) @ wdr[e]
+             for e in range(E)]
+    torch.cat(parts + [torch.zeros((M - int(offs[-1]), D), device=DEV)]).backward(dy)
+    assert _rel(xr.grad.double().cpu().numpy(), xs.grad.double().cpu().numpy()) <= 2e-2
+    ref_gu = swiglu_interleave(wgr.grad.bfloat16(), wur.grad.bfloat16())
+    assert _rel(ref_gu.double().cpu().numpy(), wgus.grad.double().cpu().numpy()) <= 2e-2
+    assert _rel(wdr.grad.double().cpu().numpy(), wds.grad.double().cpu().numpy()) <= 2e-2
