@@ -336,7 +336,7 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": {"f32": "f32 (3xTF32)", "bf16": "bf16", "fp8": "fp8e4m3 weights, bf16 x"}[cfg.dtype],
-        "data": "synthetic (seeded; BASELINE config shapes, N(0,1)/N(0,1/D)/N(0,1/F) init)",
+        "data": "synthetic (seeded; the configuration's shapes, N(0,1)/N(0,1/D)/N(0,1/F) init)",
         "config": {"workload": cfg.name, "M_per_gpu": cfg.M, "D": cfg.D, "F": cfg.F, "E": cfg.E,
                    "routing": cfg.routing, "parallelism": f"ep{world}" if world > 1 else "single",
                    **({"waves": getattr(layer, "waves", args.waves), "transport": args.transport}

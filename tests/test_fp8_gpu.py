@@ -1,6 +1,6 @@
 """FP8 e4m3 block-scaled weights (bf16 X, 128x128 f32 block scales) through
 the large-D grouped GEMMs.  Tolerance: L2 relative error <= 2e-2 against the
-float64 oracle on the dequantised weights (BASELINE FP8 contract)."""
+float64 oracle on the dequantised weights, the FP8 bar of this library."""
 
 import numpy as np
 import pytest

@@ -1,6 +1,6 @@
 """Parity of the large-D path (two grouped GEMMs on CTA pairs, bf16) against
 the CPU oracle.  Tolerance: L2 relative error <= 1e-2 against the float64
-oracle on the bf16-rounded inputs (BASELINE bf16 contract)."""
+oracle on the bf16-rounded inputs, the bf16 bar of this library."""
 
 import numpy as np
 import pytest
