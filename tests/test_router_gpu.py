@@ -49,7 +49,7 @@ def test_permute_matches_oracle(T, k, E, kind):
     assert _lib.device_status(reset=True) == (16 if kind == "bad" else 0)
 
 
-@pytest.mark.parametrize("dt,D", [(torch.bfloat16, 7168), (torch.float32, 128), (torch.bfloat16, 8)])
+@pytest.mark.parametrize("dt,D", [(torch.bfloat16, 7168), (torch.float32, 128), (torch.bfloat16, 8), (torch.float32, 400)])
 def test_gather_and_combine_match_oracle(dt, D):
     T, k, E = 777, 4, 32
     rng = np.random.default_rng(D)
