@@ -1,0 +1,53 @@
+"""moe_fused_mlp_launch_count (the bench's `gpu_launches`) against the
+kernels a call actually launches, counted with torch's profiler."""
+
+import pytest
+import torch
+
+from src import _lib
+from src.kernel import fused_ragged_dot_caller
+from src.routing import make_group_sizes, quantize_e4m3_blockwise
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+
+
+def _library_kernels(fn) -> int:
+    from torch.profiler import ProfilerActivity, profile
+    fn()
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    names = [e.key for e in prof.key_averages()]
+    if not names:
+        pytest.skip("the profiler recorded no GPU activity on this box")
+    return sum(e.count for e in prof.key_averages() if "moe::" in e.key)
+
+
+@pytest.mark.parametrize("M,D,F,E,dt", [
+    (4096, 128, 1024, 8, "f32"),     # weight split + fused kernel
+    (16384, 128, 512, 4, "bf16"),    # one wave of whole blocks: the fused kernel alone
+    (512, 128, 512, 4, "bf16"),      # F split across CTAs: Y zeroed first
+    (1024, 512, 1024, 4, "bf16"),    # two grouped GEMMs
+    (1024, 512, 1024, 4, "fp8"),     # X to f16 + two grouped GEMMs
+])
+def test_launch_count_matches_launched_kernels(M, D, F, E, dt):
+    g = torch.Generator(device=DEV)
+    g.manual_seed(1)
+    tdt = torch.float32 if dt == "f32" else torch.bfloat16
+    x = torch.randn((M, D), generator=g, device=DEV).to(tdt)
+    wu = torch.randn((E, D, F), generator=g, device=DEV) / D ** 0.5
+    wd = torch.randn((E, F, D), generator=g, device=DEV) / F ** 0.5
+    kw = {}
+    if dt == "fp8":
+        (wu, su), (wd, sd) = quantize_e4m3_blockwise(wu), quantize_e4m3_blockwise(wd)
+        kw = {"w_up_scale": su, "w_down_scale": sd}
+    else:
+        wu, wd = wu.to(tdt), wd.to(tdt)
+    gs = torch.from_numpy(make_group_sizes(M, E)).to(DEV)
+    out = torch.empty((M, D), device=DEV)
+    code = {"f32": _lib.MOE_DTYPE_F32, "bf16": _lib.MOE_DTYPE_BF16, "fp8": _lib.MOE_DTYPE_FP8_E4M3_BLK128}[dt]
+    claimed = _lib.lib().moe_fused_mlp_launch_count(M, D, F, E, code)
+    counted = _library_kernels(lambda: fused_ragged_dot_caller(x, wu, wd, gs, max_group_size=M, out=out, **kw))
+    assert counted == claimed, (counted, claimed)
