@@ -252,6 +252,28 @@ int moe_fused_mlp_swiglu(const void* x, const void* w_gate_up, const void* w_dow
                          size_t workspace_bytes, void* stream);
 
 /*
+ * SwiGLU experts with e4m3 weights and 128 x 128 f32 block scales (the
+ * DeepSeek-V3 weight format).  Dequantised weight = e4m3 value * its block's
+ * scale, as for MOE_DTYPE_FP8_E4M3_BLK128; x is bf16; the GEMMs run on f16
+ * operands with f32 accumulation.  D a multiple of 256, F of 128.
+ *
+ * moe_swiglu_interleave_fp8  w_gate, w_up (E, D, F) e4m3 with s_gate, s_up
+ *                  (E, D/128, F/128) -> w_gate_up (E, D, 2F) interleaved every
+ *                  128 columns and s_gate_up (E, D/128, 2F/128) (one gate
+ *                  block, then the up block of the same columns).
+ * moe_fused_mlp_swiglu_fp8   y (M, D) f32 from x, w_gate_up / s_gate_up and
+ *                  w_down (E, F, D) e4m3 / s_down (E, F/128, D/128); workspace
+ *                  moe_fused_mlp_swiglu_fp8_workspace_size bytes (H and X in
+ *                  f16), 256-byte aligned.
+ */
+int moe_swiglu_interleave_fp8(const void* w_gate, const void* w_up, const float* s_gate, const float* s_up,
+                              void* w_gate_up, float* s_gate_up, int32_t E, int32_t D, int32_t F, void* stream);
+size_t moe_fused_mlp_swiglu_fp8_workspace_size(int64_t M, int32_t D, int32_t F);
+int moe_fused_mlp_swiglu_fp8(const void* x, const void* w_gate_up, const void* w_down, const float* s_gate_up,
+                             const float* s_down, const int32_t* group_sizes, float* y, int64_t M, int32_t D,
+                             int32_t F, int32_t E, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Training: forward with the pre-activation saved, and the backward.  No
  * counterpart in the reference, which has no backward pass (its kernel is
  * forward-only, src/kernel.py:9-123); the forward math, ragged layout and

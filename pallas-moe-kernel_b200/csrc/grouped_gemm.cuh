@@ -86,7 +86,8 @@ __device__ __forceinline__ void store_y_rows(uint32_t taddr, float4* stage, uint
 }
 
 // EPI 0: GELU -> H, 1: f32 Y, 2: SwiGLU -> H (B holds gate and up weights
-// interleaved every 128 columns; H has half the columns), 3: GELU -> H plus
+// interleaved every 128 columns, and for e4m3 their block scales one
+// block per period; H has half the columns), 3: GELU -> H plus
 // the pre-activation (bf16) to out2, 4: SwiGLU plus the raw gate/up columns
 // (bf16) to out2; BFP8: e4m3 B dequantised in smem, f16 operands.
 template <int EPI, bool BFP8>
@@ -641,14 +642,19 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
             tmem_ld32(acc + c0 + 32 * hh, g);
             tmem_ld32(acc + C::BN / 2 + c0 + 32 * hh, u);
             tmem_ld_wait();
-            auto h = [&](int i) { return silu_fast(__uint_as_float(g[i])) * __uint_as_float(u[i]); };
+            // e4m3 weights: the tile was accumulated with weights scaled by
+            // 2^k (mul = 2^-k); H is the f16 operand of the down GEMM.
+            auto h = [&](int i) {
+              return silu_fast(__uint_as_float(g[i]) * mul) * (__uint_as_float(u[i]) * mul);
+            };
+            auto pk = [&](float a, float b) { return BFP8 ? pack_f16x2_sat(a, b) : pack_bf16x2(a, b); };
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               uint4 w;
-              w.x = pack_bf16x2(h(8 * k + 0), h(8 * k + 1));
-              w.y = pack_bf16x2(h(8 * k + 2), h(8 * k + 3));
-              w.z = pack_bf16x2(h(8 * k + 4), h(8 * k + 5));
-              w.w = pack_bf16x2(h(8 * k + 6), h(8 * k + 7));
+              w.x = pk(h(8 * k + 0), h(8 * k + 1));
+              w.y = pk(h(8 * k + 2), h(8 * k + 3));
+              w.z = pk(h(8 * k + 4), h(8 * k + 5));
+              w.w = pk(h(8 * k + 6), h(8 * k + 7));
               srow[(4 * hh + k) ^ (lane & 7)] = w;
             }
           }

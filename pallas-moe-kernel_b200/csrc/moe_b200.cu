@@ -585,46 +585,89 @@ static int run_swiglu_backward(const void* x, const void* w_gu, const void* w_do
 // 128: [gate 0..127 | up 0..127 | gate 128..255 | up 128..255 | ...], so that
 // every 256-column tile of the up GEMM holds matching gate and up columns.
 // One thread per 16-byte vector (8 bf16).
+// `vin` vectors per input row, `vblk` vectors per 128-column block (16 for
+// bf16, 8 for e4m3): output period = one gate block then one up block.
 __global__ void swiglu_interleave_kernel(const uint4* __restrict__ gate, const uint4* __restrict__ up,
-                                         uint4* __restrict__ out, size_t rows, int F) {
-  const int vin = F / 8, vout = 2 * vin;
+                                         uint4* __restrict__ out, size_t rows, int vin, int vblk) {
+  const int vout = 2 * vin;
   const size_t n = rows * (size_t)vout;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     const size_t r = i / vout;
     const int v = (int)(i - r * vout);
-    const int j = v / 32, w = v % 32;   // 32 vectors = 256 columns per interleave period
-    const uint4* src = w < 16 ? gate : up;
-    out[i] = src[r * vin + (size_t)j * 16 + (w & 15)];
+    const int j = v / (2 * vblk), w = v % (2 * vblk);
+    const uint4* src = w < vblk ? gate : up;
+    out[i] = src[r * vin + (size_t)j * vblk + (w % vblk)];
+  }
+}
+
+// 128 x 128 block scales of e4m3 gate and up weights, (rows, nb) each ->
+// (rows, 2 nb): one gate block, then the up block of the same columns.
+__global__ void swiglu_interleave_scales_kernel(const float* __restrict__ gate, const float* __restrict__ up,
+                                                float* __restrict__ out, size_t rows, int nb) {
+  const size_t n = rows * (size_t)(2 * nb);
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / (2 * nb);
+    const int c = (int)(i - r * (2 * nb));
+    out[i] = ((c & 1) ? up : gate)[r * nb + (c >> 1)];
   }
 }
 
 static bool swiglu_supported(int D, int F) { return D >= 256 && D % 256 == 0 && F % 128 == 0; }
 
-static int run_swiglu(const void* x, const void* w_gu, const void* w_down, const int32_t* gs, float* y, int64_t M,
-                      int D, int F, int E, void* ws, size_t ws_bytes, cudaStream_t st) {
+static size_t swiglu_ws_bytes(int64_t M, int D, int F, bool fp8) {
+  return align256((size_t)M * F * 2) + (fp8 ? align256((size_t)M * D * 2) : 0);
+}
+
+// SwiGLU experts on the two grouped GEMMs.  e4m3 weights (fp8): block
+// scales s_gu (E, D/128, 2F/128) interleaved like the weights and s_down
+// (E, F/128, D/128); the GEMMs run on f16 operands, X converted once.
+static int run_swiglu(const void* x, const void* w_gu, const void* w_down, const float* s_gu, const float* s_down,
+                      const int32_t* gs, float* y, int64_t M, int D, int F, int E, bool fp8, void* ws,
+                      size_t ws_bytes, cudaStream_t st) {
   int dev;
   DevInfo* di;
   if (int r = device_info(&dev, &di)) return r;
-  const size_t need = align256((size_t)M * F * 2);
+  const size_t need = swiglu_ws_bytes(M, D, F, fp8);
   if (ws_bytes < need) return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", ws_bytes, need);
   if (reinterpret_cast<uintptr_t>(ws) & 255u) return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
   int* status = di->status;
   const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const auto A16 = fp8 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : BF16;
+  const auto U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const int ctas = (int)g_tune_ctas;
+  const void* xa = x;
+  if (fp8) {
+    if (reinterpret_cast<uintptr_t>(x) & 15u) return fail(MOE_ERR_MISALIGNED, "x must be 16-byte aligned");
+    void* x16 = static_cast<uint8_t*>(ws) + align256((size_t)M * F * 2);
+    const size_t n8 = (size_t)M * D / 8;
+    const int blocks = (int)std::min<size_t>((n8 + 255) / 256, (size_t)di->sms * 8);
+    bf16_to_f16_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint4*>(x), static_cast<uint4*>(x16), n8);
+    MOE_CUDA_TRY(cudaGetLastError());
+    xa = x16;
+  }
   // up: H = SiLU(X @ W_gate[e]) * (X @ W_up[e]) over the interleaved (E*D, 2F) weights
   GemmMaps m1;
   memset(&m1, 0, sizeof(m1));
-  if (int r = make_map_2d(&m1.a, x, BF16, 2, (uint64_t)M, D, 64, 128)) return r;
-  if (int r = make_map_2d(&m1.b, w_gu, BF16, 2, (uint64_t)E * D, 2 * F, 64, 64)) return r;
-  GemmParams p1{gs, ws, (int)M, E, 2 * F, D, D, 8, status, nullptr, 0};
-  if (int r = launch_gemm<2, false>(m1, p1, di, st, ctas)) return r;
+  if (int r = make_map_2d(&m1.a, xa, A16, 2, (uint64_t)M, D, 64, 128)) return r;
+  if (fp8) {
+    if (int r = make_map_2d(&m1.b, w_gu, U8, 1, (uint64_t)E * D, 2 * F, 128, 64)) return r;
+  } else {
+    if (int r = make_map_2d(&m1.b, w_gu, BF16, 2, (uint64_t)E * D, 2 * F, 64, 64)) return r;
+  }
+  GemmParams p1{gs, ws, (int)M, E, 2 * F, D, D, 8, status, s_gu, 0};
+  if (int r = fp8 ? launch_gemm<2, true>(m1, p1, di, st, ctas) : launch_gemm<2, false>(m1, p1, di, st, ctas))
+    return r;
   // down: Y = H @ W_down[e]
   GemmMaps m2;
   memset(&m2, 0, sizeof(m2));
-  if (int r = make_map_2d(&m2.a, ws, BF16, 2, (uint64_t)M, F, 64, 128)) return r;
-  if (int r = make_map_2d(&m2.b, w_down, BF16, 2, (uint64_t)E * F, D, 64, 64)) return r;
-  GemmParams p2{gs, y, (int)M, E, D, F, F, 8, status, nullptr, 0};
-  return launch_gemm<1, false>(m2, p2, di, st, ctas);
+  if (int r = make_map_2d(&m2.a, ws, A16, 2, (uint64_t)M, F, 64, 128)) return r;
+  if (fp8) {
+    if (int r = make_map_2d(&m2.b, w_down, U8, 1, (uint64_t)E * F, D, 128, 64)) return r;
+  } else {
+    if (int r = make_map_2d(&m2.b, w_down, BF16, 2, (uint64_t)E * F, D, 64, 64)) return r;
+  }
+  GemmParams p2{gs, y, (int)M, E, D, F, F, 8, status, s_down, 0};
+  return fp8 ? launch_gemm<1, true>(m2, p2, di, st, ctas) : launch_gemm<1, false>(m2, p2, di, st, ctas);
 }
 
 // ------------------------------------------------------------------ small-D dispatch
@@ -1652,7 +1695,8 @@ int moe_swiglu_interleave(const void* w_gate, const void* w_up, void* w_gate_up,
   const size_t rows = (size_t)E * D, n = rows * (size_t)(F / 4);
   const int blocks = (int)std::min<size_t>((n + 255) / 256, (size_t)di->sms * 8);
   swiglu_interleave_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint4*>(w_gate), static_cast<const uint4*>(w_up), static_cast<uint4*>(w_gate_up), rows, F);
+      static_cast<const uint4*>(w_gate), static_cast<const uint4*>(w_up), static_cast<uint4*>(w_gate_up), rows, F / 8,
+      16);
   MOE_CUDA_TRY(cudaGetLastError());
   return 0;
 }
@@ -1674,8 +1718,8 @@ int moe_fused_mlp_swiglu(const void* x, const void* w_gate_up, const void* w_dow
   if (M == 0) return 0;
   if (!x || !w_gate_up || !w_down || !group_sizes || !y) return fail(MOE_ERR_INVALID_ARG, "null operand pointer");
   if (reinterpret_cast<uintptr_t>(y) & 15u) return fail(MOE_ERR_MISALIGNED, "y must be 16-byte aligned");
-  return run_swiglu(x, w_gate_up, w_down, group_sizes, y, M, D, F, E, workspace, workspace_bytes,
-                    static_cast<cudaStream_t>(stream));
+  return run_swiglu(x, w_gate_up, w_down, nullptr, nullptr, group_sizes, y, M, D, F, E, false, workspace,
+                    workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 int moe_fused_mlp_launch_count(int64_t M, int32_t D, int32_t F, int32_t E, int32_t dtype) {
@@ -1789,6 +1833,53 @@ int moe_fused_mlp_swiglu_backward(const void* x, const void* w_gate_up, const vo
     return fail(MOE_ERR_MISALIGNED, "operands must be 16-byte aligned");
   return run_swiglu_backward(x, w_gate_up, w_down, group_sizes, gu_saved, dy, dy_dtype, dx, dw_gate_up, dw_down, M, D,
                              F, E, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int moe_swiglu_interleave_fp8(const void* w_gate, const void* w_up, const float* s_gate, const float* s_up,
+                              void* w_gate_up, float* s_gate_up, int32_t E, int32_t D, int32_t F, void* stream) {
+  t_err[0] = 0;
+  if (E <= 0 || D <= 0 || F <= 0 || D % 128 || F % 128)
+    return fail(MOE_ERR_INVALID_ARG, "E=%d D=%d F=%d (D and F multiples of 128)", E, D, F);
+  if (!w_gate || !w_up || !s_gate || !s_up || !w_gate_up || !s_gate_up) return fail(MOE_ERR_INVALID_ARG, "null pointer");
+  if ((reinterpret_cast<uintptr_t>(w_gate) | reinterpret_cast<uintptr_t>(w_up) |
+       reinterpret_cast<uintptr_t>(w_gate_up)) & 15u)
+    return fail(MOE_ERR_MISALIGNED, "weights must be 16-byte aligned");
+  int dev;
+  DevInfo* di;
+  if (int r = device_info(&dev, &di)) return r;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t rows = (size_t)E * D, n = rows * (size_t)(F / 8);
+  const int blocks = (int)std::min<size_t>((n + 255) / 256, (size_t)di->sms * 8);
+  swiglu_interleave_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint4*>(w_gate), static_cast<const uint4*>(w_up),
+                                                   static_cast<uint4*>(w_gate_up), rows, F / 16, 8);
+  MOE_CUDA_TRY(cudaGetLastError());
+  const size_t srows = (size_t)E * (D / 128);
+  const int sblocks = (int)std::min<size_t>((srows * (2 * F / 128) + 255) / 256, (size_t)di->sms * 4);
+  swiglu_interleave_scales_kernel<<<sblocks, 256, 0, st>>>(s_gate, s_up, s_gate_up, srows, F / 128);
+  MOE_CUDA_TRY(cudaGetLastError());
+  return 0;
+}
+
+size_t moe_fused_mlp_swiglu_fp8_workspace_size(int64_t M, int32_t D, int32_t F) {
+  if (M < 0 || !swiglu_supported(D, F)) return 0;
+  return swiglu_ws_bytes(M, D, F, true);
+}
+
+int moe_fused_mlp_swiglu_fp8(const void* x, const void* w_gate_up, const void* w_down, const float* s_gate_up,
+                             const float* s_down, const int32_t* group_sizes, float* y, int64_t M, int32_t D,
+                             int32_t F, int32_t E, void* workspace, size_t workspace_bytes, void* stream) {
+  t_err[0] = 0;
+  if (M < 0 || D <= 0 || F <= 0 || E <= 0)
+    return fail(MOE_ERR_INVALID_ARG, "bad sizes M=%lld D=%d F=%d E=%d", (long long)M, D, F, E);
+  if (M > (int64_t)0x7fffffff) return fail(MOE_ERR_UNSUPPORTED_SHAPE, "M=%lld exceeds 2^31-1", (long long)M);
+  if (!swiglu_supported(D, F))
+    return fail(MOE_ERR_UNSUPPORTED_SHAPE, "SwiGLU experts need D %% 256 == 0 (D >= 256) and F %% 128 == 0");
+  if (M == 0) return 0;
+  if (!x || !w_gate_up || !w_down || !s_gate_up || !s_down || !group_sizes || !y)
+    return fail(MOE_ERR_INVALID_ARG, "null operand pointer");
+  if (reinterpret_cast<uintptr_t>(y) & 15u) return fail(MOE_ERR_MISALIGNED, "y must be 16-byte aligned");
+  return run_swiglu(x, w_gate_up, w_down, s_gate_up, s_down, group_sizes, y, M, D, F, E, true, workspace,
+                    workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -112,6 +112,12 @@ def lib() -> ctypes.CDLL:
     L.moe_fused_mlp_swiglu_backward.argtypes = [vp, vp, vp, vp, vp, vp, i32, vp, vp, vp, i64, i32, i32, i32, vp, sz,
                                                 vp]
     L.moe_fused_mlp_swiglu_backward.restype = ctypes.c_int
+    L.moe_swiglu_interleave_fp8.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, vp]
+    L.moe_swiglu_interleave_fp8.restype = ctypes.c_int
+    L.moe_fused_mlp_swiglu_fp8_workspace_size.argtypes = [i64, i32, i32]
+    L.moe_fused_mlp_swiglu_fp8_workspace_size.restype = sz
+    L.moe_fused_mlp_swiglu_fp8.argtypes = [vp, vp, vp, vp, vp, vp, vp, i64, i32, i32, i32, vp, sz, vp]
+    L.moe_fused_mlp_swiglu_fp8.restype = ctypes.c_int
     L.moe_ep_destroy.argtypes = [vp]
     L.moe_ep_destroy.restype = ctypes.c_int
     _lib = L

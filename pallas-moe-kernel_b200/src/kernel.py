@@ -189,15 +189,48 @@ def swiglu_interleave(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def swiglu_interleave_fp8(w_gate: torch.Tensor, w_up: torch.Tensor, s_gate: torch.Tensor, s_up: torch.Tensor):
+    """e4m3 gate and up weights (E, D, F) with their 128 x 128 block scales
+    (E, D/128, F/128) -> (w_gate_up (E, D, 2F), s_gate_up (E, D/128, 2F/128)),
+    the operands of ``fused_ragged_swiglu`` with FP8 weights."""
+    if w_gate.shape != w_up.shape or w_gate.dim() != 3 or s_gate.shape != s_up.shape:
+        raise ValueError("gate and up weights (and scales) must have the same shapes")
+    if _FP8 is None or w_gate.dtype != _FP8 or w_up.dtype != _FP8:
+        raise TypeError("weights must be float8_e4m3fn")
+    E, D, F = w_gate.shape
+    if tuple(s_gate.shape) != (E, D // 128, F // 128):
+        raise ValueError(f"scales must be (E, D/128, F/128) = {(E, D // 128, F // 128)}")
+    dev = w_gate.device
+    w_gate, w_up = w_gate.contiguous(), w_up.contiguous()
+    s_gate = s_gate.to(device=dev, dtype=torch.float32).contiguous()
+    s_up = s_up.to(device=dev, dtype=torch.float32).contiguous()
+    w = torch.empty((E, D, 2 * F), device=dev, dtype=_FP8)
+    sc = torch.empty((E, D // 128, 2 * F // 128), device=dev, dtype=torch.float32)
+    with torch.cuda.device(dev):
+        rc = _lib.lib().moe_swiglu_interleave_fp8(
+            w_gate.data_ptr(), w_up.data_ptr(), s_gate.data_ptr(), s_up.data_ptr(), w.data_ptr(), sc.data_ptr(),
+            E, D, F, _stream_handle(dev))
+    _lib.check(rc)
+    return w, sc
+
+
 def fused_ragged_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor, group_sizes,
-                        *, out: Optional[torch.Tensor] = None,
+                        *, w_gate_up_scale: Optional[torch.Tensor] = None,
+                        w_down_scale: Optional[torch.Tensor] = None,
+                        out: Optional[torch.Tensor] = None,
                         workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
     """SwiGLU experts: ``Y = ragged_dot(silu(X W_gate) * (X W_up), W_down)``.
 
     x (M, D) bf16, w_gate_up (E, D, 2F) bf16 from ``swiglu_interleave``,
-    w_down (E, F, D) bf16, group_sizes (E,) -> y (M, D) f32.  Same ragged
-    semantics as ``fused_ragged_mlp``; D a multiple of 256, F of 128.
+    w_down (E, F, D) bf16, group_sizes (E,) -> y (M, D) f32.  With
+    float8_e4m3fn weights pass their block scales: w_gate_up_scale
+    (E, D/128, 2F/128) from ``swiglu_interleave_fp8`` and w_down_scale
+    (E, F/128, D/128).  Same ragged semantics as ``fused_ragged_mlp``; D a
+    multiple of 256, F of 128.
     """
+    if _FP8 is not None and w_gate_up.dtype == _FP8:
+        return _fused_ragged_swiglu_fp8(x, w_gate_up, w_down, group_sizes, w_gate_up_scale, w_down_scale, out,
+                                        workspace)
     if not x.is_cuda:
         raise ValueError("fused_ragged_swiglu runs on CUDA tensors only (no CPU path)")
     M, D = x.shape
@@ -230,6 +263,40 @@ def fused_ragged_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.
             ctypes.c_void_p(w_down.data_ptr()), ctypes.c_void_p(gs.data_ptr()), ctypes.c_void_p(out.data_ptr()),
             M, D, F, E, ctypes.c_void_p(workspace.data_ptr() if ws_bytes else 0), ws_bytes,
             ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream))
+    _lib.check(rc)
+    return out
+
+
+def _fused_ragged_swiglu_fp8(x, w_gate_up, w_down, group_sizes, s_gu, s_down, out, workspace):
+    if not x.is_cuda:
+        raise ValueError("fused_ragged_swiglu runs on CUDA tensors only (no CPU path)")
+    if s_gu is None or s_down is None:
+        raise ValueError("FP8 weights need w_gate_up_scale and w_down_scale")
+    M, D = x.shape
+    E, D2, F2 = w_gate_up.shape
+    F = F2 // 2
+    if D != D2 or F2 % 2 or tuple(w_down.shape) != (E, F, D) or x.dtype != torch.bfloat16 or w_down.dtype != _FP8:
+        raise ValueError(f"expected bf16 x (M, D), e4m3 w_gate_up (E, D, 2F) and w_down (E, F, D); got "
+                         f"{tuple(x.shape)} {x.dtype}, {tuple(w_gate_up.shape)}, {tuple(w_down.shape)} {w_down.dtype}")
+    dev = x.device
+    x, w_gate_up, w_down = x.contiguous(), w_gate_up.contiguous(), w_down.contiguous()
+    s_gu = s_gu.to(device=dev, dtype=torch.float32).contiguous()
+    s_down = s_down.to(device=dev, dtype=torch.float32).contiguous()
+    gs = _as_device_group_sizes(group_sizes, dev)
+    if gs.numel() != E:
+        raise ValueError(f"group_sizes has {gs.numel()} entries, expected E={E}")
+    if out is None:
+        out = torch.empty((M, D), device=dev, dtype=torch.float32)
+    elif out.shape != (M, D) or out.dtype != torch.float32 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous (M, D) float32 tensor")
+    L = _lib.lib()
+    ws_bytes = int(L.moe_fused_mlp_swiglu_fp8_workspace_size(M, D, F))
+    if ws_bytes and (workspace is None or workspace.numel() * workspace.element_size() < ws_bytes):
+        workspace = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    with torch.cuda.device(dev):
+        rc = L.moe_fused_mlp_swiglu_fp8(x.data_ptr(), w_gate_up.data_ptr(), w_down.data_ptr(), s_gu.data_ptr(),
+                                        s_down.data_ptr(), gs.data_ptr(), out.data_ptr(), M, D, F, E,
+                                        workspace.data_ptr() if ws_bytes else None, ws_bytes, _stream_handle(dev))
     _lib.check(rc)
     return out
 

@@ -126,3 +126,70 @@ def test_swiglu_mixtral_shape_sampled_rows():
         gots.append(y[rows].cpu().numpy())
     m = orc.correctness_metrics(np.concatenate(refs), np.concatenate(gots))
     assert m["fused_is_finite"] and m["l2_relative_error"] <= TOL, m
+
+
+# ----------------------------------------------------------------------------- e4m3 weights (DeepSeek-V3 format)
+from src.kernel import swiglu_interleave_fp8  # noqa: E402
+from src.routing import dequantize_e4m3_blockwise, quantize_e4m3_blockwise  # noqa: E402
+
+FP8_TOL = 2e-2  # the FP8 bar of this library, against the dequantised weights
+
+
+def _fp8_weights(E, D, F, seed):
+    wg, wu, wd = _weights(E, D, F, seed)
+    (qg, sg), (qu, su), (qd, sd) = (quantize_e4m3_blockwise(w.float()) for w in (wg, wu, wd))
+    return (qg, sg), (qu, su), (qd, sd)
+
+
+def test_fp8_interleave_bit_exact():
+    E, D, F = 3, 256, 384
+    (qg, sg), (qu, su), _ = _fp8_weights(E, D, F, seed=11)
+    w, s = swiglu_interleave_fp8(qg, qu, sg, su)
+    torch.cuda.synchronize()
+    ref = orc.swiglu_interleave(qg.view(torch.uint8).cpu().numpy(), qu.view(torch.uint8).cpu().numpy())
+    np.testing.assert_array_equal(w.view(torch.uint8).cpu().numpy(), ref)
+    ref_s = orc.swiglu_interleave(np.repeat(sg.cpu().numpy(), 128, axis=2), np.repeat(su.cpu().numpy(), 128, axis=2))
+    np.testing.assert_array_equal(s.cpu().numpy(), ref_s[:, :, ::128])
+
+
+@pytest.mark.parametrize("M,D,F,E,gs", [(2048, 512, 512, 4, None), (1536, 768, 384, 3, None),
+                                        (1024, 512, 256, 4, [0, 700, 0, 5]), (1024, 512, 256, 4, [300, 0, 0, 0])])
+def test_fp8_swiglu_matches_oracle_on_dequantised_weights(M, D, F, E, gs):
+    gs = make_group_sizes(M, E) if gs is None else np.asarray(gs, np.int32)
+    (qg, sg), (qu, su), (qd, sd) = _fp8_weights(E, D, F, seed=M + F)
+    wgu, sgu = swiglu_interleave_fp8(qg, qu, sg, su)
+    x = _x(M, D, seed=F)
+    out = torch.full((M, D), float("nan"), device=DEV)
+    y = fused_ragged_swiglu(x, wgu, qd, torch.from_numpy(gs).to(DEV), w_gate_up_scale=sgu, w_down_scale=sd, out=out)
+    torch.cuda.synchronize()
+    y = y.cpu().numpy()
+    n = int(gs.sum())
+    assert np.all(np.isfinite(y)) and np.all(y[n:] == 0.0)
+    deq = [dequantize_e4m3_blockwise(q, s).cpu().numpy() for q, s in ((qg, sg), (qu, su), (qd, sd))]
+    ref = orc.ref_ragged_swiglu(_np(x), *deq, gs)
+    if n:
+        m = orc.correctness_metrics(ref[:n], y[:n])
+        assert m["l2_relative_error"] <= FP8_TOL, m
+
+
+def test_fp8_swiglu_deepseek_shape_sampled_rows():
+    """DeepSeek-V3 expert shape (D=7168, F=2048) with 16 experts of a
+    top-8-of-2048 routing (M=16384); 12 sampled rows per expert."""
+    M, D, F, E = 16384, 7168, 2048, 16
+    gs = make_group_sizes(M, E)
+    (qg, sg), (qu, su), (qd, sd) = _fp8_weights(E, D, F, seed=5)
+    wgu, sgu = swiglu_interleave_fp8(qg, qu, sg, su)
+    x = _x(M, D, seed=5)
+    y = fused_ragged_swiglu(x, wgu, qd, torch.from_numpy(gs).to(DEV), w_gate_up_scale=sgu, w_down_scale=sd)
+    torch.cuda.synchronize()
+    offs = orc.group_sizes_to_offsets(gs)
+    rng = np.random.default_rng(2)
+    refs, gots = [], []
+    for e in range(E):
+        a, b = int(offs[e]), int(offs[e + 1])
+        rows = np.unique(np.concatenate([rng.integers(a, b, 10), [a, b - 1]]))
+        deq = [dequantize_e4m3_blockwise(q[e:e + 1], s[e:e + 1]).cpu().numpy() for q, s in ((qg, sg), (qu, su), (qd, sd))]
+        refs.append(orc.ref_ragged_swiglu(_np(x[rows]), *deq, [len(rows)]))
+        gots.append(y[rows].cpu().numpy())
+    m = orc.correctness_metrics(np.concatenate(refs), np.concatenate(gots))
+    assert m["fused_is_finite"] and m["l2_relative_error"] <= FP8_TOL, m
