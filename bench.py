@@ -593,26 +593,43 @@ def run_swiglu(args, cfg, device) -> dict:
     experts' three weight matrices + Y (H is an intermediate)."""
     import torch
     from src import _lib
-    from src.kernel import fused_ragged_swiglu, swiglu_interleave
-    from src.routing import config_group_sizes
+    from src.kernel import fused_ragged_swiglu, swiglu_interleave, swiglu_interleave_fp8
+    from src.routing import config_group_sizes, quantize_e4m3_blockwise
 
     gs = config_group_sizes(cfg, seed=0)
     g = torch.Generator(device=device)
     g.manual_seed(1234)
     x = torch.randn((cfg.M, cfg.D), generator=g, device=device).to(torch.bfloat16)
-    w_gate = (torch.randn((cfg.E, cfg.D, cfg.F), generator=g, device=device) / math.sqrt(cfg.D)).to(torch.bfloat16)
-    w_up = (torch.randn((cfg.E, cfg.D, cfg.F), generator=g, device=device) / math.sqrt(cfg.D)).to(torch.bfloat16)
-    w_down = (torch.randn((cfg.E, cfg.F, cfg.D), generator=g, device=device) / math.sqrt(cfg.F)).to(torch.bfloat16)
-    w_gu = swiglu_interleave(w_gate, w_up)
-    del w_gate, w_up
+    fp8 = cfg.dtype == "fp8"
+    sc = {}
+    if fp8:  # e4m3 weights with 128 x 128 block scales, built one expert at a time
+        E, D, F = cfg.E, cfg.D, cfg.F
+        q = [torch.empty(shape, device=device, dtype=torch.float8_e4m3fn) for shape in ((E, D, F), (E, D, F), (E, F, D))]
+        s = [torch.empty(shape, device=device) for shape in ((E, D // 128, F // 128), (E, D // 128, F // 128),
+                                                            (E, F // 128, D // 128))]
+        for e in range(E):
+            for i, (r, c, fan) in enumerate(((D, F, D), (D, F, D), (F, D, F))):
+                q[i][e], s[i][e] = quantize_e4m3_blockwise(torch.randn((r, c), generator=g, device=device)
+                                                           / math.sqrt(fan))
+        w_gu, s_gu = swiglu_interleave_fp8(q[0], q[1], s[0], s[1])
+        w_down = q[2]
+        sc = {"w_gate_up_scale": s_gu, "w_down_scale": s[2]}
+        del q[0:2], s[0:2]
+        ws_bytes = _lib.lib().moe_fused_mlp_swiglu_fp8_workspace_size(cfg.M, cfg.D, cfg.F)
+    else:
+        w_gate = (torch.randn((cfg.E, cfg.D, cfg.F), generator=g, device=device) / math.sqrt(cfg.D)).to(torch.bfloat16)
+        w_up = (torch.randn((cfg.E, cfg.D, cfg.F), generator=g, device=device) / math.sqrt(cfg.D)).to(torch.bfloat16)
+        w_down = (torch.randn((cfg.E, cfg.F, cfg.D), generator=g, device=device) / math.sqrt(cfg.F)).to(torch.bfloat16)
+        w_gu = swiglu_interleave(w_gate, w_up)
+        del w_gate, w_up
+        ws_bytes = _lib.lib().moe_fused_mlp_swiglu_workspace_size(cfg.M, cfg.D, cfg.F)
     gs_dev = torch.from_numpy(gs).to(device)
     y = torch.empty((cfg.M, cfg.D), device=device)
-    ws = torch.empty(int(_lib.lib().moe_fused_mlp_swiglu_workspace_size(cfg.M, cfg.D, cfg.F)), dtype=torch.uint8,
-                     device=device)
+    ws = torch.empty(int(ws_bytes), dtype=torch.uint8, device=device)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     st = torch.cuda.current_stream(device)
     for _ in range(args.warmup):
-        fused_ragged_swiglu(x, w_gu, w_down, gs_dev, out=y, workspace=ws)
+        fused_ragged_swiglu(x, w_gu, w_down, gs_dev, out=y, workspace=ws, **sc)
     torch.cuda.synchronize(device)
     clocks = ClockSampler(device.index)
     clocks.start()
@@ -623,7 +640,7 @@ def run_swiglu(args, cfg, device) -> dict:
         flush.zero_()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(st)
-        fused_ragged_swiglu(x, w_gu, w_down, gs_dev, out=y, workspace=ws)
+        fused_ragged_swiglu(x, w_gu, w_down, gs_dev, out=y, workspace=ws, **sc)
         b.record(st)
         torch.cuda.synchronize(device)
         times.append(a.elapsed_time(b))
@@ -636,15 +653,17 @@ def run_swiglu(args, cfg, device) -> dict:
     peak = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
     flops = 6 * cfg.M * cfg.D * cfg.F
     active = int(np.count_nonzero(gs > 0))
-    byts = cfg.M * cfg.D * 2 + active * 3 * cfg.D * cfg.F * 2 + cfg.M * cfg.D * 4
+    wbytes = 1 if fp8 else 2
+    byts = cfg.M * cfg.D * 2 + active * 3 * cfg.D * cfg.F * wbytes + cfg.M * cfg.D * 4
     achieved = flops / (ms / 1e3) / 1e12
     return {
         "metric": "routed_tokens_per_s", "value": cfg.M / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "dtype": "bf16", "data": "synthetic (seeded N(0,1) X, N(0,1/D) / N(0,1/F) weights)",
+        "dtype": "fp8 e4m3 weights, f16 operands" if fp8 else "bf16",
+        "data": "synthetic (seeded N(0,1) X, N(0,1/D) / N(0,1/F) weights)",
         "config": {"workload": f"{cfg.name}_swiglu", "M": cfg.M, "D": cfg.D, "F": cfg.F, "E": cfg.E,
                    "activation": "swiglu", "l2": "flushed before every step (256 MiB write)"},
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": (3 if fp8 else 2) * args.steps,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": None, "algorithmic_flops": flops,
                      "algorithmic_bytes": byts, "peak_source": f"{peak_src}: bf16_tflops",
