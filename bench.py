@@ -119,6 +119,51 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(win)}
 
 
+class DeviceClock:
+    """SM clock measured on the device: one-thread blocks record (SM id,
+    clock64, globaltimer) before and after a region on the launching stream;
+    per SM, cycles / nanoseconds is the clock averaged over the region (the
+    cycle counter is per SM, so only SMs seen in both samples count).  Unlike
+    NVML's sampled clock it covers the whole region and nothing else."""
+
+    def __init__(self, device):
+        import torch
+        from src import _lib
+        self.L = _lib.lib()
+        self.device = device
+        self.blocks = min(1024, 2 * torch.cuda.get_device_properties(device).multi_processor_count)
+
+    def sample(self, stream):
+        import ctypes
+        import torch
+        buf = torch.zeros(3 * self.blocks, dtype=torch.int64, device=self.device)
+        rc = self.L.moe_sm_clock_sample(ctypes.c_void_p(buf.data_ptr()), self.blocks,
+                                        ctypes.c_void_p(stream.cuda_stream))
+        if rc != 0:
+            raise RuntimeError(self.L.moe_last_error().decode())
+        return buf
+
+    @staticmethod
+    def mhz(a, b) -> dict:
+        first = {}
+        for sm, cyc, ns in a.cpu().view(-1, 3).tolist():
+            first.setdefault(sm, (cyc, ns))
+        rates = []
+        seen = set()
+        for sm, cyc, ns in b.cpu().view(-1, 3).tolist():
+            if sm in first and sm not in seen and ns > first[sm][1]:
+                seen.add(sm)
+                rates.append((cyc - first[sm][0]) / (ns - first[sm][1]) * 1e3)
+        if not rates:
+            return {"sm_mhz": None, "sms": 0}
+        return {"sm_mhz": statistics.median(rates), "sm_mhz_min": min(rates), "sm_mhz_max": max(rates),
+                "sms": len(rates)}
+
+
+# dense kind::f16 MMA rate per SM and clock cycle (M=128, N=256, K=16 in 128 cycles)
+F16_FLOP_PER_CLK_SM = 8192
+
+
 # --------------------------------------------------------------------- workload
 def make_workload(cfg, device, seed: int = 0, experts=None):
     """Seeded synthetic inputs on the device: X ~ N(0,1) (M, D) and the routed
@@ -240,6 +285,7 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
     torch.cuda.synchronize(device)
     _lib.device_status(reset=True)
 
+    dclk = DeviceClock(device)
     clocks = ClockSampler(device.index)
     clocks.start()
     time.sleep(0.05)
@@ -247,16 +293,37 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
         dist.barrier()
     torch.cuda.synchronize(device)
     t0 = time.perf_counter()
+    c_a = dclk.sample(stream)   # outside the step events: not part of any step's time
     step_ms = timed(step_fn, args.steps)
+    c_b = dclk.sample(stream)
     t1 = time.perf_counter()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(device)
     clocks.stop()
     total_ms = float(sum(step_ms))
+    step_clock = DeviceClock.mhz(c_a, c_b)
     if launches_per_step is None:
         launches_per_step = layer.last_launches
-    kern_ms = timed(kern_fn, args.steps) if kern_fn else None
+    rl = None
+    if kern_fn:
+        # Roofline leg: the dominant kernel(s) alone (weights prepared) and
+        # the whole step, alternated launch by launch in one region so both
+        # run at the same clock; the region's clock is measured on the device.
+        k_ev, s_ev = [], []
+        r_a = dclk.sample(stream)
+        for _ in range(args.steps):
+            for fn, evs in ((step_fn, s_ev), (kern_fn, k_ev)):
+                flush.zero_()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                fn()
+                b.record(stream)
+                evs.append((a, b))
+        r_b = dclk.sample(stream)
+        torch.cuda.synchronize(device)
+        rl = {"kern_ms": [a.elapsed_time(b) for a, b in k_ev], "step_ms": [a.elapsed_time(b) for a, b in s_ev],
+              "clock": DeviceClock.mhz(r_a, r_b)}
     status = _lib.device_status(reset=True)
     if status:
         raise RuntimeError(f"device status {status} after the timed region")
@@ -345,14 +412,21 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
         "useful_tflops": alg["flops"] * world / (ms_per_step / 1e3) / 1e12,
         "gpu_launches": launches_per_step * args.steps,
     }
-    if kern_ms is not None:
-        k_avg = statistics.mean(kern_ms)
+    if rl is not None:
+        k_avg = statistics.mean(rl["kern_ms"])
+        s_avg = statistics.mean(rl["step_ms"])
         peak, basis = tensor_peak(cfg, peaks)
         achieved = alg["flops"] / (k_avg / 1e3) / 1e12
         t_mem = alg["bytes"] / (float(peaks["hbm_gbs"]) * 1e9)
         t_cmp = alg["flops"] / (peak * 1e12)
-        kname = ("fused_mlp_small_kernel" if cfg.D <= 256
+        kname = ("fused_mlp_small_kernel" if cfg.D in (64, 128, 256)
                  else "grouped_gemm_pair_kernel (up + down launches of one step)")
+        mhz = rl["clock"].get("sm_mhz")
+        sms = torch.cuda.get_device_properties(device).multi_processor_count
+        # The tensor peak at the clock the region ran at (kind::f16 rate; the
+        # 3xTF32 path: a sixth of it).
+        clk_peak = (F16_FLOP_PER_CLK_SM * sms * mhz * 1e6 / 1e12 / (6.0 if cfg.dtype == "f32" else 1.0)
+                    if mhz else None)
         line["roofline"] = {
             "bound": "tensor" if t_cmp >= t_mem else "hbm",
             "kernel": kname,
@@ -362,7 +436,16 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
             "kernel_ms": k_avg, "algorithmic_flops": alg["flops"], "algorithmic_bytes": alg["bytes"],
             "hbm_frac": (alg["bytes"] / (k_avg / 1e3)) / (float(peaks["hbm_gbs"]) * 1e9),
             "traffic": None,
+            "timing": "kernel leg and whole step alternated launch by launch in one region "
+                      f"({args.steps} each, L2 flushed before each)",
+            "step_ms_same_region": s_avg,
+            "kernel_le_step": bool(k_avg <= s_avg * 1.005),
+            "sm_mhz_device": mhz,
+            "tensor_peak_at_clock": clk_peak,
+            "frac_at_clock": achieved / clk_peak if clk_peak else None,
         }
+        if not line["roofline"]["kernel_le_step"]:
+            print(f"warning: kernel leg {k_avg:.3f} ms > step {s_avg:.3f} ms in the same region", file=sys.stderr)
         prof = REPO / "profiles" / f"traffic_{cfg.name}.json"
         if prof.exists():
             try:
@@ -370,6 +453,8 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
             except Exception:
                 pass
     line["clocks"] = clocks.summary(t0, t1)
+    line["clocks"]["sm_mhz_device"] = step_clock.get("sm_mhz")
+    line["clocks"]["device_sms_sampled"] = step_clock.get("sms")
     h2d = cfg.M * cfg.D * x.element_size() + gs_np.nbytes
     line["e2e"] = {"value": world * cfg.M * args.steps / (e2e_ms / 1e3), "unit": "tokens/s",
                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": cfg.M * cfg.D * 4,
@@ -684,11 +769,19 @@ def cpu_reference(cfg, budget_s: float, seed: int = 0) -> dict:
     from src.routing import config_group_sizes
 
     gs = config_group_sizes(cfg, seed=seed)
-    # Bounded sample: the first `rows` routed rows (whole experts in order).
+    # Bounded sample: the first routed rows in expert order, always whole
+    # experts and at least one (so BLAS runs at the expert's real M), up to
+    # about 30 GFLOP per timed call when one expert is smaller than that.
     rng = np.random.default_rng(seed)
     per_row_flops = 4 * cfg.D * cfg.F
-    rows = int(min(cfg.M, max(128, 3e10 / per_row_flops)))  # ~30 GFLOP per timed call at most
     offs = np.concatenate([[0], np.cumsum(gs)])
+    target = min(cfg.M, 3e10 / per_row_flops)
+    rows = 0
+    for e in range(cfg.E):
+        rows = int(offs[e + 1])
+        if rows >= target and rows > 0:
+            break
+    rows = max(1, min(rows, cfg.M))
     gs_s = np.clip(np.minimum(offs[1:], rows) - np.minimum(offs[:-1], rows), 0, None).astype(np.int32)
     active = np.nonzero(gs_s)[0]
     x = rng.standard_normal((rows, cfg.D), dtype=np.float32)
@@ -716,8 +809,8 @@ def cpu_reference(cfg, budget_s: float, seed: int = 0) -> dict:
     if limiter is not None:
         limiter.restore_original_limits()
     return {"value": rows / med, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"{rows} of {cfg.M} routed rows ({len(active)} experts), f32 numpy/BLAS, "
-                      f"median of {len(times)} calls",
+            "sample": f"{rows} of {cfg.M} routed rows ({len(active)} whole experts), f32 numpy/BLAS, "
+                      f"median of {len(times)} calls; tokens/s = rows / seconds per call",
             "seconds_per_call": med}
 
 

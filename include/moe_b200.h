@@ -117,6 +117,8 @@ int moe_fused_mlp_prepared(const void* x, const void* w_up, const void* w_down, 
  * MOE_ERR_WORKSPACE_TOO_SMALL, and moe_fused_mlp with a workspace is the way).
  * The first call on a device looks up the scratch array's device address
  * (cudaGetSymbolAddress), so make that first call before any stream capture.
+ * After cudaDeviceReset the next call looks it up again (the array is a new
+ * allocation of the new context and starts with undefined contents).
  * All calls share the one array: calls that can overlap on the GPU (other
  * streams, other host threads on the same device) race on it and must be
  * serialised by the caller.  Nothing in it has to start zeroed -- each call
@@ -347,6 +349,17 @@ int moe_device_status(int reset);
 
 /* Library version: major * 10000 + minor * 100 + patch. */
 int moe_version(void);
+
+/*
+ * Clock evidence for benchmarks (no counterpart in the reference).  Launches
+ * `blocks` one-thread blocks on `stream`; block b writes out[3 b .. 3 b + 2]
+ * = {SM id, the SM's cycle counter (clock64), the global nanosecond timer}.
+ * Two samples taken around a region on the same stream give, for every SM
+ * that appears in both, the SM clock averaged over the region:
+ * cycles / nanoseconds.  `out` is device memory of 3 * blocks uint64 values;
+ * blocks in 1 .. 1024.  Returns 0 or a negative MOE_ERR_* code.
+ */
+int moe_sm_clock_sample(uint64_t* out, int32_t blocks, void* stream);
 
 /*
  * Tuning overrides for tests and benchmarks (0 restores the automatic

@@ -284,6 +284,13 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
           // Wait for every peer whose rows of this expert meet this CTA's 128
           // rows (a peer's flag covers all its rows of this step), then order
           // the TMA reads after the peer's stores.
+          // The A box still spans all 128 rows, so in the expert's last row
+          // block it also reads rows past the expert's end: the next expert's
+          // rows, possibly from sources not waited for here and still being
+          // written over NVLink.  That is correct only because each output
+          // row depends on its own A row alone and the epilogue never stores
+          // rows past the expert's end; an epilogue that mixes rows (or a
+          // split-K sum) would have to wait for those sources as well.
           const EpDispatch& d = p.dispatch;
           for (int s = 0; s < d.world && ok; ++s) {
             if (s == d.rank || (arrived >> s) & 1u) continue;

@@ -60,6 +60,27 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// The current context of the calling thread (driver API through the runtime's
+// entry-point query, so the library links no libcuda).  Per-device caches
+// below remember the context they were filled in: after cudaDeviceReset the
+// primary context is rebuilt, modules reload (device symbols may move) and
+// function attributes are gone, so a cache from the old context is refilled.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+static CUcontext current_ctx() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  CUcontext c = nullptr;
+  if (fn) fn(&c);
+  return c;
+}
+
 // Encoded maps of recent calls, per host thread: a map is a pure function of
 // (base, type, shape, box), so a hit skips the driver call.  Weights,
 // workspaces and reused activation buffers hit on repeated calls.
@@ -115,6 +136,7 @@ static int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType d
 
 // ------------------------------------------------------------------ device info
 struct DevInfo {
+  CUcontext ctx = nullptr;  // context the entries below belong to
   int sms = 0;
   int* status = nullptr;  // device address of g_status on this device
   bool attr_set[40] = {};
@@ -127,8 +149,12 @@ static int device_info(int* dev_out, DevInfo** info) {
   int dev = 0;
   MOE_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return fail(MOE_ERR_CUDA, "device ordinal %d out of range", dev);
+  // cudaGetDevice above made the device's primary context current (or kept
+  // the caller's), so the context read here is the one kernels launch in.
+  const CUcontext ctx = current_ctx();
   std::lock_guard<std::mutex> lk(g_dev_mu);
-  if (g_dev[dev].sms == 0) {
+  if (g_dev[dev].sms == 0 || g_dev[dev].ctx != ctx) {
+    g_dev[dev] = DevInfo();
     int sms = 0;
     MOE_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     int major = 0, minor = 0;
@@ -141,6 +167,7 @@ static int device_info(int* dev_out, DevInfo** info) {
     MOE_CUDA_TRY(cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_status));
     g_dev[dev].status = status;
     g_dev[dev].sms = sms;
+    g_dev[dev].ctx = ctx;
   }
   *dev_out = dev;
   *info = &g_dev[dev];
@@ -941,22 +968,26 @@ constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 // In host code `g_noalloc_scratch` only names a host-side stand-in, so its
-// device address is looked up once per device (with that device current)
-// and cached here.
+// device address is looked up per device (with that device current) and
+// cached here together with the context it was resolved in; a new context
+// (after cudaDeviceReset) resolves it again.
 static void* g_noalloc_ptr[64] = {};
+static CUcontext g_noalloc_ctx[64] = {};
 static std::mutex g_noalloc_mu;
 
 static int noalloc_scratch(void** out) {
   int dev = 0;
   MOE_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return fail(MOE_ERR_CUDA, "device ordinal %d out of range", dev);
+  const CUcontext ctx = current_ctx();
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
+  if (!g_noalloc_ptr[dev] || g_noalloc_ctx[dev] != ctx) {
     void* ptr = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
     if (e != cudaSuccess || !ptr)
       return fail(MOE_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed: %s", cudaGetErrorString(e));
     g_noalloc_ptr[dev] = ptr;
+    g_noalloc_ctx[dev] = ctx;
   }
   *out = g_noalloc_ptr[dev];
   return 0;
@@ -1057,9 +1088,31 @@ static int ep_check_device(const moe_ep_s* ep) {
 
 using namespace moe;
 
+namespace moe {
+// One sample per block: {SM id, SM cycle counter, global ns timer}.
+__global__ void sm_clock_sample_kernel(uint64_t* out) {
+  uint32_t smid;
+  uint64_t ns;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(ns));
+  const uint64_t cyc = clock64();
+  out[3 * blockIdx.x] = smid;
+  out[3 * blockIdx.x + 1] = cyc;
+  out[3 * blockIdx.x + 2] = ns;
+}
+}  // namespace moe
+
 extern "C" {
 
 const char* moe_last_error(void) { return t_err; }
+
+int moe_sm_clock_sample(uint64_t* out, int32_t blocks, void* stream) {
+  t_err[0] = 0;
+  if (!out || blocks < 1 || blocks > 1024) return fail(MOE_ERR_INVALID_ARG, "out=%p blocks=%d", out, blocks);
+  sm_clock_sample_kernel<<<blocks, 1, 0, static_cast<cudaStream_t>(stream)>>>(out);
+  MOE_CUDA_TRY(cudaGetLastError());
+  return 0;
+}
 
 int moe_version(void) { return 100; }
 

@@ -61,6 +61,8 @@ def lib() -> ctypes.CDLL:
     L.moe_last_error.restype = ctypes.c_char_p
     L.moe_device_status.argtypes = [ctypes.c_int]
     L.moe_device_status.restype = ctypes.c_int
+    L.moe_sm_clock_sample.argtypes = [vp, i32, vp]
+    L.moe_sm_clock_sample.restype = ctypes.c_int
     L.moe_version.argtypes = []
     L.moe_version.restype = ctypes.c_int
     L.moe_set_tuning.argtypes = [i32, i64]

@@ -23,15 +23,15 @@ def make_group_sizes(M: int, E: int, group_fractions: Optional[Sequence[float]] 
     """Largest-remainder split of M rows over E experts
     (``src/benchmark.py:42-91``)."""
     if M < E:
-        raise ValueError(f"M={M} must be at least E={E} so every expert can receive at least one token.")
+        raise ValueError(f"need M >= E to give each of the {E} experts a row (M={M})")
     if group_fractions is None:
         weights = np.linspace(0.85, 1.15, E, dtype=np.float64)
     else:
         weights = np.asarray(group_fractions, dtype=np.float64)
         if weights.shape != (E,):
-            raise ValueError(f"group_fractions must have shape ({E},), but received {weights.shape}.")
+            raise ValueError(f"group_fractions: expected {E} values, got shape {weights.shape}")
         if np.any(weights <= 0):
-            raise ValueError("Every group fraction must be positive.")
+            raise ValueError("group_fractions: all values must be > 0")
     weights = weights / weights.sum()
     exact = M * weights
     sizes = np.floor(exact).astype(np.int32)
@@ -59,7 +59,7 @@ def routing_weights(E: int, pattern: str) -> np.ndarray:
             w = np.full(E, 0.30 / (E - 1), dtype=np.float64)
             w[0] = 0.70
     else:
-        raise ValueError(f"Unknown routing pattern: {pattern}")
+        raise ValueError(f"routing pattern {pattern!r} is not one of balanced, mild, skewed, one_dominant")
     return w / w.sum()
 
 
@@ -67,7 +67,7 @@ def make_group_sizes_pattern(M: int, E: int, pattern: str) -> np.ndarray:
     """At least one token per expert, the rest by largest remainders
     (``src/ragged_moe_speedup_experiment.py:475-493``)."""
     if M < E:
-        raise ValueError(f"M={M} must be at least E={E}.")
+        raise ValueError(f"need M >= E (M={M}, E={E})")
     w = routing_weights(E, pattern)
     remaining = M - E
     exact = remaining * w
@@ -78,7 +78,7 @@ def make_group_sizes_pattern(M: int, E: int, pattern: str) -> np.ndarray:
         extra[order[:rem]] += 1
     sizes = (extra + 1).astype(np.int32)
     if int(sizes.sum()) != M:
-        raise AssertionError("Internal routing allocation error.")
+        raise AssertionError(f"group sizes sum to {int(sizes.sum())}, expected {M}")
     return sizes
 
 

@@ -1,27 +1,45 @@
-"""Generates the golden fixtures that pin the host-side routing generators.
+"""Generates the fixtures that pin the host-side routing generators and the
+structured sweep's comparison table.
 
-Reads the reference's own sources from /root/reference (this container only;
-the fixtures travel, the reference does not):
+Reads a checkout of the reference (Krushna-B/pallas-moe-kernel), given as the
+first argument or in the environment variable ``MOE_REFERENCE_DIR``; only the
+fixtures it writes are committed and travel, the reference does not:
 
 * executes ``make_group_sizes`` (src/benchmark.py:42-91) and
   ``routing_weights`` / ``make_group_sizes`` (src/ragged_moe_speedup_experiment.py:455-493)
   -- plain numpy functions, extracted with ``ast`` because their modules
   import JAX at the top -- on a grid of inputs;
 * collects the group sizes the reference recorded in
-  results/structured_float32/results.csv (M, E, routing pattern -> sizes).
+  results/structured_float32/results.csv (M, E, routing pattern -> sizes);
+* writes ``pallas-moe-kernel_b200/src/data/l4_structured_float32.json``: per
+  shape of that published sweep (measured on an NVIDIA L4), the fused
+  kernel's best median over the swept (BM, BF) tiles and the median of the
+  unfused ``ragged_dot`` reference, which ``src/sweep.py`` compares against.
 
-Run:  python tests/golden/make_golden.py
+Run:  python tests/golden/make_golden.py <reference checkout>
 """
 
 import ast
 import csv
 import json
+import os
+import sys
 from pathlib import Path
 
 import numpy as np
 
-REF = Path("/root/reference")
 OUT = Path(__file__).resolve().parent
+L4_TABLE = OUT.parent.parent / "pallas-moe-kernel_b200" / "src" / "data" / "l4_structured_float32.json"
+
+
+def _reference_dir() -> Path:
+    arg = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("MOE_REFERENCE_DIR")
+    if not arg:
+        raise SystemExit("usage: make_golden.py <reference checkout> (or set MOE_REFERENCE_DIR)")
+    ref = Path(arg)
+    if not (ref / "src" / "benchmark.py").exists():
+        raise SystemExit(f"{ref} does not look like a checkout of the reference (no src/benchmark.py)")
+    return ref
 
 
 def _load_functions(path, names):
@@ -33,7 +51,32 @@ def _load_functions(path, names):
     return ns
 
 
+def write_l4_table(ref: Path) -> int:
+    """Per-shape summary of the reference's published L4 sweep."""
+    import pandas as pd
+
+    src = ref / "results" / "structured_float32"
+    r = pd.read_csv(src / "results.csv")
+    rows = []
+    for (M, D, F, E, pat), g in r.groupby(["M", "D", "F", "E", "group_pattern"]):
+        best = g.loc[g.fused_median_ms.idxmin()]
+        rows.append({"M": int(M), "D": int(D), "F": int(F), "E": int(E), "pattern": pat,
+                     "fused_median_ms": float(best.fused_median_ms), "BM": int(best.BM), "BF": int(best.BF),
+                     "ref_median_ms": float(g.ref_median_ms.median()), "tiles": int(len(g)),
+                     "group_sizes": json.loads(best.group_sizes), "useful_flops": int(best.useful_flops),
+                     "reference_min_bytes": int(best.reference_min_bytes),
+                     "ideal_memory_speedup": float(best.ideal_memory_speedup)})
+    cfg = json.loads((src / "config.json").read_text())
+    env = json.loads((src / "environment.json").read_text()) if (src / "environment.json").exists() else {}
+    L4_TABLE.write_text(json.dumps({"source": "Krushna-B/pallas-moe-kernel results/structured_float32",
+                                    "hardware": (env.get("devices") or [{}])[0].get("device_kind", "NVIDIA L4"),
+                                    "warmup": cfg.get("warmup"), "iterations": cfg.get("iterations"),
+                                    "shapes": rows}, indent=1, default=str))
+    return len(rows)
+
+
 def main():
+    REF = _reference_dir()
     bench = _load_functions(REF / "src/benchmark.py", {"make_group_sizes"})
     exp = _load_functions(REF / "src/ragged_moe_speedup_experiment.py", {"routing_weights", "make_group_sizes"})
 
@@ -73,7 +116,7 @@ def main():
         "experiment_make_group_sizes": cases_exp,
         "results_csv_recorded": recorded_list,
     }, indent=0))
-    print(len(cases_bench), len(cases_exp), len(recorded_list))
+    print(len(cases_bench), len(cases_exp), len(recorded_list), write_l4_table(REF))
 
 
 if __name__ == "__main__":

@@ -9,7 +9,9 @@ import torch
 from oracle import moe_oracle as orc
 from src import _lib
 from src.kernel import fused_ragged_mlp
-from src.routing import CONFIGS, config_group_sizes, make_inputs_numpy, zipf_group_sizes
+from src.routing import CONFIGS, config_group_sizes, make_inputs_numpy, with_shape, zipf_group_sizes
+
+import parity_checks
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-2
@@ -74,33 +76,34 @@ def test_large_d_zipf_many_experts():
     assert m["l2_relative_error"] <= TOL, m
 
 
-def test_c4_mixtral_shape_sampled_rows():
-    """Full C4 shape (D=4096, F=14336, E=8, top-2 of 16384 tokens -> M=32768),
-    inputs generated on the device; the oracle checks 24 sampled rows per
-    expert (a row depends only on its own X row and its expert's weights)."""
-    cfg = CONFIGS["c4"]
-    gs = config_group_sizes(cfg, seed=0)
-    assert gs.sum() == cfg.M
+def _mixtral_inputs(cfg, seed):
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev)
-    g.manual_seed(0)
+    g.manual_seed(seed)
     x = torch.randn((cfg.M, cfg.D), generator=g, device=dev).to(torch.bfloat16)
     wu = (torch.randn((cfg.E, cfg.D, cfg.F), generator=g, device=dev) / cfg.D ** 0.5).to(torch.bfloat16)
     wd = (torch.randn((cfg.E, cfg.F, cfg.D), generator=g, device=dev) / cfg.F ** 0.5).to(torch.bfloat16)
-    y = fused_ragged_mlp(x, wu, wd, torch.from_numpy(gs).to(dev))
+    return x, wu, wd
+
+
+@pytest.mark.parametrize("tokens", [16384, 32768])
+def test_mixtral_shape_every_expert_every_block(tokens):
+    """The C4 shape (D=4096, F=14336, E=8, top-2 router) at 16384 tokens
+    (M = 32768, the benchmarked configuration) and 32768 tokens (M = 65536,
+    the bf16 target point of at least 64K routed rows).  Inputs are generated
+    on the device.  The float64 oracle checks, per row, every expert's first
+    and last row and one row in each of its 128-row blocks; an fp32 torch
+    recomputation screens every row, per 128-row block."""
+    cfg = with_shape(CONFIGS["c4"], M=2 * tokens, tokens=tokens)
+    gs = config_group_sizes(cfg, seed=0)
+    assert gs.sum() == cfg.M
+    x, wu, wd = _mixtral_inputs(cfg, seed=tokens)
+    dev = x.device
+    out = torch.full((cfg.M, cfg.D), float("nan"), device=dev)
+    y = fused_ragged_mlp(x, wu, wd, torch.from_numpy(gs).to(dev), out=out)
     torch.cuda.synchronize()
-    offs = orc.group_sizes_to_offsets(gs)
-    rng = np.random.default_rng(1)
-    refs, gots = [], []
-    for e in range(cfg.E):
-        a, b = int(offs[e]), int(offs[e + 1])
-        if b <= a:
-            continue
-        rows = np.unique(np.concatenate([rng.integers(a, b, 22), [a, b - 1]]))
-        xe = x[rows].float().cpu().numpy()
-        wue = wu[e].float().cpu().numpy()
-        wde = wd[e].float().cpu().numpy()
-        refs.append(orc.ref_ragged_mlp(xe, wue[None], wde[None], [len(rows)]))
-        gots.append(y[rows].cpu().numpy())
-    m = orc.correctness_metrics(np.concatenate(refs), np.concatenate(gots))
-    assert m["fused_is_finite"] and m["l2_relative_error"] <= TOL, m
+    o = parity_checks.oracle_rows_check(x, lambda e: wu[e], lambda e: wd[e], gs, y, TOL, seed=tokens)
+    assert o["experts"] == int(np.count_nonzero(gs))
+    assert o["rows"] >= cfg.M // 128
+    s = parity_checks.torch_screen(x, lambda e: wu[e], lambda e: wd[e], gs, y, TOL)
+    assert s["blocks"] >= cfg.M // 128

@@ -1,6 +1,6 @@
 """The structured sweep's case grid and traffic model against the
-reference's own recorded sweep (the per-shape fixture its
-``make_l4_table.py`` extracts from the reference's results.csv)."""
+reference's own recorded sweep (the per-shape fixture that
+``tests/golden/make_golden.py`` extracts from the reference's results.csv)."""
 
 import json
 from pathlib import Path

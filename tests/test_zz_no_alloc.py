@@ -89,3 +89,24 @@ def test_noalloc_refuses_problems_above_its_static_scratch():
     assert b"static buffer" in L.moe_last_error()
     torch.cuda.synchronize()
     assert torch.isnan(y).all()               # output untouched
+
+
+def test_noalloc_warm_calls_leave_device_memory_unchanged():
+    """After a first call (module load, scratch address look-up), further
+    calls take no device memory: the free bytes the driver reports stay the
+    same.  Inputs and outputs are created before the measurement."""
+    L = _lib_bound()
+    M, D, F, E = 2048, 128, 512, 8
+    x, wu, wd, gs = _inputs(M, D, F, E, 3)
+    y = torch.empty((M, D), device=x.device)
+    args = (vp(x.data_ptr()), vp(wu.data_ptr()), vp(wd.data_ptr()), vp(gs.data_ptr()), vp(y.data_ptr()),
+            M, D, F, E, _stream())
+    assert L.moe_fused_mlp_noalloc(*args) == 0, L.moe_last_error().decode()
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        assert L.moe_fused_mlp_noalloc(*args) == 0, L.moe_last_error().decode()
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, (free0, free1)
+    assert _lib.device_status(reset=True) == 0
