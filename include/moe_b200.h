@@ -366,7 +366,10 @@ int moe_sm_clock_sample(uint64_t* out, int32_t blocks, void* stream);
  * choice).  Keys: 1 = F-splits per 128-row block (power of two),
  * 2 = persistent CTAs per launch, 3 = device address of an event-trace
  * buffer (read only by builds compiled with -DMOE_TRACE), 4 = kernel family
- * (0 automatic, 1 one CTA per 128-row block, 2 CTA pairs per 256 rows).
+ * (0 automatic, 1 one CTA per 128-row block, 2 CTA pairs per 256 rows),
+ * 5 = grouped GEMMs' tile rasterisation group in 256-row blocks (1 .. 64;
+ * 0 = 8), 6 = grouped GEMMs' L2 hints for the A / B tile loads (0 evict_last
+ * for both, 1 evict_normal for both, 2 A evict_first, 3 B evict_first).
  * Returns 0 or MOE_ERR_INVALID_ARG.
  */
 int moe_set_tuning(int32_t key, int64_t value);

@@ -167,8 +167,9 @@ using BlockCursor = BlockCursorT<7>;
 // both the writes and the reads are bank-conflict free) and leaves as
 // row-contiguous 128-byte stores, masked per row at the expert's end.
 template <int D>
+// Columns at or past `col_end` (relative to `y`, like c0) are not stored.
 __device__ __forceinline__ void store_y_block(uint32_t taddr, float4* stage, float* y, int row_base, int row_end,
-                                              int c0, uint32_t lane, bool atomic, int ld = D) {
+                                              int c0, uint32_t lane, bool atomic, int ld = D, int col_end = 1 << 30) {
   uint32_t v[32];
   tmem_ld32(taddr, v);
   tmem_ld_wait();
@@ -183,7 +184,7 @@ __device__ __forceinline__ void store_y_block(uint32_t taddr, float4* stage, flo
     const int k = (int)(lane & 7);
     const float4 val = stage[r * 8 + (k ^ (r & 7))];
     const int row = row_base + r;
-    if (row < row_end) {
+    if (row < row_end && c0 + 4 * k < col_end) {
       float* dst = y + (size_t)row * ld + c0 + 4 * k;
       if (atomic)
         red_add_v4(dst, val.x, val.y, val.z, val.w);

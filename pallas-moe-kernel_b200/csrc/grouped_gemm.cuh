@@ -11,6 +11,18 @@
 // M = 256, N = 256, K = 16 into TMEM; accumulators are double-buffered (2 x
 // 256 columns) so the epilogue of one tile overlaps the MMAs of the next.
 //
+// f32 inputs (TF32 = true) run as 3xTF32 on kind::tf32: A and B come as tf32
+// hi/lo planes (value = hi + lo, hi = the value with its low 13 mantissa bits
+// cleared), B transposed to K-major (W^T (N, K) per expert), and every K step
+// issues hi*hi + hi*lo + lo*hi.  The up GEMM's epilogue writes H as hi/lo f32
+// planes for the down GEMM.
+//
+// Weights are read through 3-D tensor maps [E][K][N] (K-major planes:
+// [E][N][K]), so a box never reaches into the next expert: columns past N
+// and rows past K read as zero, and N and K need not be multiples of the
+// tile (N, K multiples of 8 for 16-bit data, 4 for f32, 16 for e4m3, so that
+// rows start on 16-byte boundaries); stores mask the columns past N.
+//
 // Tiles are (expert, 256-row block, 256-column block), enumerated on the
 // device from the group sizes (no padded grid; the last row block of an
 // expert is row-masked at the store), walked by every pair with a static
@@ -49,20 +61,32 @@ struct GemmParams {
   int E;
   int N;              // output columns (F for up, D for down)
   int K;              // reduction (D for up, F for down)
-  int k_rows_per_e;   // rows of the 2-D B tensor map per expert (= K)
   int group_m;        // tile rasterisation group (row blocks)
   int* status;
-  const float* b_scale;  // FP8 weights: (E, K/128, N/128) f32 block scales, else null
+  const float* b_scale;  // FP8 weights: (E, ceil(K/128), ceil(N/128)) f32 block scales, else null
   int skip_tail;         // 1: leave rows at or past sum(group_sizes) unwritten (Y only)
   EpScatter scatter;     // Y only: rows go to their source ranks (expert parallelism)
-  void* out2;            // EPI 3: the pre-activation X W_up (bf16, [M, N]) saved for the backward
+  void* out2;            // EPI 3: the pre-activation X W_up (bf16, [M, N]) saved for the backward;
+                         // TF32 EPI 0: the lo plane of H (f32, [M, N]; `out` holds the hi plane)
   EpDispatch dispatch;   // EPI 0, bf16: expert-parallel dispatch fused into the up GEMM
+  int l2_mode;           // L2 hints of the A / B loads: 0 evict_last / evict_last, 1 evict_normal / evict_normal,
+                         // 2 evict_first / evict_last, 3 evict_last / evict_first
 };
 
+__device__ __forceinline__ uint64_t gemm_l2_policy(int mode, bool b_operand) {
+  switch (mode) {
+    case 1: return l2_policy_evict_normal();
+    case 2: return b_operand ? l2_policy_evict_last() : l2_policy_evict_first();
+    case 3: return b_operand ? l2_policy_evict_first() : l2_policy_evict_last();
+    default: return l2_policy_evict_last();
+  }
+}
+
 // store_y_block with one destination row pointer per row: lane l of the warp
-// holds the pointer of row l of the 32-row block (null = not stored).
+// holds the pointer of row l of the 32-row block (null = not stored); columns
+// at or past `col_end` are not stored.
 __device__ __forceinline__ void store_y_rows(uint32_t taddr, float4* stage, uint8_t* row_ptr, int col0,
-                                             uint32_t lane, float mul) {
+                                             uint32_t lane, float mul, int col_end) {
   uint32_t v[32];
   tmem_ld32(taddr, v);
   tmem_ld_wait();
@@ -80,7 +104,7 @@ __device__ __forceinline__ void store_y_rows(uint32_t taddr, float4* stage, uint
     const float4 val = stage[r * 8 + (k ^ (r & 7))];
     uint8_t* dst = reinterpret_cast<uint8_t*>(
         __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(row_ptr), r));
-    if (dst) *reinterpret_cast<float4*>(dst + (size_t)(col0 + 4 * k) * 4) = val;
+    if (dst && col0 + 4 * k < col_end) *reinterpret_cast<float4*>(dst + (size_t)(col0 + 4 * k) * 4) = val;
   }
   __syncwarp();
 }
@@ -89,17 +113,20 @@ __device__ __forceinline__ void store_y_rows(uint32_t taddr, float4* stage, uint
 // interleaved every 128 columns, and for e4m3 their block scales one
 // block per period; H has half the columns), 3: GELU -> H plus
 // the pre-activation (bf16) to out2, 4: SwiGLU plus the raw gate/up columns
-// (bf16) to out2; BFP8: e4m3 B dequantised in smem, f16 operands.
-template <int EPI, bool BFP8>
+// (bf16) to out2; BFP8: e4m3 B dequantised in smem, f16 operands; TF32: f32
+// operands as tf32 hi/lo planes (3xTF32), EPI 0 or 1 only.
+template <int EPI, bool BFP8, bool TF32 = false>
 struct GemmCfg {
+  static_assert(!(TF32 && (BFP8 || EPI > 1)), "3xTF32 runs the GELU and Y epilogues on f32 planes");
   static constexpr int BM = 128;   // rows per CTA (256 per pair)
   static constexpr int BN = 256;   // output columns per tile (128 per CTA of B)
-  static constexpr int BK = 64;    // 16-bit elements = one 128-byte swizzle row
-  static constexpr int A_BYTES = BM * BK * 2;          // 16 KB
-  static constexpr int B_BYTES = (BN / 2) * BK * 2;    // 16 KB (two 64-column atoms, 16-bit)
+  static constexpr int BK = TF32 ? 32 : 64;  // elements of one 128-byte swizzle row
+  static constexpr int A_BYTES = BM * 128;             // 16 KB (one plane)
+  static constexpr int B_BYTES = (BN / 2) * 128;       // 16 KB (one plane of this CTA's B half)
   static constexpr int B8_BYTES = BFP8 ? (BN / 2) * BK : 0;  // 8 KB raw e4m3 tile
-  static constexpr int STAGE = A_BYTES + B_BYTES;      // operand stage (A + 16-bit B)
-  static constexpr int NS = BFP8 ? 4 : 6;              // operand stages
+  static constexpr int PLANES = TF32 ? 2 : 1;          // hi and lo planes of A and of B
+  static constexpr int STAGE = PLANES * (A_BYTES + B_BYTES);  // operand stage
+  static constexpr int NS = TF32 ? 3 : (BFP8 ? 4 : 6); // operand stages
   static constexpr int NR = BFP8 ? 10 : 0;             // raw e4m3 stages (HBM stream runs ahead)
   static constexpr int EPI_WARPS = 4;
   static constexpr int CVT_WARPS = BFP8 ? 8 : 0;  // two per SM sub-partition
@@ -107,13 +134,15 @@ struct GemmCfg {
   static constexpr int BAR_BYTES = BFP8 ? 512 : 256;
   // bf16 up GEMM: four warps that run the expert-parallel dispatch (idle
   // otherwise), with the slice row prefix in shared memory.
-  static constexpr int PUSH_WARPS = (EPI == 0 && !BFP8) ? 4 : 0;
+  static constexpr int PUSH_WARPS = (EPI == 0 && !BFP8 && !TF32) ? 4 : 0;
   static constexpr int PUSH_SMEM = PUSH_WARPS ? (kEpMaxExperts + 1) * 4 : 0;
   static constexpr int SMEM = 1024 + NS * STAGE + NR * B8_BYTES + OUT_STAGE + BAR_BYTES + PUSH_SMEM;
   static constexpr int TMEM_COLS = 512;                 // 2 accumulators x 256 columns
   // e4m3 weights run as f16 operands (f16 X, f16 H, f16 dequantised B).
-  static constexpr uint32_t IDESC = make_idesc(BFP8 ? kFmtF16 : kFmtBF16, 256, BN, 0, 1);
-  static constexpr uint32_t TX = 2 * (A_BYTES + B_BYTES);  // both CTAs (bf16 B)
+  // 16-bit B is read MN-major (the weights' own layout); tf32 B is K-major.
+  static constexpr uint32_t IDESC = TF32 ? make_idesc(kFmtTF32, 256, BN, 0, 0)
+                                         : make_idesc(BFP8 ? kFmtF16 : kFmtBF16, 256, BN, 0, 1);
+  static constexpr uint32_t TX = 2 * STAGE;                // both CTAs (bf16 or tf32 B)
   static constexpr uint32_t TX_A = 2 * A_BYTES;            // both CTAs' A (FP8 B arrives converted)
   static constexpr int RAW_WARP = 2 + EPI_WARPS + CVT_WARPS;  // FP8: producer of the raw ring
   static constexpr int THREADS = 64 + (EPI_WARPS + CVT_WARPS + PUSH_WARPS) * 32 + (BFP8 ? 32 : 0);
@@ -121,12 +150,15 @@ struct GemmCfg {
   // was scheduled under it), or of the FP8 block with its extra warps.
   static constexpr int LAUNCH_BOUND = THREADS > 320 ? THREADS : 320;
   static_assert(SMEM <= kMaxSmemPerBlock, "shared memory budget");
-  static_assert(NS % 2 == 0 && NR % 2 == 0, "alternating converter groups keep fixed stage parities");
+  static_assert(!BFP8 || (NS % 2 == 0 && NR % 2 == 0), "alternating converter groups keep fixed stage parities");
 };
 
 struct GemmMaps {
-  CUtensorMap a;  // X or H: [M, K] bf16 (f16 with e4m3 weights), box {64, 128}
-  CUtensorMap b;  // W_up / W_down as [E*K, N]: bf16 box {64, 64}, or e4m3 bytes box {128, 64}
+  CUtensorMap a;     // X or H: [M, K] bf16 (f16 with e4m3 weights), box {64, 128}; TF32: hi plane, box {32, 128}
+  CUtensorMap b;     // W_up / W_down as [E][K][N]: bf16 box {64, 64, 1}, or e4m3 bytes box {128, 64, 1};
+                     // TF32: hi plane of W^T as [E][N][K], box {32, 128, 1}
+  CUtensorMap a_lo;  // TF32 only: lo planes
+  CUtensorMap b_lo;
 };
 
 // Four e4m3 values (one 32-bit word, lowest byte first) -> four f16 (two
@@ -150,10 +182,12 @@ __device__ __forceinline__ uint2 e4m3x4_to_f16x4(uint32_t v, uint32_t s2) {
 // weights by scale * 2^k; the epilogue multiplies the accumulator by 2^-k
 // (exact).  Every lane of the calling warp returns the same k, in [-100, 100].
 __device__ __forceinline__ int fp8_tile_shift(const float* b_scale, int K, int N, int e, int nb, uint32_t lane) {
-  const int nkb = K / 128, nnb = N / 128;
+  const int nkb = (K + 127) / 128, nnb = (N + 127) / 128;
   const float* sc = b_scale + (size_t)e * nkb * nnb + (size_t)nb * 2;
+  const int ncb = nnb - 2 * nb < 2 ? nnb - 2 * nb : 2;  // scale blocks of this tile inside N (1 or 2)
   float m = 0.f;
-  for (int i = (int)lane; i < 2 * nkb; i += 32) m = fmaxf(m, __ldg(sc + (size_t)(i >> 1) * nnb + (i & 1)));
+  for (int i = (int)lane; i < 2 * nkb; i += 32)
+    if ((i & 1) < ncb) m = fmaxf(m, __ldg(sc + (size_t)(i >> 1) * nnb + (i & 1)));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   const int ex = (int)((__float_as_uint(m) >> 23) & 0xFFu);
@@ -200,10 +234,10 @@ struct TileCursor {
   }
 };
 
-template <int EPI, bool BFP8>
-__global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
+template <int EPI, bool BFP8, bool TF32 = false>
+__global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32>::LAUNCH_BOUND, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
-  using C = GemmCfg<EPI, BFP8>;
+  using C = GemmCfg<EPI, BFP8, TF32>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -227,8 +261,8 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
   const int pair = (int)(blockIdx.x >> 1);
   const int npairs = (int)(gridDim.x >> 1);
   constexpr uint16_t kBoth = 0x3;
-  const int nt = p.N / C::BN;
-  const int nk = p.K / C::BK;
+  const int nt = (p.N + C::BN - 1) / C::BN;
+  const int nk = (p.K + C::BK - 1) / C::BK;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::NS; ++i) {
@@ -255,6 +289,10 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&maps.a);
     tma_prefetch_desc(&maps.b);
+    if constexpr (TF32) {
+      tma_prefetch_desc(&maps.a_lo);
+      tma_prefetch_desc(&maps.b_lo);
+    }
   }
   tc_fence_before();
   cluster_sync();
@@ -269,8 +307,8 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
       TileCursor cur;
       int stage = 0;
       uint32_t phase = 0;
-      const uint64_t pol_a = l2_policy_evict_last();
-      const uint64_t pol_b = l2_policy_evict_last();
+      const uint64_t pol_a = gemm_l2_policy(p.l2_mode, false);
+      const uint64_t pol_b = gemm_l2_policy(p.l2_mode, true);
       uint32_t arrived = 0;  // dispatch: sources whose rows have landed here
       for (int t = pair;; t += npairs) {
         if (!cur.seek(t, p.group_sizes, p.E, p.M, nt)) break;
@@ -278,7 +316,6 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
         cur.coords(t, nt, p.group_m, mb, nb);
         const int row0 = cur.row_begin + mb * 256 + (int)rank * C::BM;
         const int n0 = nb * C::BN + (int)rank * (C::BN / 2);
-        const int brow0 = cur.e * p.k_rows_per_e;
         bool ok = true;
         if (C::PUSH_WARPS > 0 && p.dispatch.on) {
           // Wait for every peer whose rows of this expert meet this CTA's 128
@@ -327,12 +364,20 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
             const uint32_t bar = full_l0 + stage * 8;
             if (rank == 0) mbar_arrive_expect_tx(full + stage, C::TX_A);
             tma_load_2d_pair(st, &maps.a, bar, kb * C::BK, row0, pol_a);
+          } else if constexpr (TF32) {
+            // Stage layout: A hi | A lo | B hi | B lo (K-major, 128 rows x 128 B each).
+            const uint32_t bar = full_l0 + stage * 8;
+            if (rank == 0) mbar_arrive_expect_tx(full + stage, C::TX);
+            tma_load_2d_pair(st, &maps.a, bar, kb * C::BK, row0, pol_a);
+            tma_load_2d_pair(st + C::A_BYTES, &maps.a_lo, bar, kb * C::BK, row0, pol_a);
+            tma_load_3d_pair(st + 2 * C::A_BYTES, &maps.b, bar, kb * C::BK, n0, cur.e, pol_b);
+            tma_load_3d_pair(st + 2 * C::A_BYTES + C::B_BYTES, &maps.b_lo, bar, kb * C::BK, n0, cur.e, pol_b);
           } else {
             const uint32_t bar = full_l0 + stage * 8;
             if (rank == 0) mbar_arrive_expect_tx(full + stage, C::TX);
             tma_load_2d_pair(st, &maps.a, bar, kb * C::BK, row0, pol_a);
-            tma_load_2d_pair(st + C::A_BYTES, &maps.b, bar, n0, brow0 + kb * C::BK, pol_b);
-            tma_load_2d_pair(st + C::A_BYTES + 64 * 128, &maps.b, bar, n0 + 64, brow0 + kb * C::BK, pol_b);
+            tma_load_3d_pair(st + C::A_BYTES, &maps.b, bar, n0, kb * C::BK, cur.e, pol_b);
+            tma_load_3d_pair(st + C::A_BYTES + 64 * 128, &maps.b, bar, n0 + 64, kb * C::BK, cur.e, pol_b);
           }
           if (++stage == C::NS) {
             stage = 0;
@@ -364,13 +409,28 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
           }
           tc_fence_after();
           const uint32_t st = smem_u32(ring + stage * C::STAGE);
-          const uint64_t a_desc = make_sdesc(st, 16, 1024);
-          const uint64_t b_desc = make_sdesc(st + C::A_BYTES, 64 * 128, 1024);
+          if constexpr (TF32) {
+            // K = 8 per instruction (32 bytes along the 128-byte row); the
+            // small cross terms first, then hi * hi.
+            const uint64_t ah = make_sdesc(st, 16, 1024), al = make_sdesc(st + C::A_BYTES, 16, 1024);
+            const uint64_t bh = make_sdesc(st + 2 * C::A_BYTES, 16, 1024);
+            const uint64_t bl = make_sdesc(st + 2 * C::A_BYTES + C::B_BYTES, 16, 1024);
 #pragma unroll
-          for (int ki = 0; ki < C::BK / 16; ++ki)
-            umma_ss_pair<Kind::F16>(d_tmem, a_desc + (uint64_t)((ki * 32) >> 4),
-                                    b_desc + (uint64_t)((ki * 16 * 128) >> 4), C::IDESC,
-                                    (kb > 0 || ki > 0) ? 1u : 0u);
+            for (int ki = 0; ki < C::BK / 8; ++ki) {
+              const uint64_t o = (uint64_t)((ki * 32) >> 4);
+              umma_ss_pair<Kind::TF32>(d_tmem, ah + o, bl + o, C::IDESC, (kb > 0 || ki > 0) ? 1u : 0u);
+              umma_ss_pair<Kind::TF32>(d_tmem, al + o, bh + o, C::IDESC, 1u);
+              umma_ss_pair<Kind::TF32>(d_tmem, ah + o, bh + o, C::IDESC, 1u);
+            }
+          } else {
+            const uint64_t a_desc = make_sdesc(st, 16, 1024);
+            const uint64_t b_desc = make_sdesc(st + C::A_BYTES, 64 * 128, 1024);
+#pragma unroll
+            for (int ki = 0; ki < C::BK / 16; ++ki)
+              umma_ss_pair<Kind::F16>(d_tmem, a_desc + (uint64_t)((ki * 32) >> 4),
+                                      b_desc + (uint64_t)((ki * 16 * 128) >> 4), C::IDESC,
+                                      (kb > 0 || ki > 0) ? 1u : 0u);
+          }
           umma_commit_pair(empty + stage, kBoth);
           if (++stage == C::NS) {
             stage = 0;
@@ -389,21 +449,20 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
       TileCursor cur;
       int rs = 0;
       uint32_t rph = 0;
-      const uint64_t pol_b = l2_policy_evict_last();
+      const uint64_t pol_b = gemm_l2_policy(p.l2_mode, true);
       bool ok = true;
       for (int t = pair; ok; t += npairs) {
         if (!cur.seek(t, p.group_sizes, p.E, p.M, nt)) break;
         int mb, nb;
         cur.coords(t, nt, p.group_m, mb, nb);
         const int n0 = nb * C::BN + (int)rank * (C::BN / 2);
-        const int brow0 = cur.e * p.k_rows_per_e;
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(raw_empty + rs, rph ^ 1u, abort_flag, p.status)) {
             ok = false;
             break;
           }
           mbar_arrive_expect_tx(raw_full + rs, C::B8_BYTES);
-          tma_load_2d_hint(rawring + rs * C::B8_BYTES, &maps.b, raw_full + rs, n0, brow0 + kb * C::BK, pol_b);
+          tma_load_3d_hint(rawring + rs * C::B8_BYTES, &maps.b, raw_full + rs, n0, kb * C::BK, cur.e, pol_b);
           if (++rs == C::NR) {
             rs = 0;
             rph ^= 1u;
@@ -413,10 +472,12 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
     }
   } else if (BFP8 && warp >= 2u + C::EPI_WARPS) {
     // ------------------------------------------------------------ e4m3 -> f16 B converters (both CTAs)
-    // Two groups of four warps take alternate K steps (K / 64 is even, so a
-    // group keeps its parity across tiles): each group has two stage times
-    // for its stage, and the fixed costs of a stage (barrier checks, fence,
-    // hand-off) of the two groups overlap.  In a group, thread t handles
+    // Two groups of four warps take alternate K steps of each tile: each
+    // group has two stage times for its stage, and the fixed costs of a stage
+    // (barrier checks, fence, hand-off) of the two groups overlap.  Every K
+    // step goes to exactly one group and every barrier counts the arrivals of
+    // one group, so an odd number of K steps per tile (K % 128 != 0) only
+    // gives one group two steps in a row at the tile boundary.  In a group, thread t handles
     // k-row r = t % 64 of the 64 x 128 raw tile and half h = t / 64 of its
     // 128 columns (= one 64-column f16 atom row, 128 bytes): the 8 threads of
     // a quarter-warp own 8 consecutive rows, so their swizzled 16-byte
@@ -425,7 +486,7 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
     const int ct = (int)threadIdx.x - 64 - C::EPI_WARPS * 32;  // 0..255
     const int grp = ct >> 7;
     const int r = ct & 63, h = (ct >> 6) & 1;
-    const int nkb_scale = p.K / 128, nnb_scale = p.N / 128;
+    const int nkb_scale = (p.K + 127) / 128, nnb_scale = (p.N + 127) / 128;
     TileCursor cur;
     uint32_t gk = 0;  // K steps of this CTA's earlier tiles
     bool ok = true;
@@ -434,12 +495,15 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
       int mb, nb;
       cur.coords(t, nt, p.group_m, mb, nb);
       const int n0 = nb * C::BN + (int)rank * (C::BN / 2);
-      const float* srow = p.b_scale + ((size_t)cur.e * nkb_scale) * nnb_scale + n0 / 128;
+      // A half that starts at or past N holds only zero-filled columns: its
+      // scales are never read (0 is used).
+      const bool col_in = n0 / 128 < nnb_scale;
+      const float* srow = p.b_scale + ((size_t)cur.e * nkb_scale) * nnb_scale + (col_in ? n0 / 128 : 0);
       // The tile's block scales along K (one per 128 rows of B), fetched once
       // per tile -- lane l holds k-blocks l and l + 32 -- and broadcast per
       // stage, so no stage waits on a global load.
-      const float s_lo = (int)lane < nkb_scale ? __ldg(srow + (size_t)lane * nnb_scale) : 0.f;
-      const float s_hi = (int)lane + 32 < nkb_scale ? __ldg(srow + (size_t)(lane + 32) * nnb_scale) : 0.f;
+      const float s_lo = col_in && (int)lane < nkb_scale ? __ldg(srow + (size_t)lane * nnb_scale) : 0.f;
+      const float s_hi = col_in && (int)lane + 32 < nkb_scale ? __ldg(srow + (size_t)(lane + 32) * nnb_scale) : 0.f;
       const float up = exp2i(fp8_tile_shift(p.b_scale, p.K, p.N, cur.e, nb, lane));
       for (int kb = grp; kb < nk; kb += 2) {
         const uint32_t g = gk + (uint32_t)kb;
@@ -453,7 +517,7 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
         }
         const int kblk = (kb * C::BK) / 128;
         const float s_reg = __shfl_sync(0xffffffffu, kblk < 32 ? s_lo : s_hi, kblk & 31);
-        const float sc = kblk < 64 ? s_reg : __ldg(srow + (size_t)kblk * nnb_scale);
+        const float sc = kblk < 64 ? s_reg : (col_in ? __ldg(srow + (size_t)kblk * nnb_scale) : 0.f);
         const uint32_t s2 = pack_f16x2_sat(sc * up, sc * up);
         const uint8_t* src = rawring + rs * C::B8_BYTES + r * 128;             // 128-byte swizzled raw row
         uint8_t* dst = ring + stage * C::STAGE + C::A_BYTES + h * (64 * 128) + r * 128;  // atom h, row r
@@ -557,12 +621,55 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
       const uint32_t acc = lane_base + ab * C::BN;
       // FP8 tiles were accumulated with weights scaled by 2^k.
       const float mul = BFP8 ? exp2i(-fp8_tile_shift(p.b_scale, p.K, p.N, cur.e, nb, lane)) : 1.f;
-      if constexpr (EPI == 0 || EPI == 3) {
+      // Columns of this tile inside N (the last column tile may be partial).
+      const int ncol = p.N - nb * C::BN < C::BN ? p.N - nb * C::BN : C::BN;
+      if constexpr (TF32 && EPI == 0) {
+        // 32 columns per step: GELU (f32 accuracy), then the tf32 split
+        // g = hi + lo (hi = g with its low 13 mantissa bits cleared); each
+        // plane goes out through the 32-row x 128-byte staging as full-line
+        // row stores.
+        float4* wst4 = reinterpret_cast<float4*>(wst);
+#pragma unroll 1
+        for (int c0 = 0; c0 < ncol; c0 += 32) {
+          uint32_t v[32];
+          tmem_ld32(acc + c0, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(gelu_tanh_exp(__uint_as_float(v[i])));
+          const int gcol = nb * C::BN + c0;
+#pragma unroll 1
+          for (int pl = 0; pl < 2; ++pl) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              float q[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float g = __uint_as_float(v[4 * k + j]);
+                const float h = __uint_as_float(v[4 * k + j] & 0xFFFFE000u);
+                q[j] = pl == 0 ? h : g - h;
+              }
+              wst4[lane * 8 + (k ^ (lane & 7))] = make_float4(q[0], q[1], q[2], q[3]);
+            }
+            __syncwarp();
+            float* P = reinterpret_cast<float*>(pl == 0 ? p.out : p.out2);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int r = 4 * i + (int)(lane >> 3);
+              const int k = (int)(lane & 7);
+              const float4 val = wst4[r * 8 + (k ^ (r & 7))];
+              const int row = wrow0 + r;
+              if (row < row_end && c0 + 4 * k < ncol)
+                *reinterpret_cast<float4*>(P + (size_t)row * p.N + gcol + 4 * k) = val;
+            }
+            __syncwarp();
+          }
+        }
+      } else if constexpr (EPI == 0 || EPI == 3) {
         // 64 columns per step: GELU, pack to bf16 (f16 for FP8 weights),
         // stage 32 rows x 128 B, store rows as full 128-byte lines.
         uint16_t* H = reinterpret_cast<uint16_t*>(p.out);  // bf16 / f16 bits
 #pragma unroll 1
-        for (int c0 = 0; c0 < C::BN; c0 += 64) {
+        for (int c0 = 0; c0 < ncol; c0 += 64) {
           uint32_t v[64];
           uint4* srow = reinterpret_cast<uint4*>(wst) + lane * 8;
           if constexpr (BFP8) {
@@ -605,7 +712,7 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
             const int k = (int)(lane & 7);
             const uint4 val = reinterpret_cast<const uint4*>(wst)[r * 8 + (k ^ (r & 7))];
             const int row = wrow0 + r;
-            if (row < row_end)
+            if (row < row_end && c0 + 8 * k < ncol)
               *reinterpret_cast<uint4*>(H + (size_t)row * p.N + gcol + 8 * k) = val;
           }
           __syncwarp();
@@ -628,7 +735,7 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
               const int k = (int)(lane & 7);
               const uint4 val = reinterpret_cast<const uint4*>(wst)[r * 8 + (k ^ (r & 7))];
               const int row = wrow0 + r;
-              if (row < row_end)
+              if (row < row_end && c0 + 8 * k < ncol)
                 *reinterpret_cast<uint4*>(A + (size_t)row * p.N + gcol + 8 * k) = val;
             }
             __syncwarp();
@@ -731,7 +838,8 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
         }
         float4* wst4 = reinterpret_cast<float4*>(wst);
 #pragma unroll 1
-        for (int c0 = 0; c0 < C::BN; c0 += 32) store_y_rows(acc + c0, wst4, row_ptr, nb * C::BN + c0, lane, mul);
+        for (int c0 = 0; c0 < ncol; c0 += 32)
+          store_y_rows(acc + c0, wst4, row_ptr, nb * C::BN + c0, lane, mul, p.N);
       } else if (BFP8) {
         // f32 Y rows scaled back by 2^-k, through the same staging as below.
         float* Y = reinterpret_cast<float*>(p.out);
@@ -739,13 +847,14 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8>::LAUNCH_BOUND, 1)
         const int R = wrow0 + (int)lane;
         uint8_t* row_ptr = R < row_end ? reinterpret_cast<uint8_t*>(Y + (size_t)R * p.N) : nullptr;
 #pragma unroll 1
-        for (int c0 = 0; c0 < C::BN; c0 += 32) store_y_rows(acc + c0, wst4, row_ptr, nb * C::BN + c0, lane, mul);
+        for (int c0 = 0; c0 < ncol; c0 += 32)
+          store_y_rows(acc + c0, wst4, row_ptr, nb * C::BN + c0, lane, mul, p.N);
       } else {
         float* Y = reinterpret_cast<float*>(p.out);
         float4* wst4 = reinterpret_cast<float4*>(wst);
 #pragma unroll 1
-        for (int c0 = 0; c0 < C::BN; c0 += 32)
-          store_y_block<0>(acc + c0, wst4, Y + (size_t)nb * C::BN, wrow0, row_end, c0, lane, false, p.N);
+        for (int c0 = 0; c0 < ncol; c0 += 32)
+          store_y_block<0>(acc + c0, wst4, Y + (size_t)nb * C::BN, wrow0, row_end, c0, lane, false, p.N, ncol);
       }
       tc_fence_before();
       __syncwarp();

@@ -41,6 +41,8 @@ static int64_t g_tune_splits = 0;
 static int64_t g_tune_ctas = 0;
 static int64_t g_tune_trace = 0;  // device address of a trace buffer (MOE_TRACE builds)
 static int64_t g_tune_pair = 0;   // 0 auto, 1 single-CTA kernel, 2 CTA-pair kernel
+static int64_t g_tune_group_m = 0;  // grouped GEMMs: rasterisation group in 256-row blocks (0 = 8)
+static int64_t g_tune_l2 = 0;       // grouped GEMMs: L2 hint mode of the A / B loads (GemmParams::l2_mode)
 
 // ------------------------------------------------------------------ driver entry point
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -89,9 +91,10 @@ struct MapKey {
   uint64_t rows, cols;
   uint32_t box_cols, box_rows;
   int dt;
+  uint64_t depth;  // 3-D maps: the outer extent (experts); 0 for 2-D maps
   bool operator==(const MapKey& o) const {
     return base == o.base && rows == o.rows && cols == o.cols && box_cols == o.box_cols &&
-           box_rows == o.box_rows && dt == o.dt;
+           box_rows == o.box_rows && dt == o.dt && depth == o.depth;
   }
 };
 struct MapCacheEntry {
@@ -108,7 +111,7 @@ static int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType d
                        uint64_t cols, uint32_t box_cols, uint32_t box_rows) {
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
     return fail(MOE_ERR_MISALIGNED, "operand base %p is not 16-byte aligned", base);
-  const MapKey key{base, rows, cols, box_cols, box_rows, (int)dt};
+  const MapKey key{base, rows, cols, box_cols, box_rows, (int)dt, 0};
   const uint64_t h = (reinterpret_cast<uintptr_t>(base) >> 8) * 0x9E3779B97F4A7C15ull ^ rows * 0xC2B2AE3D27D4EB4Full ^
                      cols * 0x165667B19E3779F9ull ^ ((uint64_t)box_cols << 20 | (uint64_t)box_rows << 8 | (uint64_t)dt);
   MapCacheEntry& slot = t_maps[(h >> 40) % kMapCacheSlots];
@@ -134,13 +137,51 @@ static int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType d
   return 0;
 }
 
+// 3-D row-major tensor [depth][rows][cols] (per-expert weights) with a
+// {box_cols, box_rows, 1} box and the 128-byte swizzle; a box never crosses
+// from one expert into the next, and out-of-range elements read as zero.
+static int make_map_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int esz, uint64_t depth,
+                       uint64_t rows, uint64_t cols, uint32_t box_cols, uint32_t box_rows) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+    return fail(MOE_ERR_MISALIGNED, "operand base %p is not 16-byte aligned", base);
+  if ((cols * (uint64_t)esz) % 16 != 0)
+    return fail(MOE_ERR_UNSUPPORTED_SHAPE, "row of %llu elements x %d bytes is not a multiple of 16 bytes",
+                (unsigned long long)cols, esz);
+  const MapKey key{base, rows, cols, box_cols, box_rows, (int)dt, depth};
+  const uint64_t h = (reinterpret_cast<uintptr_t>(base) >> 8) * 0x9E3779B97F4A7C15ull ^ rows * 0xC2B2AE3D27D4EB4Full ^
+                     cols * 0x165667B19E3779F9ull ^ depth * 0xD6E8FEB86659FD93ull ^
+                     ((uint64_t)box_cols << 20 | (uint64_t)box_rows << 8 | (uint64_t)dt);
+  MapCacheEntry& slot = t_maps[(h >> 40) % kMapCacheSlots];
+  if (slot.valid && slot.key == key) {
+    *map = slot.map;
+    return 0;
+  }
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t dims[3] = {cols, rows, depth};
+  cuuint64_t strides[2] = {cols * (uint64_t)esz, rows * cols * (uint64_t)esz};
+  cuuint32_t box[3] = {box_cols, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d) depth=%llu rows=%llu cols=%llu box=%ux%u",
+                (int)r, (unsigned long long)depth, (unsigned long long)rows, (unsigned long long)cols, box_cols,
+                box_rows);
+  slot.key = key;
+  slot.map = *map;
+  slot.valid = true;
+  return 0;
+}
+
 // ------------------------------------------------------------------ device info
 struct DevInfo {
   CUcontext ctx = nullptr;  // context the entries below belong to
   int sms = 0;
   int* status = nullptr;  // device address of g_status on this device
-  bool attr_set[40] = {};
-  int pairs[24] = {};  // co-resident CTA pairs per pair-kernel variant (0 = not queried)
+  bool attr_set[44] = {};
+  int pairs[26] = {};  // co-resident CTA pairs per pair-kernel variant (0 = not queried)
 };
 static DevInfo g_dev[64];
 static std::mutex g_dev_mu;
@@ -266,15 +307,42 @@ __global__ void __launch_bounds__(256) small_prep_kernel(const PrepArgs a) {
 }
 
 // ------------------------------------------------------------------ large-D dispatch (two grouped GEMMs)
+// Any D and F whose rows start on 16-byte boundaries in every operand (the
+// TMA rule): the grouped GEMMs mask partial column tiles and read zeros past
+// K.  Shapes the fused small-D kernel covers are routed there first.
 static bool large_supported(int D, int F, int dtype) {
-  if (dtype == MOE_DTYPE_BF16) return D % 256 == 0 && F % 256 == 0 && D > 256;
-  if (dtype == MOE_DTYPE_FP8_E4M3_BLK128) return D % 256 == 0 && F % 256 == 0;
+  if (dtype == MOE_DTYPE_BF16) return D % 8 == 0 && F % 8 == 0;
+  if (dtype == MOE_DTYPE_FP8_E4M3_BLK128) return D % 16 == 0 && F % 16 == 0;
+  if (dtype == MOE_DTYPE_F32) return D % 4 == 0 && F % 4 == 0;
   return false;
 }
 static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-// Large-D workspace: H (M, F) in 16 bits; with e4m3 weights also X in f16.
-static size_t large_ws_bytes(int64_t M, int D, int F, int dtype) {
+// Large-D workspace.  bf16: H (M, F) bf16.  e4m3 weights: H (M, F) f16, then
+// X (M, D) f16.  f32 (3xTF32): the tf32 hi/lo planes of W_up^T (E, F, D) and
+// W_down^T (E, D, F) -- the layout moe_prepare_weights writes -- then X hi/lo
+// (M, D) and H hi/lo (M, F), all f32.
+struct Tf32LargeLayout {
+  size_t wu_hi, wu_lo, wd_hi, wd_lo, x_hi, x_lo, h_hi, h_lo, total;  // byte offsets
+};
+static Tf32LargeLayout tf32_large_layout(int64_t M, int D, int F, int E) {
+  Tf32LargeLayout l{};
+  const size_t w = (size_t)E * D * F * sizeof(float);
+  size_t o = 0;
+  l.wu_hi = o;  // the first four match the small-D path's (and moe_prepare_weights') planes
+  l.wu_lo = o += w;
+  l.wd_hi = o += w;
+  l.wd_lo = o += w;
+  o = align256(o + w);
+  l.x_hi = o;
+  l.x_lo = o = align256(o + (size_t)M * D * sizeof(float));
+  l.h_hi = o = align256(o + (size_t)M * D * sizeof(float));
+  l.h_lo = o = align256(o + (size_t)M * F * sizeof(float));
+  l.total = align256(o + (size_t)M * F * sizeof(float));
+  return l;
+}
+static size_t large_ws_bytes(int64_t M, int D, int F, int E, int dtype) {
+  if (dtype == MOE_DTYPE_F32) return tf32_large_layout(M, D, F, E).total;
   const size_t h = align256((size_t)M * F * 2);
   return dtype == MOE_DTYPE_FP8_E4M3_BLK128 ? h + (size_t)M * D * 2 : h;
 }
@@ -292,13 +360,16 @@ __global__ void bf16_to_f16_kernel(const uint4* __restrict__ x, uint4* __restric
   }
 }
 
-template <int EPI, bool BFP8>
-static int launch_gemm(const GemmMaps& maps, const GemmParams& prm, DevInfo* di, cudaStream_t st, int ctas_req) {
-  using Cfg = GemmCfg<EPI, BFP8>;
-  auto kern = grouped_gemm_pair_kernel<EPI, BFP8>;
-  constexpr int slot = 24 + 2 * EPI + (BFP8 ? 1 : 0);
-  constexpr int pslot = 8 + 2 * EPI + (BFP8 ? 1 : 0);
-  static_assert(slot < 36 && pslot < 18, "attribute slot");
+template <int EPI, bool BFP8, bool TF32 = false>
+static int launch_gemm(const GemmMaps& maps, const GemmParams& prm_in, DevInfo* di, cudaStream_t st, int ctas_req) {
+  GemmParams prm = prm_in;
+  if (g_tune_group_m > 0) prm.group_m = (int)g_tune_group_m;
+  prm.l2_mode = (int)g_tune_l2;
+  using Cfg = GemmCfg<EPI, BFP8, TF32>;
+  auto kern = grouped_gemm_pair_kernel<EPI, BFP8, TF32>;
+  constexpr int slot = TF32 ? 40 + EPI : 24 + 2 * EPI + (BFP8 ? 1 : 0);
+  constexpr int pslot = TF32 ? 24 + EPI : 8 + 2 * EPI + (BFP8 ? 1 : 0);
+  static_assert(slot < 44 && pslot < 26 && (TF32 ? EPI < 2 : slot < 36 && pslot < 18), "attribute slot");
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -337,14 +408,86 @@ struct RunOpts {
   const EpDispatch* dispatch = nullptr;  // large-D bf16 path: the token dispatch runs inside the up GEMM
 };
 
+// f32 inputs with D outside the fused small-D kernels: the two grouped GEMMs
+// in 3xTF32.  One preparation launch splits X (and, unless the weights were
+// prepared, W_up and W_down, transposed) into tf32 hi/lo planes; the up GEMM
+// writes H as hi/lo planes; the down GEMM writes Y.
+static int run_large_tf32(const float* x, const float* w_up, const float* w_down, const int32_t* gs, float* y,
+                          int64_t M, int D, int F, int E, void* ws, size_t ws_bytes, cudaStream_t st, RunOpts opt,
+                          bool split_weights, DevInfo* di) {
+  const Tf32LargeLayout L = tf32_large_layout(M, D, F, E);
+  if (ws_bytes < L.total) return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", ws_bytes, L.total);
+  if (reinterpret_cast<uintptr_t>(ws) & 255u) return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+  if (reinterpret_cast<uintptr_t>(x) & 15u) return fail(MOE_ERR_MISALIGNED, "x must be 16-byte aligned");
+  uint8_t* b = static_cast<uint8_t*>(ws);
+  float* wu_hi = reinterpret_cast<float*>(b + L.wu_hi);
+  float* wu_lo = reinterpret_cast<float*>(b + L.wu_lo);
+  float* wd_hi = reinterpret_cast<float*>(b + L.wd_hi);
+  float* wd_lo = reinterpret_cast<float*>(b + L.wd_lo);
+  float* x_hi = reinterpret_cast<float*>(b + L.x_hi);
+  float* x_lo = reinterpret_cast<float*>(b + L.x_lo);
+  float* h_hi = reinterpret_cast<float*>(b + L.h_hi);
+  float* h_lo = reinterpret_cast<float*>(b + L.h_lo);
+  const int ctas = opt.ctas > 0 ? opt.ctas : (int)g_tune_ctas;
+  {
+    PrepArgs pa{};
+    const int cap = di->sms * 4;
+    if (split_weights) {
+      pa.wu = w_up;
+      pa.wd = w_down;
+      pa.wu_hi = wu_hi;
+      pa.wu_lo = wu_lo;
+      pa.wd_hi = wd_hi;
+      pa.wd_lo = wd_lo;
+      pa.D = D;
+      pa.F = F;
+      pa.E = E;
+      pa.w_blocks = E * ((D + 31) / 32) * ((F + 31) / 32);
+    }
+    pa.x = reinterpret_cast<const float4*>(x);
+    pa.x_hi = reinterpret_cast<float4*>(x_hi);
+    pa.x_lo = reinterpret_cast<float4*>(x_lo);
+    pa.x_n4 = (size_t)M * D / 4;
+    pa.x_blocks = (int)std::min<size_t>((pa.x_n4 + 255) / 256, (size_t)cap);
+    small_prep_kernel<<<2 * pa.w_blocks + pa.x_blocks, 256, 0, st>>>(pa);
+    MOE_CUDA_TRY(cudaGetLastError());
+  }
+  const auto F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  // up: H = GELU(X @ W_up[e]); B = W_up^T planes [E][F][D] (K-major)
+  GemmMaps m1;
+  memset(&m1, 0, sizeof(m1));
+  if (int r = make_map_2d(&m1.a, x_hi, F32, 4, (uint64_t)M, D, 32, 128)) return r;
+  if (int r = make_map_2d(&m1.a_lo, x_lo, F32, 4, (uint64_t)M, D, 32, 128)) return r;
+  if (int r = make_map_3d(&m1.b, wu_hi, F32, 4, (uint64_t)E, F, D, 32, 128)) return r;
+  if (int r = make_map_3d(&m1.b_lo, wu_lo, F32, 4, (uint64_t)E, F, D, 32, 128)) return r;
+  GemmParams p1{gs, h_hi, (int)M, E, F, D, 8, di->status, nullptr, 0};
+  p1.out2 = h_lo;
+  if (int r = launch_gemm<0, false, true>(m1, p1, di, st, ctas)) return r;
+  // down: Y = H @ W_down[e]; B = W_down^T planes [E][D][F]
+  GemmMaps m2;
+  memset(&m2, 0, sizeof(m2));
+  if (int r = make_map_2d(&m2.a, h_hi, F32, 4, (uint64_t)M, F, 32, 128)) return r;
+  if (int r = make_map_2d(&m2.a_lo, h_lo, F32, 4, (uint64_t)M, F, 32, 128)) return r;
+  if (int r = make_map_3d(&m2.b, wd_hi, F32, 4, (uint64_t)E, D, F, 32, 128)) return r;
+  if (int r = make_map_3d(&m2.b_lo, wd_lo, F32, 4, (uint64_t)E, D, F, 32, 128)) return r;
+  GemmParams p2{gs, y, (int)M, E, D, F, 8, di->status, nullptr, opt.skip_tail ? 1 : 0};
+  if (opt.scatter) p2.scatter = *opt.scatter;
+  return launch_gemm<1, false, true>(m2, p2, di, st, ctas);
+}
+
 static int run_large(const void* x, const void* w_up, const void* w_down, const int32_t* gs,
                      const float* w_up_scale, const float* w_down_scale, float* y, int64_t M, int D, int F, int E,
-                     int dtype, void* ws, size_t ws_bytes, cudaStream_t st, RunOpts opt = RunOpts()) {
+                     int dtype, void* ws, size_t ws_bytes, cudaStream_t st, RunOpts opt = RunOpts(),
+                     bool split_weights = true) {
   int dev;
   DevInfo* di;
   if (int r = device_info(&dev, &di)) return r;
+  if (dtype == MOE_DTYPE_F32)
+    return run_large_tf32(static_cast<const float*>(x), static_cast<const float*>(w_up),
+                          static_cast<const float*>(w_down), gs, y, M, D, F, E, ws, ws_bytes, st, opt, split_weights,
+                          di);
   const int ctas = opt.ctas > 0 ? opt.ctas : (int)g_tune_ctas;
-  const size_t need = large_ws_bytes(M, D, F, dtype);
+  const size_t need = large_ws_bytes(M, D, F, E, dtype);
   if (ws_bytes < need) return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", ws_bytes, need);
   if (reinterpret_cast<uintptr_t>(ws) & 255u) return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
   const bool fp8 = dtype == MOE_DTYPE_FP8_E4M3_BLK128;
@@ -371,12 +514,12 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
   memset(&m1, 0, sizeof(m1));
   if (int r = make_map_2d(&m1.a, xa, A16, 2, (uint64_t)M, D, 64, 128)) return r;
   if (fp8) {
-    if (int r = make_map_2d(&m1.b, w_up, U8, 1, (uint64_t)E * D, F, 128, 64)) return r;
+    if (int r = make_map_3d(&m1.b, w_up, U8, 1, (uint64_t)E, D, F, 128, 64)) return r;
   } else {
-    if (int r = make_map_2d(&m1.b, w_up, BF16, 2, (uint64_t)E * D, F, 64, 64)) return r;
+    if (int r = make_map_3d(&m1.b, w_up, BF16, 2, (uint64_t)E, D, F, 64, 64)) return r;
   }
-  GemmParams p1{gs, ws, (int)M, E, F, D, D, 8, status, w_up_scale, 0};
-  if (opt.dispatch && !fp8) p1.dispatch = *opt.dispatch;
+  GemmParams p1{gs, ws, (int)M, E, F, D, 8, status, w_up_scale, 0};
+  if (opt.dispatch && !fp8) p1.dispatch = *opt.dispatch;  // (f32 took run_large_tf32 above)
   if (int r = fp8 ? launch_gemm<0, true>(m1, p1, di, st, ctas) : launch_gemm<0, false>(m1, p1, di, st, ctas))
     return r;
   // down: Y = H @ W_down[e]
@@ -384,11 +527,11 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
   memset(&m2, 0, sizeof(m2));
   if (int r = make_map_2d(&m2.a, ws, A16, 2, (uint64_t)M, F, 64, 128)) return r;
   if (fp8) {
-    if (int r = make_map_2d(&m2.b, w_down, U8, 1, (uint64_t)E * F, D, 128, 64)) return r;
+    if (int r = make_map_3d(&m2.b, w_down, U8, 1, (uint64_t)E, F, D, 128, 64)) return r;
   } else {
-    if (int r = make_map_2d(&m2.b, w_down, BF16, 2, (uint64_t)E * F, D, 64, 64)) return r;
+    if (int r = make_map_3d(&m2.b, w_down, BF16, 2, (uint64_t)E, F, D, 64, 64)) return r;
   }
-  GemmParams p2{gs, y, (int)M, E, D, F, F, 8, status, w_down_scale, opt.skip_tail ? 1 : 0};
+  GemmParams p2{gs, y, (int)M, E, D, F, 8, status, w_down_scale, opt.skip_tail ? 1 : 0};
   if (opt.scatter) p2.scatter = *opt.scatter;
   return fp8 ? launch_gemm<1, true>(m2, p2, di, st, ctas) : launch_gemm<1, false>(m2, p2, di, st, ctas);
 }
@@ -446,7 +589,7 @@ static int run_train_forward(const void* x, const void* w_up, const void* w_down
   int dev;
   DevInfo* di;
   if (int r = device_info(&dev, &di)) return r;
-  const size_t need = large_ws_bytes(M, D, F, MOE_DTYPE_BF16);
+  const size_t need = large_ws_bytes(M, D, F, E, MOE_DTYPE_BF16);
   if (ws_bytes < need) return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", ws_bytes, need);
   if (reinterpret_cast<uintptr_t>(ws) & 255u) return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
   int* status = di->status;
@@ -455,15 +598,15 @@ static int run_train_forward(const void* x, const void* w_up, const void* w_down
   GemmMaps m1;
   memset(&m1, 0, sizeof(m1));
   if (int r = make_map_2d(&m1.a, x, BF16, 2, (uint64_t)M, D, 64, 128)) return r;
-  if (int r = make_map_2d(&m1.b, w_up, BF16, 2, (uint64_t)E * D, F, 64, 64)) return r;
-  GemmParams p1{gs, ws, (int)M, E, F, D, D, 8, status, nullptr, 0};
+  if (int r = make_map_3d(&m1.b, w_up, BF16, 2, (uint64_t)E, D, F, 64, 64)) return r;
+  GemmParams p1{gs, ws, (int)M, E, F, D, 8, status, nullptr, 0};
   p1.out2 = a_save;
   if (int r = launch_gemm<3, false>(m1, p1, di, st, ctas)) return r;
   GemmMaps m2;
   memset(&m2, 0, sizeof(m2));
   if (int r = make_map_2d(&m2.a, ws, BF16, 2, (uint64_t)M, F, 64, 128)) return r;
-  if (int r = make_map_2d(&m2.b, w_down, BF16, 2, (uint64_t)E * F, D, 64, 64)) return r;
-  GemmParams p2{gs, y, (int)M, E, D, F, F, 8, status, nullptr, 0};
+  if (int r = make_map_3d(&m2.b, w_down, BF16, 2, (uint64_t)E, F, D, 64, 64)) return r;
+  GemmParams p2{gs, y, (int)M, E, D, F, 8, status, nullptr, 0};
   return launch_gemm<1, false>(m2, p2, di, st, ctas);
 }
 
@@ -541,15 +684,15 @@ static int run_swiglu_train_forward(const void* x, const void* w_gu, const void*
   GemmMaps m1;
   memset(&m1, 0, sizeof(m1));
   if (int r = make_map_2d(&m1.a, x, BF16, 2, (uint64_t)M, D, 64, 128)) return r;
-  if (int r = make_map_2d(&m1.b, w_gu, BF16, 2, (uint64_t)E * D, 2 * F, 64, 64)) return r;
-  GemmParams p1{gs, ws, (int)M, E, 2 * F, D, D, 8, status, nullptr, 0};
+  if (int r = make_map_3d(&m1.b, w_gu, BF16, 2, (uint64_t)E, D, 2 * F, 64, 64)) return r;
+  GemmParams p1{gs, ws, (int)M, E, 2 * F, D, 8, status, nullptr, 0};
   p1.out2 = gu_save;
   if (int r = launch_gemm<4, false>(m1, p1, di, st, ctas)) return r;
   GemmMaps m2;
   memset(&m2, 0, sizeof(m2));
   if (int r = make_map_2d(&m2.a, ws, BF16, 2, (uint64_t)M, F, 64, 128)) return r;
-  if (int r = make_map_2d(&m2.b, w_down, BF16, 2, (uint64_t)E * F, D, 64, 64)) return r;
-  GemmParams p2{gs, y, (int)M, E, D, F, F, 8, status, nullptr, 0};
+  if (int r = make_map_3d(&m2.b, w_down, BF16, 2, (uint64_t)E, F, D, 64, 64)) return r;
+  GemmParams p2{gs, y, (int)M, E, D, F, 8, status, nullptr, 0};
   return launch_gemm<1, false>(m2, p2, di, st, ctas);
 }
 
@@ -677,11 +820,11 @@ static int run_swiglu(const void* x, const void* w_gu, const void* w_down, const
   memset(&m1, 0, sizeof(m1));
   if (int r = make_map_2d(&m1.a, xa, A16, 2, (uint64_t)M, D, 64, 128)) return r;
   if (fp8) {
-    if (int r = make_map_2d(&m1.b, w_gu, U8, 1, (uint64_t)E * D, 2 * F, 128, 64)) return r;
+    if (int r = make_map_3d(&m1.b, w_gu, U8, 1, (uint64_t)E, D, 2 * F, 128, 64)) return r;
   } else {
-    if (int r = make_map_2d(&m1.b, w_gu, BF16, 2, (uint64_t)E * D, 2 * F, 64, 64)) return r;
+    if (int r = make_map_3d(&m1.b, w_gu, BF16, 2, (uint64_t)E, D, 2 * F, 64, 64)) return r;
   }
-  GemmParams p1{gs, ws, (int)M, E, 2 * F, D, D, 8, status, s_gu, 0};
+  GemmParams p1{gs, ws, (int)M, E, 2 * F, D, 8, status, s_gu, 0};
   if (int r = fp8 ? launch_gemm<2, true>(m1, p1, di, st, ctas) : launch_gemm<2, false>(m1, p1, di, st, ctas))
     return r;
   // down: Y = H @ W_down[e]
@@ -689,11 +832,11 @@ static int run_swiglu(const void* x, const void* w_gu, const void* w_down, const
   memset(&m2, 0, sizeof(m2));
   if (int r = make_map_2d(&m2.a, ws, A16, 2, (uint64_t)M, F, 64, 128)) return r;
   if (fp8) {
-    if (int r = make_map_2d(&m2.b, w_down, U8, 1, (uint64_t)E * F, D, 128, 64)) return r;
+    if (int r = make_map_3d(&m2.b, w_down, U8, 1, (uint64_t)E, F, D, 128, 64)) return r;
   } else {
-    if (int r = make_map_2d(&m2.b, w_down, BF16, 2, (uint64_t)E * F, D, 64, 64)) return r;
+    if (int r = make_map_3d(&m2.b, w_down, BF16, 2, (uint64_t)E, F, D, 64, 64)) return r;
   }
-  GemmParams p2{gs, y, (int)M, E, D, F, F, 8, status, s_down, 0};
+  GemmParams p2{gs, y, (int)M, E, D, F, 8, status, s_down, 0};
   return fp8 ? launch_gemm<1, true>(m2, p2, di, st, ctas) : launch_gemm<1, false>(m2, p2, di, st, ctas);
 }
 
@@ -750,8 +893,9 @@ static int check_workspace(const SmallPlan& plan, const void* ws, size_t ws_byte
   return 0;
 }
 
-// Weight preparation: for the 3xTF32 path, split W_up / W_down into K-major
-// tf32 hi/lo planes at the start of the workspace.  Nothing for bf16.
+// Weight preparation: for the 3xTF32 paths (fused small-D and grouped
+// large-D), split W_up / W_down into K-major tf32 hi/lo planes at the start
+// of the workspace.  Nothing for bf16 or e4m3.
 static int prepare_small(const void* w_up, const void* w_down, int D, int F, int E, int dtype, void* ws,
                          size_t ws_bytes, cudaStream_t st) {
   const SmallPlan plan = small_plan(0, D, F, E, dtype);
@@ -1133,6 +1277,14 @@ int moe_set_tuning(int32_t key, int64_t value) {
       if (value > 2) return fail(MOE_ERR_INVALID_ARG, "pair mode must be 0, 1 or 2");
       g_tune_pair = value;
       return 0;
+    case 5:
+      if (value > 64) return fail(MOE_ERR_INVALID_ARG, "rasterisation group must be 0 .. 64 row blocks");
+      g_tune_group_m = value;
+      return 0;
+    case 6:
+      if (value > 3) return fail(MOE_ERR_INVALID_ARG, "L2 hint mode must be 0 .. 3");
+      g_tune_l2 = value;
+      return 0;
   }
   return fail(MOE_ERR_INVALID_ARG, "unknown tuning key %d", key);
 }
@@ -1151,7 +1303,7 @@ int moe_device_status(int reset) {
 size_t moe_fused_mlp_workspace_size(int64_t M, int32_t D, int32_t F, int32_t E, int32_t dtype) {
   if (M < 0 || D <= 0 || F <= 0 || E <= 0) return 0;
   if (small_supported(D, F, dtype)) return align256(small_plan(M, D, F, E, dtype).ws_bytes);
-  if (large_supported(D, F, dtype)) return align256(large_ws_bytes(M, D, F, dtype));
+  if (large_supported(D, F, dtype)) return align256(large_ws_bytes(M, D, F, E, dtype));
   return 0;
 }
 
@@ -1180,9 +1332,10 @@ int moe_prepare_weights(const void* w_up, const void* w_down, const float* w_up_
   if (dtype != MOE_DTYPE_F32 && dtype != MOE_DTYPE_BF16 && dtype != MOE_DTYPE_FP8_E4M3_BLK128)
     return fail(MOE_ERR_UNSUPPORTED_DTYPE, "dtype %d", dtype);
   if (!w_up || !w_down) return fail(MOE_ERR_INVALID_ARG, "null weight pointer");
-  if (large_supported(D, F, dtype) && !small_supported(D, F, dtype)) return 0;  // weights used as given
-  if (!small_supported(D, F, dtype))
+  if (!small_supported(D, F, dtype) && !large_supported(D, F, dtype))
     return fail(MOE_ERR_UNSUPPORTED_SHAPE, "no kernel for D=%d F=%d dtype=%d", D, F, dtype);
+  // 16-bit and e4m3 weights are used as given; f32 weights (either path)
+  // become the four tf32 planes at the start of the workspace.
   return prepare_small(w_up, w_down, D, F, E, dtype, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
@@ -1195,7 +1348,7 @@ int moe_fused_mlp_prepared(const void* x, const void* w_up, const void* w_down, 
   if (M == 0) return 0;
   if (!small_supported(D, F, dtype))
     return run_large(x, w_up, w_down, group_sizes, w_up_scale, w_down_scale, y, M, D, F, E, dtype, workspace,
-                     workspace_bytes, static_cast<cudaStream_t>(stream));
+                     workspace_bytes, static_cast<cudaStream_t>(stream), RunOpts(), /*split_weights=*/false);
   return run_small(x, w_up, w_down, group_sizes, y, M, D, F, E, dtype, workspace, workspace_bytes,
                    static_cast<cudaStream_t>(stream));
 }
@@ -1254,6 +1407,12 @@ int moe_ep_create(int32_t rank, int32_t world, int32_t num_local_experts, int64_
     return fail(MOE_ERR_UNSUPPORTED_DTYPE, "dtype %d", dtype);
   if (D <= 0 || F <= 0 || (!small_supported(D, F, dtype) && !large_supported(D, F, dtype)))
     return fail(MOE_ERR_UNSUPPORTED_SHAPE, "no kernel for D=%d F=%d dtype=%d", D, F, dtype);
+  // The engine's two-GEMM experts are the 16-bit / e4m3 grouped GEMMs on
+  // whole 256-column tiles; f32 runs through the fused small-D kernels only.
+  if (!small_supported(D, F, dtype) && (dtype == MOE_DTYPE_F32 || D % 256 != 0 || F % 256 != 0))
+    return fail(MOE_ERR_UNSUPPORTED_SHAPE,
+                "expert-parallel engine: two-GEMM experts need bf16 or e4m3 with D and F multiples of 256 "
+                "(got D=%d F=%d dtype=%d)", D, F, dtype);
   int dev;
   DevInfo* di;
   if (int r = device_info(&dev, &di)) return r;
@@ -1323,7 +1482,7 @@ int moe_ep_create(int32_t rank, int32_t world, int32_t num_local_experts, int64_
   ep->abort_word = reinterpret_cast<int*>(ep->tables + t_slices + t_rows + t_gs + 256 + 256);
   if (scatter) ep->recv = reinterpret_cast<int4*>(ep->tables + t_slices + t_rows + t_gs + t_misc);
   ep->ws_bytes = small_supported(D, F, dtype) ? align256(small_plan(cap, D, F, ep->el, dtype).ws_bytes)
-                                              : align256(large_ws_bytes(cap, D, F, dtype));
+                                              : align256(large_ws_bytes(cap, D, F, ep->el, dtype));
   if (ep->ws_bytes && (e = cudaMalloc(&ep->ws, ep->ws_bytes)) != cudaSuccess) return cuda_fail(e, "cudaMalloc(workspace)");
   if ((e = cudaStreamCreateWithFlags(&ep->comm, cudaStreamNonBlocking)) != cudaSuccess)
     return cuda_fail(e, "cudaStreamCreate");
@@ -1782,7 +1941,8 @@ int moe_fused_mlp_launch_count(int64_t M, int32_t D, int32_t F, int32_t E, int32
   if (M == 0) return 0;
   if (!small_supported(D, F, dtype)) {
     if (!large_supported(D, F, dtype)) return fail(MOE_ERR_UNSUPPORTED_SHAPE, "D=%d F=%d dtype=%d", D, F, dtype);
-    return dtype == MOE_DTYPE_FP8_E4M3_BLK128 ? 3 : 2;  // (X -> f16,) up GEMM, down GEMM
+    // bf16: up GEMM, down GEMM; e4m3: X -> f16 first; f32: the tf32 split first
+    return dtype == MOE_DTYPE_BF16 ? 2 : 3;
   }
   int dev;
   DevInfo* di;
@@ -1807,7 +1967,7 @@ static int check_train_args(int64_t M, int32_t D, int32_t F, int32_t E) {
 
 size_t moe_fused_mlp_forward_train_workspace_size(int64_t M, int32_t D, int32_t F, int32_t E) {
   if (M < 0 || E <= 0 || !train_supported(D, F)) return 0;
-  return large_ws_bytes(M, D, F, MOE_DTYPE_BF16);
+  return large_ws_bytes(M, D, F, E, MOE_DTYPE_BF16);
 }
 
 int moe_fused_mlp_forward_train(const void* x, const void* w_up, const void* w_down, const int32_t* group_sizes,

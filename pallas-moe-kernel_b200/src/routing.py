@@ -182,20 +182,24 @@ def make_inputs_numpy(M: int, D: int, F: int, E: int, seed: int = 0):
 def quantize_e4m3_blockwise(w, block: int = 128):
     """FP8 e4m3 weights with per-(block x block) f32 scales: for each block of
     the last two dims, scale = amax / 448 (the e4m3 maximum) and
-    q = round_to_e4m3(w / scale).  ``w`` is a torch tensor (..., R, C) with
-    R, C multiples of ``block``; returns (q float8_e4m3fn, scale f32 of shape
-    (..., R/block, C/block)); dequantisation is q * scale per block."""
+    q = round_to_e4m3(w / scale).  ``w`` is a torch tensor (..., R, C); a
+    partial block at the end of R or C has a scale of its own.  Returns
+    (q float8_e4m3fn (..., R, C), scale f32 (..., ceil(R/block),
+    ceil(C/block))); dequantisation is q * scale per block."""
     import torch
     *lead, R, C = w.shape
-    wb = w.float().reshape(*lead, R // block, block, C // block, block)
-    amax = wb.abs().amax(dim=(-3, -1))                         # (..., R/b, C/b)
+    rb, cb = -(-R // block), -(-C // block)
+    wp = torch.zeros((*lead, rb * block, cb * block), dtype=torch.float32, device=w.device)
+    wp[..., :R, :C] = w.float()
+    wb = wp.reshape(*lead, rb, block, cb, block)
+    amax = wb.abs().amax(dim=(-3, -1))                         # (..., rb, cb)
     scale = torch.clamp(amax, min=1e-30) / 448.0
-    q = (wb / scale[..., :, None, :, None]).reshape(*lead, R, C).to(torch.float8_e4m3fn)
-    return q, scale.contiguous()
+    q = (wb / scale[..., :, None, :, None]).reshape(*lead, rb * block, cb * block)[..., :R, :C]
+    return q.contiguous().to(torch.float8_e4m3fn), scale.contiguous()
 
 
 def dequantize_e4m3_blockwise(q, scale, block: int = 128):
-    """q * scale per (block x block) tile, as float32."""
+    """q * scale per (block x block) tile (partial tiles at the ends), as float32."""
     *lead, R, C = q.shape
-    qb = q.float().reshape(*lead, R // block, block, C // block, block)
-    return (qb * scale[..., :, None, :, None]).reshape(*lead, R, C)
+    s = scale.repeat_interleave(block, dim=-2).repeat_interleave(block, dim=-1)[..., :R, :C]
+    return q.float() * s
