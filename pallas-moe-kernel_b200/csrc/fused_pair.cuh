@@ -388,10 +388,10 @@ __global__ void __launch_bounds__(64 + 256, 1)
             float4* ptr = reinterpret_cast<float4*>(rowp + ((g ^ rsw) << 4));
             float4 v = *ptr;
             float4 h;
-            h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-            h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-            h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-            h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+            h.x = __uint_as_float(tf32_hi_bits(__float_as_uint(v.x)));
+            h.y = __uint_as_float(tf32_hi_bits(__float_as_uint(v.y)));
+            h.z = __uint_as_float(tf32_hi_bits(__float_as_uint(v.z)));
+            h.w = __uint_as_float(tf32_hi_bits(__float_as_uint(v.w)));
             lo[4 * g + 0] = __float_as_uint(v.x - h.x);
             lo[4 * g + 1] = __float_as_uint(v.y - h.y);
             lo[4 * g + 2] = __float_as_uint(v.z - h.z);

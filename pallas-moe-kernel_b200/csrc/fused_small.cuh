@@ -23,7 +23,7 @@
 //   kModeBF16  : bf16 X / W, f32 accumulate, bf16 hidden operand.
 //   kModeTF32x3: f32 X / W.  Every product a*b is evaluated as
 //                a_hi*b_hi + a_hi*b_lo + a_lo*b_hi with a_hi = a rounded
-//                toward zero to tf32 (19 bits) and a_lo = a - a_hi, which
+//                to the nearest tf32 value and a_lo = a - a_hi, which
 //                keeps the result within ~1e-6 relative of f32 math.
 //                Weights arrive pre-split (hi/lo planes, transposed to
 //                K-major).  With a resident X tile (D <= 128) the GELU warps
@@ -515,7 +515,7 @@ __global__ void __launch_bounds__(64 + 256, 1)
       r = __all_sync(0xffffffffu, r);
       return r;
     };
-    // Split of the resident f32 X tile: hi = x rounded toward zero to tf32,
+    // Split of the resident f32 X tile: hi = x rounded to tf32 (tf32_hi_bits),
     // written back in place (shared memory, swizzled K-major layout); lo =
     // x - hi, written to this thread's TMEM lane as MMA1's second A operand.
     // Each thread owns one row and half of its D columns.
@@ -531,10 +531,10 @@ __global__ void __launch_bounds__(64 + 256, 1)
           float4* ptr = reinterpret_cast<float4*>(rowp + ((g ^ rsw) << 4));
           float4 v = *ptr;
           float4 h;
-          h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-          h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-          h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-          h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+          h.x = __uint_as_float(tf32_hi_bits(__float_as_uint(v.x)));
+          h.y = __uint_as_float(tf32_hi_bits(__float_as_uint(v.y)));
+          h.z = __uint_as_float(tf32_hi_bits(__float_as_uint(v.z)));
+          h.w = __uint_as_float(tf32_hi_bits(__float_as_uint(v.w)));
           lo[4 * g + 0] = __float_as_uint(v.x - h.x);
           lo[4 * g + 1] = __float_as_uint(v.y - h.y);
           lo[4 * g + 2] = __float_as_uint(v.z - h.z);

@@ -12,8 +12,8 @@
 // 256 columns) so the epilogue of one tile overlaps the MMAs of the next.
 //
 // f32 inputs (TF32 = true) run as 3xTF32 on kind::tf32: A and B come as tf32
-// hi/lo planes (value = hi + lo, hi = the value with its low 13 mantissa bits
-// cleared), B transposed to K-major (W^T (N, K) per expert), and every K step
+// hi/lo planes (value = hi + lo, hi = the value rounded to tf32), B
+// transposed to K-major (W^T (N, K) per expert), and every K step
 // issues hi*hi + hi*lo + lo*hi.  The up GEMM's epilogue writes H as hi/lo f32
 // planes for the down GEMM.
 //
@@ -138,6 +138,14 @@ struct GemmCfg {
   static constexpr int PUSH_SMEM = PUSH_WARPS ? (kEpMaxExperts + 1) * 4 : 0;
   static constexpr int SMEM = 1024 + NS * STAGE + NR * B8_BYTES + OUT_STAGE + BAR_BYTES + PUSH_SMEM;
   static constexpr int TMEM_COLS = 512;                 // 2 accumulators x 256 columns
+  // Accumulator buffers per tile: 16-bit operands double-buffer one
+  // 256-column accumulator (the epilogue of tile t overlaps the MMAs of
+  // t + 1).  3xTF32 keeps two accumulators per tile instead -- hi*hi in one,
+  // the small cross terms hi*lo + lo*hi in the other, summed in the epilogue
+  // with f32 rounding -- so that the large one takes K/8 accumulate steps
+  // rather than 3K/8 (each accumulate step into TMEM truncates, an error that
+  // grows with the number of steps), at the cost of that overlap.
+  static constexpr uint32_t NACC = TF32 ? 1 : 2;
   // e4m3 weights run as f16 operands (f16 X, f16 H, f16 dequantised B).
   // 16-bit B is read MN-major (the weights' own layout); tf32 B is K-major.
   static constexpr uint32_t IDESC = TF32 ? make_idesc(kFmtTF32, 256, BN, 0, 0)
@@ -396,8 +404,8 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32>::LAUNCH_BOUND, 1)
       uint32_t tcount = 0;
       for (int t = pair;; t += npairs, ++tcount) {
         if (!cur.seek(t, p.group_sizes, p.E, p.M, nt)) break;
-        const uint32_t ab = tcount & 1u;
-        const uint32_t use = tcount >> 1;
+        const uint32_t ab = tcount % C::NACC;
+        const uint32_t use = tcount / C::NACC;
         if (!mbar_wait_warp(acc_empty + ab, (use & 1u) ^ 1u, abort_flag, p.status)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + ab * C::BN;
@@ -418,9 +426,10 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32>::LAUNCH_BOUND, 1)
 #pragma unroll
             for (int ki = 0; ki < C::BK / 8; ++ki) {
               const uint64_t o = (uint64_t)((ki * 32) >> 4);
-              umma_ss_pair<Kind::TF32>(d_tmem, ah + o, bl + o, C::IDESC, (kb > 0 || ki > 0) ? 1u : 0u);
-              umma_ss_pair<Kind::TF32>(d_tmem, al + o, bh + o, C::IDESC, 1u);
-              umma_ss_pair<Kind::TF32>(d_tmem, ah + o, bh + o, C::IDESC, 1u);
+              const uint32_t acc = (kb > 0 || ki > 0) ? 1u : 0u;
+              umma_ss_pair<Kind::TF32>(d_tmem + C::BN, ah + o, bl + o, C::IDESC, acc);  // cross terms
+              umma_ss_pair<Kind::TF32>(d_tmem + C::BN, al + o, bh + o, C::IDESC, 1u);
+              umma_ss_pair<Kind::TF32>(d_tmem, ah + o, bh + o, C::IDESC, acc);          // hi * hi
             }
           } else {
             const uint64_t a_desc = make_sdesc(st, 16, 1024);
@@ -614,8 +623,8 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32>::LAUNCH_BOUND, 1)
       cur.coords(t, nt, p.group_m, mb, nb);
       const int row_end = cur.row_begin + cur.rows;
       const int wrow0 = cur.row_begin + mb * 256 + (int)rank * C::BM + (int)q * 32;
-      const uint32_t ab = tcount & 1u;
-      const uint32_t use = tcount >> 1;
+      const uint32_t ab = tcount % C::NACC;
+      const uint32_t use = tcount / C::NACC;
       if (!mbar_wait_warp(acc_full + ab, use & 1u, abort_flag, p.status)) break;
       tc_fence_after();
       const uint32_t acc = lane_base + ab * C::BN;
@@ -625,17 +634,18 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32>::LAUNCH_BOUND, 1)
       const int ncol = p.N - nb * C::BN < C::BN ? p.N - nb * C::BN : C::BN;
       if constexpr (TF32 && EPI == 0) {
         // 32 columns per step: GELU (f32 accuracy), then the tf32 split
-        // g = hi + lo (hi = g with its low 13 mantissa bits cleared); each
-        // plane goes out through the 32-row x 128-byte staging as full-line
-        // row stores.
+        // g = hi + lo (tf32_hi_bits); each plane goes out through the 32-row
+        // x 128-byte staging as full-line row stores.
         float4* wst4 = reinterpret_cast<float4*>(wst);
 #pragma unroll 1
         for (int c0 = 0; c0 < ncol; c0 += 32) {
-          uint32_t v[32];
+          uint32_t v[32], w[32];
           tmem_ld32(acc + c0, v);
+          tmem_ld32(acc + C::BN + c0, w);  // cross terms
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(gelu_tanh_exp(__uint_as_float(v[i])));
+          for (int i = 0; i < 32; ++i)
+            v[i] = __float_as_uint(gelu_tanh_exp(__uint_as_float(v[i]) + __uint_as_float(w[i])));
           const int gcol = nb * C::BN + c0;
 #pragma unroll 1
           for (int pl = 0; pl < 2; ++pl) {
@@ -645,7 +655,7 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32>::LAUNCH_BOUND, 1)
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
                 const float g = __uint_as_float(v[4 * k + j]);
-                const float h = __uint_as_float(v[4 * k + j] & 0xFFFFE000u);
+                const float h = __uint_as_float(tf32_hi_bits(v[4 * k + j]));
                 q[j] = pl == 0 ? h : g - h;
               }
               wst4[lane * 8 + (k ^ (lane & 7))] = make_float4(q[0], q[1], q[2], q[3]);
@@ -820,6 +830,36 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32>::LAUNCH_BOUND, 1)
             }
             __syncwarp();
           }
+        }
+      } else if constexpr (TF32) {
+        // f32 Y = hi*hi accumulator + cross-term accumulator, 32 columns per
+        // step through the same staging as store_y_block.
+        float* Y = reinterpret_cast<float*>(p.out) + (size_t)nb * C::BN;
+        float4* wst4 = reinterpret_cast<float4*>(wst);
+#pragma unroll 1
+        for (int c0 = 0; c0 < ncol; c0 += 32) {
+          uint32_t v[32], w[32];
+          tmem_ld32(acc + c0, v);
+          tmem_ld32(acc + C::BN + c0, w);
+          tmem_ld_wait();
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            wst4[lane * 8 + (k ^ (lane & 7))] = make_float4(
+                __uint_as_float(v[4 * k]) + __uint_as_float(w[4 * k]),
+                __uint_as_float(v[4 * k + 1]) + __uint_as_float(w[4 * k + 1]),
+                __uint_as_float(v[4 * k + 2]) + __uint_as_float(w[4 * k + 2]),
+                __uint_as_float(v[4 * k + 3]) + __uint_as_float(w[4 * k + 3]));
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = 4 * i + (int)(lane >> 3);
+            const int k = (int)(lane & 7);
+            const float4 val = wst4[r * 8 + (k ^ (r & 7))];
+            const int row = wrow0 + r;
+            if (row < row_end && c0 + 4 * k < ncol)
+              *reinterpret_cast<float4*>(Y + (size_t)row * p.N + c0 + 4 * k) = val;
+          }
+          __syncwarp();
         }
       } else if (p.scatter.on) {
         // Destination of row wrow0 + lane: the source rank whose rows of

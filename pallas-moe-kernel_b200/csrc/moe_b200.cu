@@ -216,8 +216,8 @@ static int device_info(int* dev_out, DevInfo** info) {
 }
 
 // ------------------------------------------------------------------ operand pre-split (3xTF32)
-// W (E, R, C) f32 -> hi/lo planes of W^T (E, C, R): hi = W rounded toward
-// zero to tf32, lo = W - hi.  32x32 tiles through shared memory so both the
+// W (E, R, C) f32 -> hi/lo planes of W^T (E, C, R): hi = W rounded to the
+// nearest tf32 value (tf32_hi_bits), lo = W - hi.  32x32 tiles through shared memory so both the
 // read and the write are coalesced.
 // One 32x32 tile (rows r0.., columns c0.. of expert e) by 256 threads laid
 // out 32 x 8 (tx = column lane, ty = row group).
@@ -236,7 +236,7 @@ __device__ __forceinline__ void split_transpose_tile(const float* __restrict__ w
     const int c = c0 + i, r = r0 + tx;
     if (r < R && c < C) {
       const float v = tile[tx][i];
-      const float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+      const float h = __uint_as_float(tf32_hi_bits(__float_as_uint(v)));
       dh[(size_t)c * R + r] = h;
       dl[(size_t)c * R + r] = v - h;
     }
@@ -251,10 +251,10 @@ __global__ void __launch_bounds__(256) split_transpose_kernel(const float* __res
 }
 
 __device__ __forceinline__ float4 tf32_hi4(float4 v) {
-  return make_float4(__uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u),
-                     __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u),
-                     __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u),
-                     __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u));
+  return make_float4(__uint_as_float(tf32_hi_bits(__float_as_uint(v.x))),
+                     __uint_as_float(tf32_hi_bits(__float_as_uint(v.y))),
+                     __uint_as_float(tf32_hi_bits(__float_as_uint(v.z))),
+                     __uint_as_float(tf32_hi_bits(__float_as_uint(v.w))));
 }
 
 // Everything a small-D call does before the fused kernel, in one launch:

@@ -21,6 +21,15 @@ enum : int {
 // and unwinds instead of spinning forever.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
+// tf32 "hi" part of an f32 value for the 3xTF32 splits v = hi + lo: v
+// rounded to the nearest value with 10 mantissa bits (ties away from zero),
+// as f32 bits.  lo = v - hi is exact (hi is within a factor of two of v),
+// |lo| <= 2^-11 |v|, and lo takes either sign, so the tensor core's
+// truncation of lo to tf32 leaves an error of either sign instead of one
+// that always shrinks |v|.  For finite v the add cannot carry out of the
+// 32-bit word (the largest finite pattern is 0xFF7FFFFF).
+__host__ __device__ __forceinline__ uint32_t tf32_hi_bits(uint32_t v) { return (v + 0x1000u) & 0xFFFFE000u; }
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -501,7 +510,8 @@ __device__ __forceinline__ void gelu_split_tf32x2(uint32_t& a0, uint32_t& a1, ui
   f2_unpack(d, d0, d1);
   const uint64_t g = f2_mul(x, f2_pack(__float_as_uint(rcp_approx(__uint_as_float(d0))),
                                        __float_as_uint(rcp_approx(__uint_as_float(d1)))));
-  const uint64_t h = g & 0xFFFFE000FFFFE000ull;
+  // tf32_hi_bits on both lanes (no carry crosses from the low word: finite f32)
+  const uint64_t h = (g + 0x0000100000001000ull) & 0xFFFFE000FFFFE000ull;
   f2_unpack(h, a0, a1);
   f2_unpack(f2_sub(g, h), b0, b1);
 }
