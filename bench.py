@@ -201,21 +201,20 @@ def make_workload(cfg, device, seed: int = 0, experts=None):
 
 
 def algorithmic(cfg, gs) -> dict:
-    """FLOPs = 4 M D F (GELU excluded); bytes = X + non-empty experts' weights + Y."""
-    sx = 4 if cfg.dtype == "f32" else 2
-    sw = {"f32": 4, "bf16": 2, "fp8": 1}[cfg.dtype]
-    active = int(np.count_nonzero(np.asarray(gs) > 0))
-    scale_bytes = 2 * (cfg.D // 128) * (cfg.F // 128) * 4 if cfg.dtype == "fp8" else 0
-    byts = cfg.M * cfg.D * sx + active * (2 * cfg.D * cfg.F * sw + scale_bytes) + cfg.M * cfg.D * 4
-    return {"flops": 4 * cfg.M * cfg.D * cfg.F, "bytes": byts}
+    """FLOPs = 4 M D F (GELU excluded); bytes = X + non-empty experts' weights
+    (+ FP8 block scales) + Y -- the analytic model's figures."""
+    from src import analysis
+    w = analysis.algorithmic_work(cfg.M, cfg.D, cfg.F, gs, cfg.dtype)
+    return {"flops": w["flops"], "bytes": w["bytes"]}
 
 
 def tensor_peak(cfg, peaks) -> tuple[float, str]:
-    bf16 = float(peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"]))
+    from src import analysis
+    p = analysis.tensor_peak(cfg.dtype, peaks)
     if cfg.dtype == "f32":
-        return bf16 / 6.0, (f"bf16 {bf16:.1f} TF/s / 6: kind::tf32 issues at half the f16 rate and "
-                            f"3xTF32 spends 3 products per f32 product")
-    return bf16, f"bf16 {bf16:.1f} TF/s"
+        return p, (f"bf16 {6 * p:.1f} TF/s / 6: kind::tf32 issues at half the f16 rate and "
+                   f"3xTF32 spends 3 products per f32 product")
+    return p, f"bf16 {p:.1f} TF/s"
 
 
 def sustained_frac(achieved: float, peak: float, peaks: dict):

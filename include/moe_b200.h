@@ -82,6 +82,44 @@ size_t moe_fused_mlp_workspace_size(int64_t M, int32_t D, int32_t F, int32_t E, 
 int moe_fused_mlp_launch_count(int64_t M, int32_t D, int32_t F, int32_t E, int32_t dtype);
 
 /*
+ * The launch plan of moe_fused_mlp for a problem, as the library would run it
+ * on a device with `sms` SMs (<= 0: the current device).  No counterpart in
+ * the reference; it feeds the analytic roofline model (src/analysis.py) with
+ * the real tiling instead of a restatement of it.  No device work, no sync.
+ * Fills out[0 .. min(count, max_out) - 1] in launch order and returns the
+ * launch count (the value moe_fused_mlp_launch_count returns), or a negative
+ * MOE_ERR_* code.  Grids are those of the automatic choices (persistent
+ * kernels: one CTA per SM, or per SM pair) and of tuning keys 1 and 2 when
+ * set; tuning key 4 (kernel family) is ignored.
+ */
+enum {
+  MOE_MMA_NONE = 0,    /* no tensor-core work (conversion / split launches) */
+  MOE_MMA_BF16 = 1,    /* tcgen05 kind::f16 on bf16 operands */
+  MOE_MMA_F16 = 2,     /* tcgen05 kind::f16 on f16 operands (e4m3 weights decoded in shared memory) */
+  MOE_MMA_TF32X3 = 3   /* tcgen05 kind::tf32, three products per f32 product */
+};
+typedef struct moe_launch_desc {
+  char kernel[48];       /* kernel family */
+  int32_t grid;          /* CTAs launched */
+  int32_t threads;       /* threads per CTA */
+  int32_t smem_bytes;    /* shared memory per CTA (dynamic + static) */
+  int32_t tmem_cols;     /* TMEM columns allocated per CTA (0: none) */
+  int32_t cluster;       /* CTAs per cluster (2: CTA pair issuing cta_group::2 MMAs) */
+  int32_t tile_m;        /* rows of one work unit (over the whole cluster) */
+  int32_t tile_n;        /* grouped GEMM: output columns per tile; fused kernel: hidden columns per chunk */
+  int32_t stage_k;       /* reduction elements per pipeline stage */
+  int32_t stages;        /* operand ring stages */
+  int32_t mma_kind;      /* MOE_MMA_* */
+  int32_t gemm_n;        /* grouped GEMM: N; fused kernel: D */
+  int32_t gemm_k;        /* grouped GEMM: K; fused kernel: F */
+  int32_t f_splits;      /* fused kernel: F-splits per row block (1 elsewhere) */
+  int32_t accumulators;  /* TMEM accumulator buffers in flight per CTA */
+  int32_t reserved;
+} moe_launch_desc;
+int moe_describe_plan(int64_t M, int32_t D, int32_t F, int32_t E, int32_t dtype, int32_t sms, moe_launch_desc* out,
+                      int32_t max_out);
+
+/*
  * Two-stage form of moe_fused_mlp for weights that stay fixed across calls
  * (no counterpart in the reference, whose entry point re-reads the weights
  * every call; moe_fused_mlp == moe_prepare_weights + moe_fused_mlp_prepared).

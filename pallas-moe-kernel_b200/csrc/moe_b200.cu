@@ -963,10 +963,10 @@ static int launch_pair(const FusedMaps& maps, const FusedParams& prm, int pairs_
 // (measured on B200 over M = 128 ... 131072, D = 64 ... 256, E = 4 ... 16,
 // f32 and bf16).  Row blocks are estimated from M; at small M every expert is
 // taken to hold a partial block of its own.
-static int small_splits(int64_t M, int E, int nch_total, bool pair, const DevInfo* di) {
+static int small_splits(int64_t M, int E, int nch_total, bool pair, int sms) {
   if (g_tune_splits > 0) return (int)g_tune_splits;
   const int rows_per_unit = pair ? 256 : 128;
-  const int64_t workers = pair ? di->sms / 2 : di->sms;
+  const int64_t workers = pair ? sms / 2 : sms;
   const int64_t blocks_est =
       std::max<int64_t>((M + rows_per_unit - 1) / rows_per_unit, std::min<int64_t>(E, (M + 15) / 16));
   int splits = 1;
@@ -994,7 +994,7 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
     return fail(MOE_ERR_INVALID_ARG, "CTA-pair kernel not available for D=%d dtype=%d", D, dtype);
   if (g_tune_splits > 0 && nch_total % g_tune_splits != 0)
     return fail(MOE_ERR_INVALID_ARG, "tuning splits=%d does not divide %d chunks", (int)g_tune_splits, nch_total);
-  const int splits = small_splits(M, E, nch_total, pair, di);
+  const int splits = small_splits(M, E, nch_total, pair, di->sms);
   const int ctas_req = opt.ctas > 0 ? opt.ctas : (int)g_tune_ctas;
   int ctas = ctas_req > 0 && ctas_req < di->sms ? ctas_req : di->sms;
 
@@ -1948,10 +1948,108 @@ int moe_fused_mlp_launch_count(int64_t M, int32_t D, int32_t F, int32_t E, int32
   DevInfo* di;
   if (int r = device_info(&dev, &di)) return r;
   const SmallPlan plan = small_plan(M, D, F, E, dtype);
-  const int splits = small_splits(M, E, F / plan.bf, g_tune_pair == 2, di);
+  const int splits = small_splits(M, E, F / plan.bf, g_tune_pair == 2, di->sms);
   // One preparation launch (weight planes, X planes, Y zeroing) when any of
   // them is needed, then the fused kernel.
   return (dtype == MOE_DTYPE_F32 || splits > 1 ? 1 : 0) + 1;
+}
+
+}  // extern "C"
+
+namespace moe {
+static void desc_set(moe_launch_desc* d, const char* name, int grid, int threads, int smem, int tmem, int cluster,
+                     int tm, int tn, int sk, int stages, int kind, int n, int k, int splits, int accs) {
+  memset(d, 0, sizeof(*d));
+  snprintf(d->kernel, sizeof(d->kernel), "%s", name);
+  d->grid = grid;
+  d->threads = threads;
+  d->smem_bytes = smem;
+  d->tmem_cols = tmem;
+  d->cluster = cluster;
+  d->tile_m = tm;
+  d->tile_n = tn;
+  d->stage_k = sk;
+  d->stages = stages;
+  d->mma_kind = kind;
+  d->gemm_n = n;
+  d->gemm_k = k;
+  d->f_splits = splits;
+  d->accumulators = accs;
+}
+template <int EPI, bool BFP8, bool TF32>
+static void desc_gemm(moe_launch_desc* d, const char* name, int pairs, int N, int K) {
+  using C = GemmCfg<EPI, BFP8, TF32>;
+  desc_set(d, name, 2 * pairs, C::THREADS, C::SMEM, C::TMEM_COLS, 2, 2 * C::BM, C::BN, C::BK, C::NS,
+           TF32 ? MOE_MMA_TF32X3 : (BFP8 ? MOE_MMA_F16 : MOE_MMA_BF16), N, K, 1, (int)C::NACC);
+}
+template <int MODE, int D, int BF, bool XR>
+static void desc_small(moe_launch_desc* d, int ctas, int F, int splits) {
+  using C = FusedCfg<MODE, D, BF, XR>;
+  desc_set(d, "fused_mlp_small_kernel", ctas, C::THREADS, C::SMEM, C::TMEM_COLS, 1, C::BM, BF, C::SK1, C::NS,
+           MODE == kModeTF32x3 ? MOE_MMA_TF32X3 : MOE_MMA_BF16, D, F, splits, 2);
+}
+}  // namespace moe
+
+extern "C" {
+
+int moe_describe_plan(int64_t M, int32_t D, int32_t F, int32_t E, int32_t dtype, int32_t sms, moe_launch_desc* out,
+                      int32_t max_out) {
+  t_err[0] = 0;
+  if (M < 0 || D <= 0 || F <= 0 || E <= 0 || dtype < 0 || dtype > 2 || max_out < 0 || (max_out > 0 && !out))
+    return fail(MOE_ERR_INVALID_ARG, "bad arguments M=%lld D=%d F=%d E=%d dtype=%d", (long long)M, D, F, E, dtype);
+  if (sms <= 0) {
+    int dev;
+    DevInfo* di;
+    if (int r = device_info(&dev, &di)) return r;
+    sms = di->sms;
+  }
+  if (M == 0) return 0;
+  moe_launch_desc d[4];
+  int n = 0;
+  const int prep_cap = sms * 4;
+  const int ctas_req = (int)g_tune_ctas;
+  if (!small_supported(D, F, dtype)) {
+    if (!large_supported(D, F, dtype)) return fail(MOE_ERR_UNSUPPORTED_SHAPE, "D=%d F=%d dtype=%d", D, F, dtype);
+    int pairs = sms / 2;
+    if (ctas_req > 0 && ctas_req / 2 < pairs) pairs = ctas_req / 2 > 0 ? ctas_req / 2 : 1;
+    if (dtype == MOE_DTYPE_F32) {
+      const int wb = E * ((D + 31) / 32) * ((F + 31) / 32);
+      const int xb = (int)std::min<int64_t>(((int64_t)M * D / 4 + 255) / 256, prep_cap);
+      desc_set(&d[n++], "small_prep_kernel", 2 * wb + xb, 256, 32 * 33 * 4, 0, 1, 0, 0, 0, 0, MOE_MMA_NONE, 0, 0, 1, 0);
+      desc_gemm<0, false, true>(&d[n++], "grouped_gemm_pair_kernel (up)", pairs, F, D);
+      desc_gemm<1, false, true>(&d[n++], "grouped_gemm_pair_kernel (down)", pairs, D, F);
+    } else if (dtype == MOE_DTYPE_FP8_E4M3_BLK128) {
+      const int xb = (int)std::min<int64_t>(((int64_t)M * D / 8 + 255) / 256, (int64_t)sms * 8);
+      desc_set(&d[n++], "bf16_to_f16_kernel", xb, 256, 0, 0, 1, 0, 0, 0, 0, MOE_MMA_NONE, 0, 0, 1, 0);
+      desc_gemm<0, true, false>(&d[n++], "grouped_gemm_pair_kernel (up)", pairs, F, D);
+      desc_gemm<1, true, false>(&d[n++], "grouped_gemm_pair_kernel (down)", pairs, D, F);
+    } else {
+      desc_gemm<0, false, false>(&d[n++], "grouped_gemm_pair_kernel (up)", pairs, F, D);
+      desc_gemm<1, false, false>(&d[n++], "grouped_gemm_pair_kernel (down)", pairs, D, F);
+    }
+  } else {
+    const SmallPlan plan = small_plan(M, D, F, E, dtype);
+    const int splits = small_splits(M, E, F / plan.bf, false, sms);
+    const int ctas = ctas_req > 0 && ctas_req < sms ? ctas_req : sms;
+    const bool f32 = dtype == MOE_DTYPE_F32;
+    const int wb = f32 ? E * ((D + 31) / 32) * ((F + 31) / 32) : 0;
+    const int xb = (f32 && !plan.x_res) ? (int)std::min<int64_t>(((int64_t)M * D / 4 + 255) / 256, prep_cap) : 0;
+    const int yb = splits > 1 ? (int)std::min<int64_t>(((int64_t)M * D / 4 + 255) / 256, prep_cap) : 0;
+    if (2 * wb + xb + yb > 0)
+      desc_set(&d[n++], "small_prep_kernel", 2 * wb + xb + yb, 256, 32 * 33 * 4, 0, 1, 0, 0, 0, 0, MOE_MMA_NONE, 0,
+               0, 1, 0);
+    if (f32) {
+      if (D == 64) desc_small<kModeTF32x3, 64, 64, true>(&d[n++], ctas, F, splits);
+      else if (D == 128) desc_small<kModeTF32x3, 128, 64, true>(&d[n++], ctas, F, splits);
+      else desc_small<kModeTF32x3, 256, 64, false>(&d[n++], ctas, F, splits);
+    } else {
+      if (D == 64) desc_small<kModeBF16, 64, 128, true>(&d[n++], ctas, F, splits);
+      else if (D == 128) desc_small<kModeBF16, 128, 128, true>(&d[n++], ctas, F, splits);
+      else desc_small<kModeBF16, 256, 128, true>(&d[n++], ctas, F, splits);
+    }
+  }
+  for (int i = 0; i < n && i < max_out; ++i) out[i] = d[i];
+  return n;
 }
 
 // ------------------------------------------------------------------ training

@@ -27,6 +27,32 @@ ERRORS = {
     -7: "MOE_ERR_MISALIGNED",
 }
 
+MMA_KINDS = {0: "none", 1: "kind::f16 (bf16)", 2: "kind::f16 (f16 from e4m3)", 3: "kind::tf32 x3"}
+
+
+class LaunchDesc(ctypes.Structure):
+    """``moe_launch_desc`` of include/moe_b200.h."""
+    _fields_ = [("kernel", ctypes.c_char * 48)] + [(n, ctypes.c_int32) for n in (
+        "grid", "threads", "smem_bytes", "tmem_cols", "cluster", "tile_m", "tile_n", "stage_k", "stages",
+        "mma_kind", "gemm_n", "gemm_k", "f_splits", "accumulators", "reserved")]
+
+    def as_dict(self) -> dict:
+        d = {n: getattr(self, n) for n, _ in self._fields_ if n not in ("kernel", "reserved")}
+        d["kernel"] = self.kernel.decode()
+        d["mma"] = MMA_KINDS.get(self.mma_kind, str(self.mma_kind))
+        return d
+
+
+def describe_plan(M: int, D: int, F: int, E: int, dtype: int, sms: int = 148) -> list[dict]:
+    """The library's launch plan for one moe_fused_mlp call (no device needed
+    when ``sms`` > 0)."""
+    arr = (LaunchDesc * 8)()
+    n = lib().moe_describe_plan(M, D, F, E, dtype, sms, arr, 8)
+    if n < 0:
+        raise MoeError(n, lib().moe_last_error().decode())
+    return [arr[i].as_dict() for i in range(n)]
+
+
 _lib = None
 
 
@@ -61,6 +87,8 @@ def lib() -> ctypes.CDLL:
     L.moe_last_error.restype = ctypes.c_char_p
     L.moe_device_status.argtypes = [ctypes.c_int]
     L.moe_device_status.restype = ctypes.c_int
+    L.moe_describe_plan.argtypes = [i64, i32, i32, i32, i32, i32, ctypes.POINTER(LaunchDesc), i32]
+    L.moe_describe_plan.restype = ctypes.c_int
     L.moe_sm_clock_sample.argtypes = [vp, i32, vp]
     L.moe_sm_clock_sample.restype = ctypes.c_int
     L.moe_version.argtypes = []

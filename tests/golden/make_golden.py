@@ -11,6 +11,8 @@ fixtures it writes are committed and travel, the reference does not:
   import JAX at the top -- on a grid of inputs;
 * collects the group sizes the reference recorded in
   results/structured_float32/results.csv (M, E, routing pattern -> sizes);
+* writes ``analysis_columns.json``: a sample of the published sweep's cases
+  with the analysis columns the reference's model recorded for them;
 * writes ``pallas-moe-kernel_b200/src/data/l4_structured_float32.json``: per
   shape of that published sweep (measured on an NVIDIA L4), the fused
   kernel's best median over the swept (BM, BF) tiles and the median of the
@@ -75,6 +77,43 @@ def write_l4_table(ref: Path) -> int:
     return len(rows)
 
 
+ANALYSIS_COLUMNS = [
+    "max_group_size", "programs_per_expert", "active_programs_Q", "launched_programs", "inactive_programs",
+    "grid_utilization", "processed_token_slots", "padded_rows", "row_utilization", "padding_overhead_fraction",
+    "padding_overhead_percent", "padding_overcompute_factor", "hidden_chunks_F_over_BF", "useful_flops",
+    "actual_fused_flops", "padding_extra_flops", "reference_min_bytes", "fused_min_bytes",
+    "hidden_activation_bytes", "hidden_intermediate_mib", "hidden_write_read_saved_bytes",
+    "memory_saved_fraction", "memory_saved_percent", "fused_no_cache_bytes", "fused_tile_upper_bytes",
+    "minimum_weight_bytes", "no_cache_weight_bytes", "weight_reread_factor_no_cache",
+    "reference_ideal_ai_flops_per_byte", "fused_ideal_effective_ai_flops_per_byte",
+    "fused_ideal_actual_ai_flops_per_byte", "fused_no_cache_actual_ai_flops_per_byte",
+    "fused_per_program_ai_flops_per_byte", "fused_large_F_ai_approximation", "expansion_ratio_F_over_D",
+    "token_to_expert_hidden_ratio_M_over_EF", "fraction_of_asymptotic_benefit",
+    "fraction_of_asymptotic_benefit_percent", "asymptotic_max_memory_speedup", "ideal_memory_speedup",
+    "logical_tile_shared_bytes", "inferred_one_extra_stage_shared_bytes",
+]
+
+
+def write_analysis_columns(ref: Path) -> int:
+    """Every 7th row of the reference's published sweep: the case's inputs
+    and the analysis columns it recorded (the values its model produced)."""
+    rows = []
+    with open(ref / "results" / "structured_float32" / "results.csv") as f:
+        for i, row in enumerate(csv.DictReader(f)):
+            if i % 7:
+                continue
+            case = {k: int(row[k]) for k in ("M", "D", "F", "E", "BM", "BF")}
+            case["group_sizes"] = json.loads(row["group_sizes"].replace("(", "[").replace(")", "]"))
+            case["dtype_bytes"] = 4
+            case["recorded"] = {c: (json.loads(row[c]) if c == "programs_per_expert" else float(row[c]))
+                                for c in ANALYSIS_COLUMNS}
+            rows.append(case)
+    (OUT / "analysis_columns.json").write_text(json.dumps({
+        "source": "results/structured_float32/results.csv of the reference (every 7th row)",
+        "cases": rows}, indent=0))
+    return len(rows)
+
+
 def main():
     REF = _reference_dir()
     bench = _load_functions(REF / "src/benchmark.py", {"make_group_sizes"})
@@ -116,7 +155,7 @@ def main():
         "experiment_make_group_sizes": cases_exp,
         "results_csv_recorded": recorded_list,
     }, indent=0))
-    print(len(cases_bench), len(cases_exp), len(recorded_list), write_l4_table(REF))
+    print(len(cases_bench), len(cases_exp), len(recorded_list), write_l4_table(REF), write_analysis_columns(REF))
 
 
 if __name__ == "__main__":

@@ -1,5 +1,6 @@
-"""moe_fused_mlp_launch_count (the bench's `gpu_launches`) against the
-kernels a call actually launches, counted with torch's profiler."""
+"""moe_fused_mlp_launch_count (the bench's `gpu_launches`) and the launch
+plan of moe_describe_plan (the analytic model's input) against the kernels a
+call actually launches, recorded with torch's profiler."""
 
 import pytest
 import torch
@@ -12,17 +13,19 @@ pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda:0")
 
 
-def _library_kernels(fn) -> int:
+def _library_kernels(fn) -> list[str]:
+    """Names of the library's kernels one call launches, in launch order."""
     from torch.profiler import ProfilerActivity, profile
     fn()
     torch.cuda.synchronize()
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         fn()
         torch.cuda.synchronize()
-    names = [e.key for e in prof.key_averages()]
-    if not names:
+    events = [e for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    if not events:
         pytest.skip("the profiler recorded no GPU activity on this box")
-    return sum(e.count for e in prof.key_averages() if "moe::" in e.key)
+    events.sort(key=lambda e: e.time_range.start)
+    return [e.name for e in events if "moe::" in e.name]
 
 
 @pytest.mark.parametrize("M,D,F,E,dt", [
@@ -31,6 +34,7 @@ def _library_kernels(fn) -> int:
     (512, 128, 512, 4, "bf16"),      # F split across CTAs: Y zeroed first
     (1024, 512, 1024, 4, "bf16"),    # two grouped GEMMs
     (1024, 512, 1024, 4, "fp8"),     # X to f16 + two grouped GEMMs
+    (1024, 320, 448, 4, "f32"),      # tf32 split + two 3xTF32 grouped GEMMs
 ])
 def test_launch_count_matches_launched_kernels(M, D, F, E, dt):
     g = torch.Generator(device=DEV)
@@ -49,5 +53,9 @@ def test_launch_count_matches_launched_kernels(M, D, F, E, dt):
     out = torch.empty((M, D), device=DEV)
     code = {"f32": _lib.MOE_DTYPE_F32, "bf16": _lib.MOE_DTYPE_BF16, "fp8": _lib.MOE_DTYPE_FP8_E4M3_BLK128}[dt]
     claimed = _lib.lib().moe_fused_mlp_launch_count(M, D, F, E, code)
-    counted = _library_kernels(lambda: fused_ragged_dot_caller(x, wu, wd, gs, max_group_size=M, out=out, **kw))
-    assert counted == claimed, (counted, claimed)
+    names = _library_kernels(lambda: fused_ragged_dot_caller(x, wu, wd, gs, max_group_size=M, out=out, **kw))
+    assert len(names) == claimed, (names, claimed)
+    plan = _lib.describe_plan(M, D, F, E, code, sms=torch.cuda.get_device_properties(DEV).multi_processor_count)
+    assert len(plan) == claimed
+    for launched, planned in zip(names, plan):
+        assert planned["kernel"].split()[0] in launched, (launched, planned["kernel"])
