@@ -120,6 +120,27 @@ int moe_describe_plan(int64_t M, int32_t D, int32_t F, int32_t E, int32_t dtype,
                       int32_t max_out);
 
 /*
+ * The expert-parallel engine's routing tables for one step, computed on the
+ * host by the same code the engine's count kernel runs on the device (no
+ * counterpart in the reference; it makes the tables testable without GPUs).
+ * `counts` is the world x E table of rows each source routes to each global
+ * expert in this step (host memory, row-major); row `rank` is this rank's own
+ * group sizes, taken as moe_ep_forward takes them (negatives count as 0, the
+ * running total is cut at M); the other rows are clamped to [0, max_rows].
+ * Outputs (host memory): slices [waves][E][4] = {first source row, rows,
+ * first row in the owner's landing region, owner} for this rank's rows;
+ * wave_rows [waves][E + 1] = the slices' row prefix per wave; local_gs
+ * [waves][num_local_experts] = this rank's landing-region group sizes;
+ * recv [num_local_experts][world][4] = {first region row, rows, first source
+ * row, source} (the scatter-mode receive table; may be null).  Returns the
+ * status bits the device would raise (2 = a negative size was clamped, 8 =
+ * rows were cut to M or a region) or a negative MOE_ERR_* code.
+ */
+int moe_ep_build_tables(const int32_t* counts, int32_t world, int32_t rank, int32_t num_local_experts,
+                        int32_t waves, int32_t region_cap, int32_t max_rows, int64_t M, int32_t* slices,
+                        int32_t* wave_rows, int32_t* local_gs, int32_t* recv);
+
+/*
  * Two-stage form of moe_fused_mlp for weights that stay fixed across calls
  * (no counterpart in the reference, whose entry point re-reads the weights
  * every call; moe_fused_mlp == moe_prepare_weights + moe_fused_mlp_prepared).

@@ -156,8 +156,90 @@ __device__ __forceinline__ bool ep_wait_flag(const uint32_t* flag, uint32_t epoc
   return true;
 }
 
-__device__ __forceinline__ int wave_cut(int c, int v, int waves) {
+__host__ __device__ __forceinline__ int wave_cut(int c, int v, int waves) {
   return (int)(((int64_t)c * v) / waves);
+}
+
+// ---------------------------------------------------------------- slice tables
+// The tables of one step are a pure function of the clamped count table
+// cnt[W][E] (rows source s routes to global expert g), this rank's own row
+// prefix own_off[E] and, in scatter mode, every source's row prefix
+// src_off[W][E].  ep_counts_kernel evaluates the pieces below one entry per
+// thread; moe_ep_build_tables evaluates them on the host, in order, so the
+// same code is testable without a GPU.
+
+// Rows of expert g in wave v over all sources.
+__host__ __device__ __forceinline__ int ep_wave_total(const int* cnt, int W, int E, int V, int v, int g) {
+  int n = 0;
+  for (int s = 0; s < W; ++s) {
+    const int c = cnt[s * E + g];
+    n += wave_cut(c, v + 1, V) - wave_cut(c, v, V);
+  }
+  return n;
+}
+
+// Owner p's landing region of wave v: turns the wave totals of its experts
+// (row[p * EL .. p * EL + EL)) into their first rows in the region, each cut
+// to what the region still holds; the cut sizes are the owner's group sizes
+// of that wave (written to local_gs when p is this rank).
+__host__ __device__ __forceinline__ void ep_owner_region(int* row, int p, int EL, int region_cap, int* local_gs) {
+  int run = 0;
+  for (int e = 0; e < EL; ++e) {
+    const int i = p * EL + e;
+    int n = row[i];
+    if (n > region_cap - run) n = region_cap - run;
+    row[i] = run;
+    if (local_gs) local_gs[e] = n;
+    run += n;
+  }
+}
+
+// This rank's slice of (wave v, expert g): inside the owner's region, sources
+// in rank order starting at the owner itself (owner o: o, o + 1, ..., o - 1
+// mod W), so that an owner's own rows lead each of its experts.  `start` is
+// the expert's first region row (ep_owner_region).  *clamped is set when the
+// slice had to be cut to the region.
+__host__ __device__ __forceinline__ EpSlice ep_slice(const int* cnt, const int* own_off, int start, int W, int E,
+                                                     int EL, int V, int rank, int region_cap, int v, int g,
+                                                     bool* clamped) {
+  const int o = g / EL;
+  int before = 0;
+  for (int s = o; s != rank; s = (s + 1 == W ? 0 : s + 1)) {
+    const int c = cnt[s * E + g];
+    before += wave_cut(c, v + 1, V) - wave_cut(c, v, V);
+  }
+  const int mine = cnt[rank * E + g];
+  EpSlice sl;
+  sl.src_row = own_off[g] + wave_cut(mine, v, V);
+  sl.n = wave_cut(mine, v + 1, V) - wave_cut(mine, v, V);
+  sl.dst_row = start + before;
+  sl.owner = o;
+  *clamped = false;
+  if (sl.dst_row + sl.n > region_cap) {
+    sl.n = sl.dst_row < region_cap ? region_cap - sl.dst_row : 0;
+    *clamped = true;
+  }
+  return sl;
+}
+
+// Scatter mode (one wave): for this rank's local expert e and source sr, the
+// region rows the source's rows landed on and where they go back to:
+// {first region row, rows, first row in the source's X, source}.  The same
+// arithmetic as the sources' side in ep_slice.
+__host__ __device__ __forceinline__ int4 ep_recv_entry(const int* cnt, const int* local_gs, const int* src_off, int W,
+                                                      int E, int EL, int rank, int region_cap, int e, int sr) {
+  const int g = rank * EL + e;
+  int start = 0;
+  for (int e2 = 0; e2 < e; ++e2) start += local_gs[e2];
+  for (int s2 = rank; s2 != sr; s2 = (s2 + 1 == W ? 0 : s2 + 1)) start += cnt[s2 * E + g];
+  int n = cnt[sr * E + g];
+  if (start + n > region_cap) n = start < region_cap ? region_cap - start : 0;
+  int4 r;
+  r.x = start;
+  r.y = n;
+  r.z = src_off[sr * E + g];
+  r.w = sr;
+  return r;
 }
 
 // Warp copy of one row of `bytes` (a multiple of 16) with 4 x 16 B in flight
@@ -296,68 +378,31 @@ __global__ void __launch_bounds__(1024) ep_counts_kernel(const __grid_constant__
   // T[v][g]: rows of expert g in wave v over all sources.
   for (int i = tid; i < V * E; i += blockDim.x) {
     const int v = i / E, g = i - v * E;
-    int n = 0;
-    for (int s = 0; s < W; ++s) {
-      const int c = s_cnt[s * E + g];
-      n += wave_cut(c, v + 1, V) - wave_cut(c, v, V);
-    }
-    s_T[i] = n;
+    s_T[i] = ep_wave_total(s_cnt, W, E, V, v, g);
   }
   __syncthreads();
-  // Per (wave, owner): exclusive prefix over the owner's experts = where each
-  // expert's rows start in the owner's landing region; the owner's own
-  // region sizes are its group sizes for that wave.
+  // Per (wave, owner): where each expert's rows start in the owner's landing
+  // region; the owner's own region sizes are its group sizes for that wave.
   for (int vp = tid; vp < V * W; vp += blockDim.x) {
     const int v = vp / W, p = vp - v * W;
-    int run = 0;
-    for (int e = 0; e < EL; ++e) {
-      const int i = v * E + p * EL + e;
-      int n = s_T[i];
-      if (n > a.region_cap - run) n = a.region_cap - run;
-      s_T[i] = run;
-      if (p == a.rank) a.local_gs[v * EL + e] = n;
-      run += n;
-    }
+    ep_owner_region(s_T + v * E, p, EL, a.region_cap, p == a.rank ? a.local_gs + v * EL : nullptr);
   }
   __syncthreads();
-  // This rank's slices: inside the owner's region, sources in rank order
-  // starting at the owner itself (owner o: o, o + 1, ..., o - 1 mod world),
-  // so that an owner's own rows lead each of its experts -- the up GEMM can
-  // start on them before any peer's rows have landed.
+  // This rank's slices (owner's own rows first in each expert: the up GEMM
+  // can start on them before any peer's rows have landed).
   for (int i = tid; i < V * E; i += blockDim.x) {
     const int v = i / E, g = i - v * E;
-    const int o = g / EL;
-    int before = 0;
-    for (int k = 0, s = o; s != a.rank; ++k, s = (s + 1 == W ? 0 : s + 1)) {
-      const int c = s_cnt[s * E + g];
-      before += wave_cut(c, v + 1, V) - wave_cut(c, v, V);
-    }
-    const int mine = s_cnt[a.rank * E + g];
-    EpSlice sl;
-    sl.src_row = s_off[g] + wave_cut(mine, v, V);
-    sl.n = wave_cut(mine, v + 1, V) - wave_cut(mine, v, V);
-    sl.dst_row = s_T[i] + before;
-    sl.owner = g / EL;
-    if (sl.dst_row + sl.n > a.region_cap) {
-      sl.n = max(0, a.region_cap - sl.dst_row);
-      atomicOr(a.status, kStatusRowsClamped);
-    }
+    bool clamped;
+    const EpSlice sl = ep_slice(s_cnt, s_off, s_T[i], W, E, EL, V, a.rank, a.region_cap, v, g, &clamped);
+    if (clamped) atomicOr(a.status, kStatusRowsClamped);
     a.slices[i] = sl;
     s_T[i] = sl.n;
   }
   if (a.recv) {
-    // Scatter mode (one wave): for each of this rank's experts and each
-    // source, the region rows the source's rows landed on and where they go
-    // back to.  Same arithmetic as the owners' side of the slices above.
+    // Scatter mode (one wave): the receive table of this rank's experts.
     for (int i = tid; i < EL * W; i += blockDim.x) {
       const int e = i / W, sr = i - e * W;
-      const int g = a.rank * EL + e;
-      int start = 0;
-      for (int e2 = 0; e2 < e; ++e2) start += a.local_gs[e2];
-      for (int s2 = a.rank; s2 != sr; s2 = (s2 + 1 == W ? 0 : s2 + 1)) start += s_cnt[s2 * E + g];
-      int n = s_cnt[sr * E + g];
-      if (start + n > a.region_cap) n = max(0, a.region_cap - start);
-      a.recv[i] = make_int4(start, n, s_src[sr * E + g], sr);
+      a.recv[i] = ep_recv_entry(s_cnt, a.local_gs, s_src, W, E, EL, a.rank, a.region_cap, e, sr);
     }
   }
   __syncthreads();

@@ -8,6 +8,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "../../include/moe_b200.h"
 #include "ep_exchange.cuh"
@@ -1991,6 +1992,86 @@ static void desc_small(moe_launch_desc* d, int ctas, int F, int splits) {
 }  // namespace moe
 
 extern "C" {
+
+int moe_ep_build_tables(const int32_t* counts, int32_t world, int32_t rank, int32_t num_local_experts,
+                        int32_t waves, int32_t region_cap, int32_t max_rows, int64_t M, int32_t* slices,
+                        int32_t* wave_rows, int32_t* local_gs, int32_t* recv) {
+  t_err[0] = 0;
+  const int W = world, EL = num_local_experts, V = waves;
+  if (W < 1 || W > kEpMaxWorld || rank < 0 || rank >= W || EL < 1 || (int64_t)EL * W > kEpMaxExperts || V < 1 ||
+      V > kEpMaxWaves || region_cap < 0 || max_rows < 0 || M < 0 || M > 0x7fffffff || !counts || !slices ||
+      !wave_rows || !local_gs)
+    return fail(MOE_ERR_INVALID_ARG, "moe_ep_build_tables: bad arguments");
+  const int E = W * EL;
+  int status = 0;
+  std::vector<int> cnt((size_t)W * E), own_off(E), src_off((size_t)W * E), T((size_t)V * E);
+  // This rank's sizes as the count kernel clamps them.
+  std::vector<int> gs(E);
+  int64_t total = 0;
+  for (int g = 0; g < E; ++g) {
+    int c = counts[(size_t)rank * E + g];
+    if (c < 0) {
+      status |= kStatusBadGroupSize;
+      c = 0;
+    }
+    c = (int64_t)c > M ? (int)M : c;
+    gs[g] = c;
+  }
+  for (int g = 0; g < E; ++g) {  // exclusive prefix saturating at M, sizes cut to the room left
+    own_off[g] = (int)std::min<int64_t>(total, M);
+    total = std::min<int64_t>(total + gs[g], M);
+    const int room = (int)(M - own_off[g]);
+    if (gs[g] > room) {
+      gs[g] = room;
+      status |= kStatusRowsClamped;
+    }
+  }
+  for (int s2 = 0; s2 < W; ++s2)
+    for (int g = 0; g < E; ++g) {
+      int c = s2 == rank ? gs[g] : counts[(size_t)s2 * E + g];
+      cnt[(size_t)s2 * E + g] = c < 0 ? 0 : (c > max_rows ? max_rows : c);
+    }
+  for (int s2 = 0; s2 < W; ++s2) {
+    int64_t run = 0;
+    for (int g = 0; g < E; ++g) {
+      src_off[(size_t)s2 * E + g] = (int)std::min<int64_t>(run, 0x7fffffff);
+      run += cnt[(size_t)s2 * E + g];
+    }
+  }
+  for (int v = 0; v < V; ++v)
+    for (int g = 0; g < E; ++g) T[(size_t)v * E + g] = ep_wave_total(cnt.data(), W, E, V, v, g);
+  for (int v = 0; v < V; ++v)
+    for (int p2 = 0; p2 < W; ++p2)
+      ep_owner_region(T.data() + (size_t)v * E, p2, EL, region_cap, p2 == rank ? local_gs + (size_t)v * EL : nullptr);
+  for (int v = 0; v < V; ++v) {
+    int64_t run = 0;
+    for (int g = 0; g < E; ++g) {
+      bool clamped;
+      const EpSlice sl = ep_slice(cnt.data(), own_off.data(), T[(size_t)v * E + g], W, E, EL, V, rank, region_cap,
+                                  v, g, &clamped);
+      if (clamped) status |= kStatusRowsClamped;
+      int32_t* o = slices + ((size_t)v * E + g) * 4;
+      o[0] = sl.src_row;
+      o[1] = sl.n;
+      o[2] = sl.dst_row;
+      o[3] = sl.owner;
+      wave_rows[(size_t)v * (E + 1) + g] = (int)std::min<int64_t>(run, 0x7fffffff);
+      run += sl.n;
+    }
+    wave_rows[(size_t)v * (E + 1) + E] = (int)std::min<int64_t>(run, 0x7fffffff);
+  }
+  if (recv)
+    for (int e = 0; e < EL; ++e)
+      for (int sr = 0; sr < W; ++sr) {
+        const int4 r = ep_recv_entry(cnt.data(), local_gs, src_off.data(), W, E, EL, rank, region_cap, e, sr);
+        int32_t* o = recv + ((size_t)e * W + sr) * 4;
+        o[0] = r.x;
+        o[1] = r.y;
+        o[2] = r.z;
+        o[3] = r.w;
+      }
+  return status;
+}
 
 int moe_describe_plan(int64_t M, int32_t D, int32_t F, int32_t E, int32_t dtype, int32_t sms, moe_launch_desc* out,
                       int32_t max_out) {

@@ -89,6 +89,9 @@ def lib() -> ctypes.CDLL:
     L.moe_device_status.restype = ctypes.c_int
     L.moe_describe_plan.argtypes = [i64, i32, i32, i32, i32, i32, ctypes.POINTER(LaunchDesc), i32]
     L.moe_describe_plan.restype = ctypes.c_int
+    ip = ctypes.POINTER(ctypes.c_int32)
+    L.moe_ep_build_tables.argtypes = [ip, i32, i32, i32, i32, i32, i32, i64, ip, ip, ip, ip]
+    L.moe_ep_build_tables.restype = ctypes.c_int
     L.moe_sm_clock_sample.argtypes = [vp, i32, vp]
     L.moe_sm_clock_sample.restype = ctypes.c_int
     L.moe_version.argtypes = []
