@@ -428,7 +428,9 @@ int moe_sm_clock_sample(uint64_t* out, int32_t blocks, void* stream);
  * (0 automatic, 1 one CTA per 128-row block, 2 CTA pairs per 256 rows),
  * 5 = grouped GEMMs' tile rasterisation group in 256-row blocks (1 .. 64;
  * 0 = 8), 6 = grouped GEMMs' L2 hints for the A / B tile loads (0 evict_last
- * for both, 1 evict_normal for both, 2 A evict_first, 3 B evict_first).
+ * for both, 1 evict_normal for both, 2 A evict_first, 3 B evict_first),
+ * 7 = e4m3-weight GELU experts (0 automatic: expert super-tiles when M <=
+ * 384 E, 1 row-tiled pair kernel, 2 expert super-tiles).
  * Returns 0 or MOE_ERR_INVALID_ARG.
  */
 int moe_set_tuning(int32_t key, int64_t value);

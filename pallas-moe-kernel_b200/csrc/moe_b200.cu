@@ -15,6 +15,7 @@
 #include "router.cuh"
 #include "fused_pair.cuh"
 #include "grouped_gemm.cuh"
+#include "grouped_gemm_swap.cuh"
 #include "grouped_gemm_bwd.cuh"
 
 namespace moe {
@@ -44,6 +45,16 @@ static int64_t g_tune_trace = 0;  // device address of a trace buffer (MOE_TRACE
 static int64_t g_tune_pair = 0;   // 0 auto, 1 single-CTA kernel, 2 CTA-pair kernel
 static int64_t g_tune_group_m = 0;  // grouped GEMMs: rasterisation group in 256-row blocks (0 = 8)
 static int64_t g_tune_l2 = 0;       // grouped GEMMs: L2 hint mode of the A / B loads (GemmParams::l2_mode)
+static int64_t g_tune_fp8 = 0;      // e4m3 weights: 0 automatic, 1 row-tiled pair kernel, 2 expert super-tiles
+
+// e4m3-weight GELU experts: the super-tile (swap) kernel when the experts are
+// small -- at most one super-tile (384 rows) on average -- else the row-tiled
+// pair kernel.  Host-side only: the group sizes stay on the device.
+static bool fp8_use_swap(int64_t M, int E) {
+  if (g_tune_fp8 == 1) return false;
+  if (g_tune_fp8 == 2) return true;
+  return M <= (int64_t)SwapCfg<0>::TOKENS * E;
+}
 
 // ------------------------------------------------------------------ driver entry point
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -182,7 +193,7 @@ struct DevInfo {
   int sms = 0;
   int* status = nullptr;  // device address of g_status on this device
   bool attr_set[44] = {};
-  int pairs[26] = {};  // co-resident CTA pairs per pair-kernel variant (0 = not queried)
+  int pairs[28] = {};  // co-resident CTA pairs per pair-kernel variant (0 = not queried)
 };
 static DevInfo g_dev[64];
 static std::mutex g_dev_mu;
@@ -398,6 +409,39 @@ static int launch_gemm(const GemmMaps& maps, const GemmParams& prm_in, DevInfo* 
   return 0;
 }
 
+template <int EPI>
+static int launch_swap(const GemmMaps& maps, const GemmParams& prm, DevInfo* di, cudaStream_t st, int ctas_req) {
+  using Cfg = SwapCfg<EPI>;
+  auto kern = grouped_gemm_swap_kernel<EPI>;
+  constexpr int slot = 42 + EPI;
+  constexpr int pslot = 26 + EPI;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!di->attr_set[slot]) {
+    MOE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    cfg.gridDim = dim3(2 * (di->sms / 2));
+    int clusters = 0;
+    MOE_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg));
+    if (clusters < 1) return fail(MOE_ERR_CUDA, "no CTA pair fits on this device");
+    di->pairs[pslot] = clusters;
+    di->attr_set[slot] = true;
+  }
+  int pairs = di->pairs[pslot];
+  if (ctas_req > 0 && ctas_req / 2 < pairs) pairs = ctas_req / 2 > 0 ? ctas_req / 2 : 1;
+  cfg.gridDim = dim3(2 * pairs);
+  MOE_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, maps, prm));
+  return 0;
+}
+
 // Launch options shared by the single-GPU entry points (defaults) and the
 // expert-parallel engine: `ctas` > 0 caps the persistent grid (leaving SMs to
 // concurrent exchange kernels), `skip_tail` leaves Y rows past
@@ -510,10 +554,14 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
     MOE_CUDA_TRY(cudaGetLastError());
     xa = x16;
   }
+  // Small experts with e4m3 weights: expert super-tiles (grouped_gemm_swap.cuh),
+  // unless the down GEMM must store Y rows into their source ranks.
+  const bool swap = fp8 && !opt.scatter && fp8_use_swap(M, E);
+  const uint32_t a_box_rows = swap ? SwapCfg<0>::XBOX : 128;
   // up: H = GELU(X @ W_up[e])
   GemmMaps m1;
   memset(&m1, 0, sizeof(m1));
-  if (int r = make_map_2d(&m1.a, xa, A16, 2, (uint64_t)M, D, 64, 128)) return r;
+  if (int r = make_map_2d(&m1.a, xa, A16, 2, (uint64_t)M, D, 64, a_box_rows)) return r;
   if (fp8) {
     if (int r = make_map_3d(&m1.b, w_up, U8, 1, (uint64_t)E, D, F, 128, 64)) return r;
   } else {
@@ -521,12 +569,14 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
   }
   GemmParams p1{gs, ws, (int)M, E, F, D, 8, status, w_up_scale, 0};
   if (opt.dispatch && !fp8) p1.dispatch = *opt.dispatch;  // (f32 took run_large_tf32 above)
-  if (int r = fp8 ? launch_gemm<0, true>(m1, p1, di, st, ctas) : launch_gemm<0, false>(m1, p1, di, st, ctas))
+  if (int r = swap ? launch_swap<0>(m1, p1, di, st, ctas)
+               : fp8  ? launch_gemm<0, true>(m1, p1, di, st, ctas)
+                      : launch_gemm<0, false>(m1, p1, di, st, ctas))
     return r;
   // down: Y = H @ W_down[e]
   GemmMaps m2;
   memset(&m2, 0, sizeof(m2));
-  if (int r = make_map_2d(&m2.a, ws, A16, 2, (uint64_t)M, F, 64, 128)) return r;
+  if (int r = make_map_2d(&m2.a, ws, A16, 2, (uint64_t)M, F, 64, a_box_rows)) return r;
   if (fp8) {
     if (int r = make_map_3d(&m2.b, w_down, U8, 1, (uint64_t)E, F, D, 128, 64)) return r;
   } else {
@@ -534,6 +584,7 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
   }
   GemmParams p2{gs, y, (int)M, E, D, F, 8, status, w_down_scale, opt.skip_tail ? 1 : 0};
   if (opt.scatter) p2.scatter = *opt.scatter;
+  if (swap) return launch_swap<1>(m2, p2, di, st, ctas);
   return fp8 ? launch_gemm<1, true>(m2, p2, di, st, ctas) : launch_gemm<1, false>(m2, p2, di, st, ctas);
 }
 
@@ -1286,6 +1337,10 @@ int moe_set_tuning(int32_t key, int64_t value) {
       if (value > 3) return fail(MOE_ERR_INVALID_ARG, "L2 hint mode must be 0 .. 3");
       g_tune_l2 = value;
       return 0;
+    case 7:
+      if (value > 2) return fail(MOE_ERR_INVALID_ARG, "e4m3 kernel choice must be 0, 1 or 2");
+      g_tune_fp8 = value;
+      return 0;
   }
   return fail(MOE_ERR_INVALID_ARG, "unknown tuning key %d", key);
 }
@@ -1983,6 +2038,13 @@ static void desc_gemm(moe_launch_desc* d, const char* name, int pairs, int N, in
   desc_set(d, name, 2 * pairs, C::THREADS, C::SMEM, C::TMEM_COLS, 2, 2 * C::BM, C::BN, C::BK, C::NS,
            TF32 ? MOE_MMA_TF32X3 : (BFP8 ? MOE_MMA_F16 : MOE_MMA_BF16), N, K, 1, (int)C::NACC);
 }
+// Super-tile kernel: tile_m = tokens per super-tile, tile_n = features per tile.
+template <int EPI>
+static void desc_swap(moe_launch_desc* d, const char* name, int pairs, int N, int K) {
+  using C = SwapCfg<EPI>;
+  desc_set(d, name, 2 * pairs, C::THREADS, C::SMEM, C::TMEM_COLS, 2, C::TOKENS, 2 * C::FM, C::BK, C::NS,
+           MOE_MMA_F16, N, K, 1, 2);
+}
 template <int MODE, int D, int BF, bool XR>
 static void desc_small(moe_launch_desc* d, int ctas, int F, int splits) {
   using C = FusedCfg<MODE, D, BF, XR>;
@@ -2102,8 +2164,13 @@ int moe_describe_plan(int64_t M, int32_t D, int32_t F, int32_t E, int32_t dtype,
     } else if (dtype == MOE_DTYPE_FP8_E4M3_BLK128) {
       const int xb = (int)std::min<int64_t>(((int64_t)M * D / 8 + 255) / 256, (int64_t)sms * 8);
       desc_set(&d[n++], "bf16_to_f16_kernel", xb, 256, 0, 0, 1, 0, 0, 0, 0, MOE_MMA_NONE, 0, 0, 1, 0);
-      desc_gemm<0, true, false>(&d[n++], "grouped_gemm_pair_kernel (up)", pairs, F, D);
-      desc_gemm<1, true, false>(&d[n++], "grouped_gemm_pair_kernel (down)", pairs, D, F);
+      if (fp8_use_swap(M, E)) {
+        desc_swap<0>(&d[n++], "grouped_gemm_swap_kernel (up)", pairs, F, D);
+        desc_swap<1>(&d[n++], "grouped_gemm_swap_kernel (down)", pairs, D, F);
+      } else {
+        desc_gemm<0, true, false>(&d[n++], "grouped_gemm_pair_kernel (up)", pairs, F, D);
+        desc_gemm<1, true, false>(&d[n++], "grouped_gemm_pair_kernel (down)", pairs, D, F);
+      }
     } else {
       desc_gemm<0, false, false>(&d[n++], "grouped_gemm_pair_kernel (up)", pairs, F, D);
       desc_gemm<1, false, false>(&d[n++], "grouped_gemm_pair_kernel (down)", pairs, D, F);
