@@ -20,7 +20,9 @@ Two layers.
    threads, shared memory, TMEM columns, cluster, tile shape, pipeline
    stages, tcgen05 MMA kind, F-splits), and per launch the work units the
    group sizes produce (256-row x 256-column pair tiles of the grouped GEMMs,
-   128-row blocks x F-splits of the fused small-D kernel), padded rows, waves
+   expert super-tiles of up to 384 tokens x 256 features for small experts
+   with e4m3 weights, 128-row blocks x F-splits of the fused small-D kernel),
+   padded rows, waves
    over the persistent grid, tensor work issued (padding and the three
    products of 3xTF32 included, in bf16-equivalent FLOPs), compulsory DRAM
    bytes (every operand once, H's round trip on the two-GEMM path, the tf32
@@ -282,12 +284,25 @@ def _launch_model(L: dict, M: int, D: int, F: int, E: int, g: list[int], dtype: 
     out = dict(L)
     routed = sum(g)
     active = sum(1 for v in g if v > 0)
-    if name.startswith("grouped_gemm_pair_kernel"):
+    if name.startswith("grouped_gemm_pair_kernel") or name.startswith("grouped_gemm_swap_kernel"):
         N, K = L["gemm_n"], L["gemm_k"]
-        rows_blocks = [-(-v // L["tile_m"]) for v in g]
         ncol = -(-N // L["tile_n"])
-        tiles = sum(rows_blocks) * ncol
-        rows_pad = sum(rows_blocks) * L["tile_m"]
+        if name.startswith("grouped_gemm_swap_kernel"):
+            # expert super-tiles of tile_m tokens: chunks of <= 256 and <= 128
+            # tokens, each an MMA with N = its tokens rounded up to 32
+            st = [-(-v // L["tile_m"]) for v in g]
+            tiles = sum(st) * ncol
+            rows_pad = 0
+            for v in g:
+                for k in range(-(-v // L["tile_m"])):
+                    rem = v - k * L["tile_m"]
+                    n0 = min(rem, 256)
+                    n1 = min(max(rem - 256, 0), 128)
+                    rows_pad += -(-n0 // 32) * 32 + -(-n1 // 32) * 32
+        else:
+            rows_blocks = [-(-v // L["tile_m"]) for v in g]
+            tiles = sum(rows_blocks) * ncol
+            rows_pad = sum(rows_blocks) * L["tile_m"]
         workers = L["grid"] // L["cluster"]
         up = name.endswith("(up)")
         k_pad = -(-K // L["stage_k"]) * L["stage_k"]
