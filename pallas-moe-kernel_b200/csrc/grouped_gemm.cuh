@@ -115,18 +115,27 @@ __device__ __forceinline__ void store_y_rows(uint32_t taddr, float4* stage, uint
 // the pre-activation (bf16) to out2, 4: SwiGLU plus the raw gate/up columns
 // (bf16) to out2; BFP8: e4m3 B dequantised in smem, f16 operands; TF32: f32
 // operands as tf32 hi/lo planes (3xTF32), EPI 0 or 1 only.
-template <int EPI, bool BFP8, bool TF32 = false>
+//
+// WIDE = 2 (bf16 Y only): a tile is 256 rows x 512 columns, two 256-column
+// MMAs per K step sharing the A tile, one 512-column accumulator (no
+// double-buffering).  Half as many tiles run the whole reduction, so half as
+// many waves stream distinct operands through L2 -- for a long reduction
+// (the down GEMM's K = F) most DRAM re-reads of H and W_down go away -- and
+// each A byte staged feeds twice the MMA work.
+template <int EPI, bool BFP8, bool TF32 = false, int WIDE = 1>
 struct GemmCfg {
   static_assert(!(TF32 && (BFP8 || EPI > 1)), "3xTF32 runs the GELU and Y epilogues on f32 planes");
+  static_assert(WIDE == 1 || (WIDE == 2 && EPI == 1 && !BFP8 && !TF32), "wide tiles: bf16 operands, f32 Y");
   static constexpr int BM = 128;   // rows per CTA (256 per pair)
-  static constexpr int BN = 256;   // output columns per tile (128 per CTA of B)
+  static constexpr int BN = 256;   // output columns per MMA (128 per CTA of B)
+  static constexpr int TILE_N = BN * WIDE;  // output columns per tile
   static constexpr int BK = TF32 ? 32 : 64;  // elements of one 128-byte swizzle row
   static constexpr int A_BYTES = BM * 128;             // 16 KB (one plane)
   static constexpr int B_BYTES = (BN / 2) * 128;       // 16 KB (one plane of this CTA's B half)
   static constexpr int B8_BYTES = BFP8 ? (BN / 2) * BK : 0;  // 8 KB raw e4m3 tile
   static constexpr int PLANES = TF32 ? 2 : 1;          // hi and lo planes of A and of B
-  static constexpr int STAGE = PLANES * (A_BYTES + B_BYTES);  // operand stage
-  static constexpr int NS = TF32 ? 3 : (BFP8 ? 4 : 6); // operand stages
+  static constexpr int STAGE = PLANES * (A_BYTES + WIDE * B_BYTES);  // operand stage
+  static constexpr int NS = TF32 ? 3 : ((BFP8 || WIDE == 2) ? 4 : 6); // operand stages
   static constexpr int NR = BFP8 ? 10 : 0;             // raw e4m3 stages (HBM stream runs ahead)
   static constexpr int EPI_WARPS = 4;
   static constexpr int CVT_WARPS = BFP8 ? 8 : 0;  // two per SM sub-partition
@@ -145,7 +154,7 @@ struct GemmCfg {
   // with f32 rounding -- so that the large one takes K/8 accumulate steps
   // rather than 3K/8 (each accumulate step into TMEM truncates, an error that
   // grows with the number of steps), at the cost of that overlap.
-  static constexpr uint32_t NACC = TF32 ? 1 : 2;
+  static constexpr uint32_t NACC = (TF32 || WIDE == 2) ? 1 : 2;
   // e4m3 weights run as f16 operands (f16 X, f16 H, f16 dequantised B).
   // 16-bit B is read MN-major (the weights' own layout); tf32 B is K-major.
   static constexpr uint32_t IDESC = TF32 ? make_idesc(kFmtTF32, 256, BN, 0, 0)
@@ -242,10 +251,10 @@ struct TileCursor {
   }
 };
 
-template <int EPI, bool BFP8, bool TF32 = false>
-__global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32>::LAUNCH_BOUND, 1)
+template <int EPI, bool BFP8, bool TF32 = false, int WIDE = 1>
+__global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32, WIDE>::LAUNCH_BOUND, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ GemmMaps maps, const GemmParams p) {
-  using C = GemmCfg<EPI, BFP8, TF32>;
+  using C = GemmCfg<EPI, BFP8, TF32, WIDE>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -269,7 +278,7 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32>::LAUNCH_BOUND, 1)
   const int pair = (int)(blockIdx.x >> 1);
   const int npairs = (int)(gridDim.x >> 1);
   constexpr uint16_t kBoth = 0x3;
-  const int nt = (p.N + C::BN - 1) / C::BN;
+  const int nt = (p.N + C::TILE_N - 1) / C::TILE_N;
   const int nk = (p.K + C::BK - 1) / C::BK;
 
   if (threadIdx.x == 0) {
@@ -323,7 +332,7 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32>::LAUNCH_BOUND, 1)
         int mb, nb;
         cur.coords(t, nt, p.group_m, mb, nb);
         const int row0 = cur.row_begin + mb * 256 + (int)rank * C::BM;
-        const int n0 = nb * C::BN + (int)rank * (C::BN / 2);
+        const int n0 = nb * C::TILE_N + (int)rank * (C::BN / 2);
         bool ok = true;
         if (C::PUSH_WARPS > 0 && p.dispatch.on) {
           // Wait for every peer whose rows of this expert meet this CTA's 128
@@ -384,8 +393,12 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32>::LAUNCH_BOUND, 1)
             const uint32_t bar = full_l0 + stage * 8;
             if (rank == 0) mbar_arrive_expect_tx(full + stage, C::TX);
             tma_load_2d_pair(st, &maps.a, bar, kb * C::BK, row0, pol_a);
-            tma_load_3d_pair(st + C::A_BYTES, &maps.b, bar, n0, kb * C::BK, cur.e, pol_b);
-            tma_load_3d_pair(st + C::A_BYTES + 64 * 128, &maps.b, bar, n0 + 64, kb * C::BK, cur.e, pol_b);
+#pragma unroll
+            for (int h = 0; h < WIDE; ++h) {  // this CTA's 128 columns of each 256-column MMA
+              uint8_t* bd = st + C::A_BYTES + h * C::B_BYTES;
+              tma_load_3d_pair(bd, &maps.b, bar, n0 + h * C::BN, kb * C::BK, cur.e, pol_b);
+              tma_load_3d_pair(bd + 64 * 128, &maps.b, bar, n0 + h * C::BN + 64, kb * C::BK, cur.e, pol_b);
+            }
           }
           if (++stage == C::NS) {
             stage = 0;
@@ -436,9 +449,11 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32>::LAUNCH_BOUND, 1)
             const uint64_t b_desc = make_sdesc(st + C::A_BYTES, 64 * 128, 1024);
 #pragma unroll
             for (int ki = 0; ki < C::BK / 16; ++ki)
-              umma_ss_pair<Kind::F16>(d_tmem, a_desc + (uint64_t)((ki * 32) >> 4),
-                                      b_desc + (uint64_t)((ki * 16 * 128) >> 4), C::IDESC,
-                                      (kb > 0 || ki > 0) ? 1u : 0u);
+#pragma unroll
+              for (int h = 0; h < WIDE; ++h)
+                umma_ss_pair<Kind::F16>(d_tmem + h * C::BN, a_desc + (uint64_t)((ki * 32) >> 4),
+                                        b_desc + (uint64_t)((h * C::B_BYTES + ki * 16 * 128) >> 4), C::IDESC,
+                                        (kb > 0 || ki > 0) ? 1u : 0u);
           }
           umma_commit_pair(empty + stage, kBoth);
           if (++stage == C::NS) {
@@ -631,7 +646,7 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32>::LAUNCH_BOUND, 1)
       // FP8 tiles were accumulated with weights scaled by 2^k.
       const float mul = BFP8 ? exp2i(-fp8_tile_shift(p.b_scale, p.K, p.N, cur.e, nb, lane)) : 1.f;
       // Columns of this tile inside N (the last column tile may be partial).
-      const int ncol = p.N - nb * C::BN < C::BN ? p.N - nb * C::BN : C::BN;
+      const int ncol = p.N - nb * C::TILE_N < C::TILE_N ? p.N - nb * C::TILE_N : C::TILE_N;
       if constexpr (TF32 && EPI == 0) {
         // 32 columns per step: GELU (f32 accuracy), then the tf32 split
         // g = hi + lo (tf32_hi_bits); each plane goes out through the 32-row
@@ -879,7 +894,7 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32>::LAUNCH_BOUND, 1)
         float4* wst4 = reinterpret_cast<float4*>(wst);
 #pragma unroll 1
         for (int c0 = 0; c0 < ncol; c0 += 32)
-          store_y_rows(acc + c0, wst4, row_ptr, nb * C::BN + c0, lane, mul, p.N);
+          store_y_rows(acc + c0, wst4, row_ptr, nb * C::TILE_N + c0, lane, mul, p.N);
       } else if (BFP8) {
         // f32 Y rows scaled back by 2^-k, through the same staging as below.
         float* Y = reinterpret_cast<float*>(p.out);
@@ -894,7 +909,7 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32>::LAUNCH_BOUND, 1)
         float4* wst4 = reinterpret_cast<float4*>(wst);
 #pragma unroll 1
         for (int c0 = 0; c0 < ncol; c0 += 32)
-          store_y_block<0>(acc + c0, wst4, Y + (size_t)nb * C::BN, wrow0, row_end, c0, lane, false, p.N, ncol);
+          store_y_block<0>(acc + c0, wst4, Y + (size_t)nb * C::TILE_N, wrow0, row_end, c0, lane, false, p.N, ncol);
       }
       tc_fence_before();
       __syncwarp();

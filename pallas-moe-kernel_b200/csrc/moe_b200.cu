@@ -46,6 +46,10 @@ static int64_t g_tune_pair = 0;   // 0 auto, 1 single-CTA kernel, 2 CTA-pair ker
 static int64_t g_tune_group_m = 0;  // grouped GEMMs: rasterisation group in 256-row blocks (0 = 8)
 static int64_t g_tune_l2 = 0;       // grouped GEMMs: L2 hint mode of the A / B loads (GemmParams::l2_mode)
 static int64_t g_tune_fp8 = 0;      // e4m3 weights: 0 automatic, 1 row-tiled pair kernel, 2 expert super-tiles
+static int64_t g_tune_wide = 0;     // bf16 down GEMM: 0 automatic, 1 256-column tiles, 2 512-column tiles
+
+// bf16 down GEMM (f32 Y): 512-column tiles unless set otherwise.
+static bool down_wide() { return g_tune_wide != 1; }
 
 // e4m3-weight GELU experts: the super-tile (swap) kernel when the experts are
 // small -- at most one super-tile (384 rows) on average -- else the row-tiled
@@ -192,8 +196,8 @@ struct DevInfo {
   CUcontext ctx = nullptr;  // context the entries below belong to
   int sms = 0;
   int* status = nullptr;  // device address of g_status on this device
-  bool attr_set[44] = {};
-  int pairs[28] = {};  // co-resident CTA pairs per pair-kernel variant (0 = not queried)
+  bool attr_set[46] = {};
+  int pairs[30] = {};  // co-resident CTA pairs per pair-kernel variant (0 = not queried)
 };
 static DevInfo g_dev[64];
 static std::mutex g_dev_mu;
@@ -372,16 +376,16 @@ __global__ void bf16_to_f16_kernel(const uint4* __restrict__ x, uint4* __restric
   }
 }
 
-template <int EPI, bool BFP8, bool TF32 = false>
+template <int EPI, bool BFP8, bool TF32 = false, int WIDE = 1>
 static int launch_gemm(const GemmMaps& maps, const GemmParams& prm_in, DevInfo* di, cudaStream_t st, int ctas_req) {
   GemmParams prm = prm_in;
   if (g_tune_group_m > 0) prm.group_m = (int)g_tune_group_m;
   prm.l2_mode = (int)g_tune_l2;
-  using Cfg = GemmCfg<EPI, BFP8, TF32>;
-  auto kern = grouped_gemm_pair_kernel<EPI, BFP8, TF32>;
-  constexpr int slot = TF32 ? 40 + EPI : 24 + 2 * EPI + (BFP8 ? 1 : 0);
-  constexpr int pslot = TF32 ? 24 + EPI : 8 + 2 * EPI + (BFP8 ? 1 : 0);
-  static_assert(slot < 44 && pslot < 26 && (TF32 ? EPI < 2 : slot < 36 && pslot < 18), "attribute slot");
+  using Cfg = GemmCfg<EPI, BFP8, TF32, WIDE>;
+  auto kern = grouped_gemm_pair_kernel<EPI, BFP8, TF32, WIDE>;
+  constexpr int slot = WIDE == 2 ? 44 : (TF32 ? 40 + EPI : 24 + 2 * EPI + (BFP8 ? 1 : 0));
+  constexpr int pslot = WIDE == 2 ? 28 : (TF32 ? 24 + EPI : 8 + 2 * EPI + (BFP8 ? 1 : 0));
+  static_assert(slot < 46 && pslot < 30 && (TF32 ? EPI < 2 : true), "attribute slot");
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -585,7 +589,9 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
   GemmParams p2{gs, y, (int)M, E, D, F, 8, status, w_down_scale, opt.skip_tail ? 1 : 0};
   if (opt.scatter) p2.scatter = *opt.scatter;
   if (swap) return launch_swap<1>(m2, p2, di, st, ctas);
-  return fp8 ? launch_gemm<1, true>(m2, p2, di, st, ctas) : launch_gemm<1, false>(m2, p2, di, st, ctas);
+  if (fp8) return launch_gemm<1, true>(m2, p2, di, st, ctas);
+  return down_wide() ? launch_gemm<1, false, false, 2>(m2, p2, di, st, ctas)
+                     : launch_gemm<1, false, false>(m2, p2, di, st, ctas);
 }
 
 // ------------------------------------------------------------------ training: forward with saved pre-activation, backward
@@ -1341,6 +1347,10 @@ int moe_set_tuning(int32_t key, int64_t value) {
       if (value > 2) return fail(MOE_ERR_INVALID_ARG, "e4m3 kernel choice must be 0, 1 or 2");
       g_tune_fp8 = value;
       return 0;
+    case 8:
+      if (value > 2) return fail(MOE_ERR_INVALID_ARG, "down-GEMM tile width choice must be 0, 1 or 2");
+      g_tune_wide = value;
+      return 0;
   }
   return fail(MOE_ERR_INVALID_ARG, "unknown tuning key %d", key);
 }
@@ -2032,10 +2042,10 @@ static void desc_set(moe_launch_desc* d, const char* name, int grid, int threads
   d->f_splits = splits;
   d->accumulators = accs;
 }
-template <int EPI, bool BFP8, bool TF32>
+template <int EPI, bool BFP8, bool TF32, int WIDE = 1>
 static void desc_gemm(moe_launch_desc* d, const char* name, int pairs, int N, int K) {
-  using C = GemmCfg<EPI, BFP8, TF32>;
-  desc_set(d, name, 2 * pairs, C::THREADS, C::SMEM, C::TMEM_COLS, 2, 2 * C::BM, C::BN, C::BK, C::NS,
+  using C = GemmCfg<EPI, BFP8, TF32, WIDE>;
+  desc_set(d, name, 2 * pairs, C::THREADS, C::SMEM, C::TMEM_COLS, 2, 2 * C::BM, C::TILE_N, C::BK, C::NS,
            TF32 ? MOE_MMA_TF32X3 : (BFP8 ? MOE_MMA_F16 : MOE_MMA_BF16), N, K, 1, (int)C::NACC);
 }
 // Super-tile kernel: tile_m = tokens per super-tile, tile_n = features per tile.
@@ -2173,7 +2183,8 @@ int moe_describe_plan(int64_t M, int32_t D, int32_t F, int32_t E, int32_t dtype,
       }
     } else {
       desc_gemm<0, false, false>(&d[n++], "grouped_gemm_pair_kernel (up)", pairs, F, D);
-      desc_gemm<1, false, false>(&d[n++], "grouped_gemm_pair_kernel (down)", pairs, D, F);
+      if (down_wide()) desc_gemm<1, false, false, 2>(&d[n++], "grouped_gemm_pair_kernel (down)", pairs, D, F);
+      else desc_gemm<1, false, false>(&d[n++], "grouped_gemm_pair_kernel (down)", pairs, D, F);
     }
   } else {
     const SmallPlan plan = small_plan(M, D, F, E, dtype);
