@@ -74,8 +74,13 @@ def test_b200_layer_by_hand():
     gs = [255, 257, 1, 511]                   # pair tiles of 256 rows: 1 + 2 + 1 + 2 = 6 row blocks
     m = analysis.b200_model(1024, 512, 512, 4, gs, "bf16")
     up, down = m["launches"]
-    assert up["units"] == 6 * 2                # 256-column tiles: 2 per row block
-    assert down["units"] == 6 * 1 and down["tile_n"] == 512   # the down GEMM's 512-column tiles
+    assert up["units"] == 6 * 2 and down["units"] == 6 * 2   # 256-column tiles: 2 per row block
+    _lib.set_tuning(8, 2)                     # the down GEMM's optional 512-column tiles
+    try:
+        wide = analysis.b200_model(1024, 512, 512, 4, gs, "bf16")["launches"][1]
+    finally:
+        _lib.set_tuning(8, 0)
+    assert wide["units"] == 6 * 1 and wide["tile_n"] == 512 and wide["accumulators"] == 1
     assert up["rows_processed"] == 6 * 256 and up["padded_rows"] == 6 * 256 - 1024
     assert up["issued_f16_equiv_flops"] == 2 * 1536 * 512 * 512
     assert up["useful_flops"] == 2 * 1024 * 512 * 512
