@@ -406,12 +406,37 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
     torch.cuda.synchronize(device)
     e2e_ms = e0.elapsed_time(e1)
 
-    vals = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=device)
+    # The host link alone: the same copies (X in, Y out, two slots, the copy
+    # streams of the e2e loop) with no compute, on every rank at once -- the
+    # ceiling the e2e figure runs into when the copies outlast the compute.
+    def copies_only(n):
+        for i in range(n):
+            b = i & 1
+            with torch.cuda.stream(s_in):
+                xd[b].copy_(xh, non_blocking=True)
+            with torch.cuda.stream(s_out):
+                yh[b].copy_(yd[b], non_blocking=True)
+    copies_only(2)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record(stream)
+    s_in.wait_event(c0)
+    s_out.wait_event(c0)
+    copies_only(args.steps)
+    stream.wait_stream(s_in)
+    stream.wait_stream(s_out)
+    c1.record(stream)
+    torch.cuda.synchronize(device)
+    copy_ms = c0.elapsed_time(c1)
+
+    vals = torch.tensor([total_ms, e2e_ms, copy_ms], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
         if hasattr(layer, "close"):
             layer.close()
-    total_ms, e2e_ms = vals.tolist()
+    total_ms, e2e_ms, copy_ms = vals.tolist()
     if rank != 0:
         return None
 
@@ -489,6 +514,10 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
                    "pipelining": "copy-in, compute and copy-out of consecutive steps on three streams, "
                                  "two buffer slots",
                    "host_copy_gbs_per_gpu": (h2d + cfg.M * cfg.D * 4) * args.steps / (e2e_ms / 1e3) / 1e9,
+                   "host_copy_ceiling_gbs_per_gpu": (cfg.M * cfg.D * x.element_size() + cfg.M * cfg.D * 4)
+                   * args.steps / (copy_ms / 1e3) / 1e9,
+                   "host_copy_ceiling": "the same H2D + D2H copies with no compute, every rank at once, "
+                                        "max over ranks",
                    "host_buffers": numa}
     return line
 
