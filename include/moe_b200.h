@@ -56,15 +56,22 @@ enum {
  * `group_sizes_to_offsets` op (src/kernel.py:126-132) plus the
  * `pl.pallas_call` of `fused_mlp_one_expert` (src/kernel.py:9-82); the result
  * equals `ref_ragged_mlp` (src/kernel.py:152-175) within the precision of
- * `dtype`.  BM, BF and max_group_size are not arguments: the kernel walks the
- * real (expert, 128-row) blocks derived on the device from `group_sizes`.
+ * `dtype`.  BM, BF and max_group_size are not arguments: the kernels walk the
+ * real work units derived on the device from `group_sizes`.
+ *
+ * Kernels: D in {64, 128, 256} (f32: F % 64 == 0; bf16: F % 128 == 0) runs the
+ * fused kernel with the hidden block on chip; every other shape runs two
+ * grouped GEMMs with H through the workspace (f32 in 3xTF32; e4m3 weights
+ * with small experts as expert super-tiles).  Any D and F whose rows start on
+ * 16-byte boundaries are accepted: multiples of 4 (f32), 8 (bf16) or 16
+ * (e4m3 weights); other shapes return MOE_ERR_UNSUPPORTED_SHAPE.
  *
  *   x            (M, D)   f32 (MOE_DTYPE_F32) or bf16 (other dtypes)
  *   w_up         (E, D, F) f32 / bf16 / e4m3 bytes
  *   w_down       (E, F, D) f32 / bf16 / e4m3 bytes
  *   group_sizes  (E,) int32, device memory; negative entries count as 0
- *   w_up_scale   (E, D/128, F/128) f32 block scales (FP8 only, else NULL)
- *   w_down_scale (E, F/128, D/128) f32 block scales (FP8 only, else NULL)
+ *   w_up_scale   (E, ceil(D/128), ceil(F/128)) f32 block scales (FP8 only, else NULL)
+ *   w_down_scale (E, ceil(F/128), ceil(D/128)) f32 block scales (FP8 only, else NULL)
  *   y            (M, D) f32 output
  *   workspace    device scratch of at least moe_fused_mlp_workspace_size()
  *                bytes, 256-byte aligned (may be NULL when that size is 0)
@@ -202,7 +209,8 @@ int moe_fused_mlp_noalloc(const float* x, const float* w_up, const float* w_down
  * every rank Y equals moe_fused_mlp over all experts.  Transfers are our own
  * kernels over peer memory (CUDA IPC mappings of one buffer per rank): rows
  * are stored straight into the owner's landing buffer.  For D > 256 (the
- * two-GEMM experts) the combine is fused into the down GEMM: its epilogue
+ * two-GEMM experts: bf16 or e4m3 weights with D and F multiples of 256; other
+ * two-GEMM shapes are refused) the combine is fused into the down GEMM: its epilogue
  * stores every Y row straight into the row's source rank (`waves` is then
  * 1).  For D <= 256 results are loaded back from the owner's outbox in
  * `waves` slices per step, so that the exchange of one slice overlaps the
