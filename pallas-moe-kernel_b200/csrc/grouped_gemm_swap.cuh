@@ -11,18 +11,16 @@
 // with the decoded weights as the MMA's A operand (M = 256 features over the
 // CTA pair, MN-major: the weights' own layout, the same f16 tile the
 // converters already produce) and the expert's tokens as B (K-major rows of X
-// or H), N = the token count rounded up to 32.  A super-tile holds up to 288
-// tokens in two chunks (N <= 224 and N <= 64): each decoded weight stage
+// or H), N = the token count rounded up to 32.  A super-tile holds up to 384
+// tokens in two chunks (N <= 256 and N <= 128): each decoded weight stage
 // feeds both chunks' MMAs.  Padding drops to < 32 rows per chunk and the
-// weights are decoded once per 288 tokens (256 +- 32: one super-tile per
-// expert of a top-8-of-256 router).
+// weights are decoded once per 384 tokens.
 //
-// TMEM: chunk 0 alternates between columns [0, 224) and [224, 448), chunk 1
-// always takes [448, 512), so every tile's epilogue overlaps the next tile's
-// MMAs (two-chunk tiles only wait for the previous two-chunk tile's small
-// chunk).  The accumulator's lanes are features and its columns tokens, so
-// the epilogue writes every token row with the warp's 32 consecutive features
-// (coalesced).
+// TMEM: two 256-column accumulator buffers, handed out in order -- a
+// one-chunk super-tile takes the next buffer (so consecutive tiles
+// double-buffer), a two-chunk one takes the next two.  The accumulator's lanes
+// are features and its columns tokens, so the epilogue writes every token row
+// with the warp's 32 consecutive features (coalesced).
 //
 // Warp roles as in grouped_gemm_pair_kernel with e4m3 weights: warp 0 TMA
 // producer of X rows (both CTAs), warp 1 TMEM owner + MMA issuer (leader),
@@ -38,23 +36,21 @@ struct SwapCfg {
   static_assert(EPI == 0 || EPI == 1, "GELU -> H or f32 Y");
   static constexpr int FM = 128;                     // features per CTA (MMA M = 256 per pair)
   static constexpr int BK = 64;                      // K per stage (one 128-byte f16 row)
-  static constexpr int N0 = 224, N1 = 64;            // tokens of chunk 0 / chunk 1 (MMA N)
+  static constexpr int N0 = 256, N1 = 128;           // tokens of chunk 0 / chunk 1 (MMA N)
   static constexpr int TOKENS = N0 + N1;             // tokens per super-tile
-  static constexpr int XBOX = 32;                    // token rows per TMA box (4 KB)
   static constexpr int A_BYTES = FM * BK * 2;        // 16 KB decoded weights (MN-major)
-  static constexpr int B0_BYTES = 4 * XBOX * 128;    // 16 KB: up to 4 boxes (N0 / 2 = 112 rows) per CTA
-  static constexpr int B1_BYTES = 1 * XBOX * 128;    // 4 KB: one box (N1 / 2 = 32 rows) per CTA
-  static constexpr int STAGE = A_BYTES + B0_BYTES + B1_BYTES;  // 36 KB
+  static constexpr int B0_BYTES = (N0 / 2) * BK * 2; // 16 KB: 128 token rows per CTA (K-major)
+  static constexpr int B1_BYTES = (N1 / 2) * BK * 2; // 8 KB: 64 token rows per CTA
+  static constexpr int STAGE = A_BYTES + B0_BYTES + B1_BYTES;  // 40 KB
   static constexpr int NS = 4;
   static constexpr int B8_BYTES = FM * BK;           // 8 KB raw e4m3 tile
-  static constexpr int NR = 10;
-  static constexpr uint32_t COL_R1 = N0, COL_R2 = 2 * N0;  // TMEM columns of regions 1 and 2 (region 0 at 0)
+  static constexpr int NR = 8;
+  static constexpr int XBOX = 32;                    // token rows per TMA box (4 KB)
   static constexpr int EPI_WARPS = 4;
   static constexpr int CVT_WARPS = 8;
   static constexpr int BAR_BYTES = 512;
   static constexpr int SMEM = 1024 + NS * STAGE + NR * B8_BYTES + BAR_BYTES;
-  static constexpr int TMEM_COLS = 512;              // regions of 224 + 224 + 64 columns
-  static_assert(2 * N0 + N1 <= TMEM_COLS && N0 % 32 == 0 && N1 % 32 == 0, "TMEM regions");
+  static constexpr int TMEM_COLS = 512;              // two 256-column accumulator buffers
   static constexpr int RAW_WARP = 2 + EPI_WARPS + CVT_WARPS;
   static constexpr int THREADS = 64 + (EPI_WARPS + CVT_WARPS) * 32 + 32;
   static_assert(SMEM <= kMaxSmemPerBlock, "shared memory budget");
@@ -125,9 +121,9 @@ __global__ void __launch_bounds__(SwapCfg<EPI>::THREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(rawring + C::NR * C::B8_BYTES);
   uint64_t* full = bars;                  // [NS] leader: producer + converters of both CTAs
   uint64_t* empty = bars + C::NS;         // [NS] both (multicast commit)
-  uint64_t* acc_full = bars + 2 * C::NS;  // [3] both (multicast commit): TMEM regions 0, 1, 2
-  uint64_t* acc_empty = acc_full + 3;     // [3] leader (epilogue warps of both CTAs)
-  uint64_t* raw_full = acc_full + 6;      // [NR] local
+  uint64_t* acc_full = bars + 2 * C::NS;  // [2] both (multicast commit)
+  uint64_t* acc_empty = acc_full + 2;     // [2] leader (epilogue warps of both CTAs)
+  uint64_t* raw_full = acc_full + 4;      // [NR] local
   uint64_t* raw_empty = raw_full + C::NR; // [NR] local
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(raw_empty + C::NR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -150,7 +146,7 @@ __global__ void __launch_bounds__(SwapCfg<EPI>::THREADS, 1)
       mbar_init(raw_full + i, 1);
       mbar_init(raw_empty + i, C::CVT_WARPS / 2);
     }
-    for (int i = 0; i < 3; ++i) {
+    for (int i = 0; i < 2; ++i) {
       mbar_init(acc_full + i, 1);
       mbar_init(acc_empty + i, 2 * C::EPI_WARPS);
     }
@@ -218,16 +214,16 @@ __global__ void __launch_bounds__(SwapCfg<EPI>::THREADS, 1)
       SwapCursor cur;
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t u = 0;                        // tiles so far: chunk 0 takes region u & 1
-      uint32_t use0 = 0, use1 = 0, use2 = 0;  // uses of TMEM regions 0 / 1 / 2 so far
+      uint32_t u = 0;            // accumulator buffers handed out so far
+      uint32_t use0 = 0, use1 = 0;  // uses of buffer 0 / 1 so far
       for (int t = pair;; t += npairs) {
         if (!cur.seek(t, p.group_sizes, p.E, p.M, nfb, C::TOKENS)) break;
         const SwapTile s = swap_tile<C>(cur, t, nfb);
-        const uint32_t b0 = u & 1u;  // TMEM region of chunk 0 (chunk 1: region 2)
+        const uint32_t b0 = u & 1u, b1 = b0 ^ 1u;  // buffers of chunk 0 / chunk 1
         bool ok = mbar_wait_warp(acc_empty + b0, ((b0 ? use1 : use0) & 1u) ^ 1u, abort_flag, p.status);
-        if (ok && s.chunks == 2) ok = mbar_wait_warp(acc_empty + 2, (use2 & 1u) ^ 1u, abort_flag, p.status);
+        if (ok && s.chunks == 2)
+          ok = mbar_wait_warp(acc_empty + b1, ((b1 ? use1 : use0) & 1u) ^ 1u, abort_flag, p.status);
         if (!ok) break;
-        const uint32_t d0 = tmem_base + (b0 ? C::COL_R1 : 0u), d1 = tmem_base + C::COL_R2;
         tc_fence_after();
         const uint32_t idesc0 = make_idesc(kFmtF16, 256, (uint32_t)s.nr[0], 1, 0);
         const uint32_t idesc1 = make_idesc(kFmtF16, 256, (uint32_t)(s.nr[1] ? s.nr[1] : 32), 1, 0);
@@ -245,8 +241,9 @@ __global__ void __launch_bounds__(SwapCfg<EPI>::THREADS, 1)
           for (int ki = 0; ki < C::BK / 16; ++ki) {
             const uint64_t ao = (uint64_t)((ki * 16 * 128) >> 4), bo = (uint64_t)((ki * 32) >> 4);
             const uint32_t acc = (kb > 0 || ki > 0) ? 1u : 0u;
-            umma_ss_pair<Kind::F16>(d0, a_desc + ao, b0_desc + bo, idesc0, acc);
-            if (s.chunks == 2) umma_ss_pair<Kind::F16>(d1, a_desc + ao, b1_desc + bo, idesc1, acc);
+            umma_ss_pair<Kind::F16>(tmem_base + b0 * 256u, a_desc + ao, b0_desc + bo, idesc0, acc);
+            if (s.chunks == 2)
+              umma_ss_pair<Kind::F16>(tmem_base + b1 * 256u, a_desc + ao, b1_desc + bo, idesc1, acc);
           }
           umma_commit_pair(empty + stage, kBoth);
           if (++stage == C::NS) {
@@ -258,10 +255,10 @@ __global__ void __launch_bounds__(SwapCfg<EPI>::THREADS, 1)
         umma_commit_pair(acc_full + b0, kBoth);
         (b0 ? use1 : use0) += 1;
         if (s.chunks == 2) {
-          umma_commit_pair(acc_full + 2, kBoth);
-          ++use2;
+          umma_commit_pair(acc_full + b1, kBoth);
+          (b1 ? use1 : use0) += 1;
         }
-        ++u;
+        u += (uint32_t)s.chunks;
       }
     }
   } else if (warp == (uint32_t)C::RAW_WARP) {
@@ -372,7 +369,7 @@ __global__ void __launch_bounds__(SwapCfg<EPI>::THREADS, 1)
     }
     SwapCursor cur;
     uint32_t u = 0;
-    uint32_t use0 = 0, use1 = 0, use2 = 0;
+    uint32_t use0 = 0, use1 = 0;
     for (int t = pair;; t += npairs) {
       if (!cur.seek(t, p.group_sizes, p.E, p.M, nfb, C::TOKENS)) break;
       const SwapTile s = swap_tile<C>(cur, t, nfb);
@@ -381,16 +378,15 @@ __global__ void __launch_bounds__(SwapCfg<EPI>::THREADS, 1)
       const float mul = exp2i(-fp8_tile_shift(p.b_scale, p.K, p.N, cur.e, s.fb, lane));
       bool ok = true;
       for (int c = 0; c < s.chunks; ++c) {
-        const uint32_t b = c == 0 ? (u & 1u) : 2u;  // TMEM region
-        const uint32_t use = b == 0 ? use0 : (b == 1 ? use1 : use2);
-        if (!mbar_wait_warp(acc_full + b, use & 1u, abort_flag, p.status)) {
+        const uint32_t b = (u + (uint32_t)c) & 1u;
+        if (!mbar_wait_warp(acc_full + b, (b ? use1 : use0) & 1u, abort_flag, p.status)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const int tokc = s.tok0 + (c == 0 ? 0 : C::N0);
         const int nc = c == 0 ? s.n[0] : s.n[1];
-        const uint32_t acc = lane_base + (b == 0 ? 0u : (b == 1 ? C::COL_R1 : C::COL_R2));
+        const uint32_t acc = lane_base + b * 256u;
 #pragma unroll 1
         for (int j0 = 0; j0 < nc; j0 += 32) {
           uint32_t v[32];
@@ -422,12 +418,10 @@ __global__ void __launch_bounds__(SwapCfg<EPI>::THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster_cta(acc_empty_l + b * 8);
-        if (b == 0) ++use0;
-        else if (b == 1) ++use1;
-        else ++use2;
+        (b ? use1 : use0) += 1;
       }
       if (!ok) break;
-      ++u;
+      u += (uint32_t)s.chunks;
     }
   }
 

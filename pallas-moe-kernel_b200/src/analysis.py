@@ -20,7 +20,7 @@ Two layers.
    threads, shared memory, TMEM columns, cluster, tile shape, pipeline
    stages, tcgen05 MMA kind, F-splits), and per launch the work units the
    group sizes produce (256-row x 256-column pair tiles of the grouped GEMMs,
-   expert super-tiles of up to 288 tokens x 256 features for small experts
+   expert super-tiles of up to 384 tokens x 256 features for small experts
    with e4m3 weights, 128-row blocks x F-splits of the fused small-D kernel),
    padded rows, waves
    over the persistent grid, tensor work issued (padding and the three
@@ -288,18 +288,16 @@ def _launch_model(L: dict, M: int, D: int, F: int, E: int, g: list[int], dtype: 
         N, K = L["gemm_n"], L["gemm_k"]
         ncol = -(-N // L["tile_n"])
         if name.startswith("grouped_gemm_swap_kernel"):
-            # expert super-tiles of tile_m tokens: a chunk of up to tile_m - 64
-            # tokens and one of up to 64, each an MMA with N = its tokens
-            # rounded up to 32
+            # expert super-tiles of tile_m tokens: chunks of <= 256 and <= 128
+            # tokens, each an MMA with N = its tokens rounded up to 32
             st = [-(-v // L["tile_m"]) for v in g]
             tiles = sum(st) * ncol
             rows_pad = 0
-            c0 = L["tile_m"] - 64
             for v in g:
                 for k in range(-(-v // L["tile_m"])):
                     rem = v - k * L["tile_m"]
-                    n0 = min(rem, c0)
-                    n1 = min(max(rem - c0, 0), 64)
+                    n0 = min(rem, 256)
+                    n1 = min(max(rem - 256, 0), 128)
                     rows_pad += -(-n0 // 32) * 32 + -(-n1 // 32) * 32
         else:
             rows_blocks = [-(-v // L["tile_m"]) for v in g]

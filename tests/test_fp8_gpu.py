@@ -78,8 +78,8 @@ def test_fp8_full_oracle(M, D, F, E, gs, fp8_kernel):
 
 
 @pytest.mark.parametrize("gs", [
-    [1, 31, 32, 33, 224, 225, 288, 289],       # 32-token MMA steps; chunk 0 full / chunk 1 / next super-tile
-    [255, 256, 257, 0, 0, 0, 576, 577],        # 256-row tiles of the row-tiled kernel; two and three super-tiles
+    [1, 31, 32, 33, 64, 96, 127, 128],         # chunk sizes around the 32-token MMA step
+    [255, 256, 257, 383, 384, 385, 0, 0],      # chunk 0 / chunk 1 / next super-tile boundaries
     [700, 0, 0, 0, 0, 0, 0, 1069],             # several super-tiles per expert; sum < M
     [0, 0, 0, 0, 0, 0, 0, 0],                  # nothing routed
 ])
