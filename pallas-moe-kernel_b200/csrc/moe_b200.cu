@@ -234,31 +234,50 @@ static int device_info(int* dev_out, DevInfo** info) {
   return 0;
 }
 
+// The tf32 split reads raw f32 weights in 16-byte vectors.
+static int check_weights_aligned(const void* w_up, const void* w_down) {
+  if ((reinterpret_cast<uintptr_t>(w_up) | reinterpret_cast<uintptr_t>(w_down)) & 15u)
+    return fail(MOE_ERR_MISALIGNED, "f32 weights must be 16-byte aligned");
+  return 0;
+}
+
 // ------------------------------------------------------------------ operand pre-split (3xTF32)
 // W (E, R, C) f32 -> hi/lo planes of W^T (E, C, R): hi = W rounded to the
-// nearest tf32 value (tf32_hi_bits), lo = W - hi.  32x32 tiles through shared memory so both the
-// read and the write are coalesced.
-// One 32x32 tile (rows r0.., columns c0.. of expert e) by 256 threads laid
-// out 32 x 8 (tx = column lane, ty = row group).
+// nearest tf32 value (tf32_hi_bits), lo = W - hi.  One 32x32 tile (rows r0..,
+// columns c0.. of expert e) per 256 threads through a padded shared tile, in
+// 16-byte vectors both ways: thread t loads row t / 8, columns 4 (t % 8) ..
+// +3, and stores column t / 8, rows 4 (t % 8) .. +3 of both planes.  R and C
+// are multiples of 4 and W and the planes 16-byte aligned (the callers check).
+// The transposed read of the tile is conflict-free: rows 4 (t % 8) + j and
+// column t / 8 fall in 32 distinct banks with the 33-float row pitch.
 __device__ __forceinline__ void split_transpose_tile(const float* __restrict__ w, float* __restrict__ hi,
                                                      float* __restrict__ lo, int R, int C, int e, int c0, int r0,
                                                      int tx, int ty, float (*tile)[33]) {
+  const int t = ty * 32 + tx;
   const float* src = w + (size_t)e * R * C;
-  for (int i = ty; i < 32; i += 8) {
-    const int r = r0 + i, c = c0 + tx;
-    tile[i][tx] = (r < R && c < C) ? src[(size_t)r * C + c] : 0.f;
+  {
+    const int i = t >> 3, c4 = (t & 7) * 4;
+    const int r = r0 + i, c = c0 + c4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r < R && c < C) v = __ldg(reinterpret_cast<const float4*>(src + (size_t)r * C + c));
+    tile[i][c4] = v.x;
+    tile[i][c4 + 1] = v.y;
+    tile[i][c4 + 2] = v.z;
+    tile[i][c4 + 3] = v.w;
   }
   __syncthreads();
-  float* dh = hi + (size_t)e * R * C;
-  float* dl = lo + (size_t)e * R * C;
-  for (int i = ty; i < 32; i += 8) {
-    const int c = c0 + i, r = r0 + tx;
-    if (r < R && c < C) {
-      const float v = tile[tx][i];
-      const float h = __uint_as_float(tf32_hi_bits(__float_as_uint(v)));
-      dh[(size_t)c * R + r] = h;
-      dl[(size_t)c * R + r] = v - h;
+  const int cc = t >> 3, r4 = (t & 7) * 4;
+  const int c = c0 + cc, r = r0 + r4;
+  if (r < R && c < C) {
+    float v[4], h[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[j] = tile[r4 + j][cc];
+      h[j] = __uint_as_float(tf32_hi_bits(__float_as_uint(v[j])));
     }
+    const size_t o = (size_t)e * R * C + (size_t)c * R + r;
+    *reinterpret_cast<float4*>(hi + o) = make_float4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<float4*>(lo + o) = make_float4(v[0] - h[0], v[1] - h[1], v[2] - h[2], v[3] - h[3]);
   }
 }
 
@@ -471,6 +490,8 @@ static int run_large_tf32(const float* x, const float* w_up, const float* w_down
   if (ws_bytes < L.total) return fail(MOE_ERR_WORKSPACE_TOO_SMALL, "workspace %zu bytes < required %zu", ws_bytes, L.total);
   if (reinterpret_cast<uintptr_t>(ws) & 255u) return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
   if (reinterpret_cast<uintptr_t>(x) & 15u) return fail(MOE_ERR_MISALIGNED, "x must be 16-byte aligned");
+  if (split_weights)
+    if (int r = check_weights_aligned(w_up, w_down)) return r;
   uint8_t* b = static_cast<uint8_t*>(ws);
   float* wu_hi = reinterpret_cast<float*>(b + L.wu_hi);
   float* wu_lo = reinterpret_cast<float*>(b + L.wu_lo);
@@ -962,6 +983,7 @@ static int prepare_small(const void* w_up, const void* w_down, int D, int F, int
   const SmallPlan plan = small_plan(0, D, F, E, dtype);
   if (dtype != MOE_DTYPE_F32) return 0;
   if (int r = check_workspace(plan, ws, ws_bytes)) return r;
+  if (int r = check_weights_aligned(w_up, w_down)) return r;
   const size_t wsz = (size_t)E * D * F;
   float* wu_hi = static_cast<float*>(ws);
   float* wu_lo = wu_hi + wsz;
@@ -1084,6 +1106,8 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
   float* x_hi = wd_lo + wsz;
   float* x_lo = x_hi + (size_t)M * D;
   const bool f32 = dtype == MOE_DTYPE_F32;
+  if (f32 && split_weights)
+    if (int r = check_weights_aligned(w_up, w_down)) return r;
   {
     // One preparation launch for what this call needs before the fused kernel.
     PrepArgs pa{};
