@@ -215,8 +215,8 @@ def make_workload(cfg, device, seed: int = 0, experts=None):
     w_down = torch.empty((e1 - e0, cfg.F, cfg.D), device=device, dtype=wdt)
     scales = None
     if cfg.dtype == "fp8":   # e4m3 weights with 128x128 f32 block scales (amax / 448)
-        scales = (torch.empty((e1 - e0, cfg.D // 128, cfg.F // 128), device=device),
-                  torch.empty((e1 - e0, cfg.F // 128, cfg.D // 128), device=device))
+        db, fb = -(-cfg.D // 128), -(-cfg.F // 128)   # partial 128-blocks at the ends
+        scales = (torch.empty((e1 - e0, db, fb), device=device), torch.empty((e1 - e0, fb, db), device=device))
     for i, e in enumerate(range(e0, e1)):
         g.manual_seed(99991 * (e + 1))
         wu = torch.randn((cfg.D, cfg.F), generator=g, device=device) / math.sqrt(cfg.D)
@@ -912,6 +912,8 @@ def main() -> int:
                     help="override the configuration's precision path (same shapes and routing)")
     ap.add_argument("--experts", type=int, default=0,
                     help="override E (with --tokens: a smaller case with the same rows per expert)")
+    ap.add_argument("--dmodel", type=int, default=0, help="override D (the model dimension)")
+    ap.add_argument("--dff", type=int, default=0, help="override F (the expert hidden dimension)")
     ap.add_argument("--waves", type=int, default=2,
                     help="N>1: token waves per step (dispatch/combine of one wave overlap the experts of the next)")
     ap.add_argument("--reserve-sms", type=int, default=0,
@@ -933,6 +935,9 @@ def main() -> int:
         cfg = with_shape(cfg, M=args.tokens, tokens=args.tokens // k if k else 0, name=f"{cfg.name}_M{args.tokens}")
     if args.experts:
         cfg = with_shape(cfg, E=args.experts, name=f"{cfg.name}_E{args.experts}")
+    if args.dmodel or args.dff:
+        D, F = args.dmodel or cfg.D, args.dff or cfg.F
+        cfg = with_shape(cfg, D=D, F=F, name=f"{cfg.name}_D{D}_F{F}")
     if args.dtype and args.dtype != cfg.dtype:
         cfg = with_shape(cfg, dtype=args.dtype, name=f"{cfg.name}_as_{args.dtype}")
     world = int(os.environ.get("WORLD_SIZE", "1"))
