@@ -436,7 +436,7 @@ static int launch_gemm(const GemmMaps& maps, const GemmParams& prm_in, DevInfo* 
 }
 
 template <int EPI>
-static int launch_swap(const GemmMaps& maps, const GemmParams& prm, DevInfo* di, cudaStream_t st, int ctas_req) {
+static int launch_swap(const SwapMaps& maps, const GemmParams& prm, DevInfo* di, cudaStream_t st, int ctas_req) {
   using Cfg = SwapCfg<EPI>;
   auto kern = grouped_gemm_swap_kernel<EPI>;
   constexpr int slot = 42 + EPI;
@@ -585,11 +585,27 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
   // Small experts with e4m3 weights: expert super-tiles (grouped_gemm_swap.cuh),
   // unless the down GEMM must store Y rows into their source ranks.
   const bool swap = fp8 && !opt.scatter && fp8_use_swap(M, E);
-  const uint32_t a_box_rows = swap ? SwapCfg<0>::XBOX : 128;
+  if (swap) {
+    // Token rows in 32-, 64- and 128-row boxes; e4m3 weights {128, 64, 1}.
+    auto swap_maps = [&](SwapMaps* m, const void* rows, int K, const void* w, int N) -> int {
+      memset(m, 0, sizeof(*m));
+      if (int r = make_map_2d(&m->x32, rows, F16, 2, (uint64_t)M, K, 64, 32)) return r;
+      if (int r = make_map_2d(&m->x64, rows, F16, 2, (uint64_t)M, K, 64, 64)) return r;
+      if (int r = make_map_2d(&m->x128, rows, F16, 2, (uint64_t)M, K, 64, 128)) return r;
+      return make_map_3d(&m->w, w, U8, 1, (uint64_t)E, K, N, 128, 64);
+    };
+    SwapMaps s1, s2;
+    if (int r = swap_maps(&s1, xa, D, w_up, F)) return r;
+    GemmParams p1{gs, ws, (int)M, E, F, D, 8, status, w_up_scale, 0};
+    if (int r = launch_swap<0>(s1, p1, di, st, ctas)) return r;
+    if (int r = swap_maps(&s2, ws, F, w_down, D)) return r;
+    GemmParams p2{gs, y, (int)M, E, D, F, 8, status, w_down_scale, opt.skip_tail ? 1 : 0};
+    return launch_swap<1>(s2, p2, di, st, ctas);
+  }
   // up: H = GELU(X @ W_up[e])
   GemmMaps m1;
   memset(&m1, 0, sizeof(m1));
-  if (int r = make_map_2d(&m1.a, xa, A16, 2, (uint64_t)M, D, 64, a_box_rows)) return r;
+  if (int r = make_map_2d(&m1.a, xa, A16, 2, (uint64_t)M, D, 64, 128)) return r;
   if (fp8) {
     if (int r = make_map_3d(&m1.b, w_up, U8, 1, (uint64_t)E, D, F, 128, 64)) return r;
   } else {
@@ -597,14 +613,12 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
   }
   GemmParams p1{gs, ws, (int)M, E, F, D, 8, status, w_up_scale, 0};
   if (opt.dispatch && !fp8) p1.dispatch = *opt.dispatch;  // (f32 took run_large_tf32 above)
-  if (int r = swap ? launch_swap<0>(m1, p1, di, st, ctas)
-               : fp8  ? launch_gemm<0, true>(m1, p1, di, st, ctas)
-                      : launch_gemm<0, false>(m1, p1, di, st, ctas))
+  if (int r = fp8 ? launch_gemm<0, true>(m1, p1, di, st, ctas) : launch_gemm<0, false>(m1, p1, di, st, ctas))
     return r;
   // down: Y = H @ W_down[e]
   GemmMaps m2;
   memset(&m2, 0, sizeof(m2));
-  if (int r = make_map_2d(&m2.a, ws, A16, 2, (uint64_t)M, F, 64, a_box_rows)) return r;
+  if (int r = make_map_2d(&m2.a, ws, A16, 2, (uint64_t)M, F, 64, 128)) return r;
   if (fp8) {
     if (int r = make_map_3d(&m2.b, w_down, U8, 1, (uint64_t)E, F, D, 128, 64)) return r;
   } else {
@@ -612,7 +626,6 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
   }
   GemmParams p2{gs, y, (int)M, E, D, F, 8, status, w_down_scale, opt.skip_tail ? 1 : 0};
   if (opt.scatter) p2.scatter = *opt.scatter;
-  if (swap) return launch_swap<1>(m2, p2, di, st, ctas);
   if (fp8) return launch_gemm<1, true>(m2, p2, di, st, ctas);
   return down_wide() ? launch_gemm<1, false, false, 2>(m2, p2, di, st, ctas)
                      : launch_gemm<1, false, false>(m2, p2, di, st, ctas);
