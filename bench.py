@@ -355,6 +355,34 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
     if status:
         raise RuntimeError(f"device status {status} after the timed region")
 
+    # Expert parallelism: what sets the step.  Each rank's landing rows (its
+    # experts' rows from every source, from the gathered group sizes) and a
+    # compute-only leg -- this rank's experts on that many rows through the
+    # single-GPU grouped GEMMs, no exchange -- timed the same way as the step.
+    ep_rank = None
+    if world > 1:
+        gs_all = torch.empty((world, cfg.E), dtype=torch.int64, device=device)
+        dist.all_gather_into_tensor(gs_all, gs_dev.to(torch.int64))
+        lgs = gs_all[:, rank * el:(rank + 1) * el].clamp(min=0).sum(dim=0)
+        land = int(lgs.sum())
+        local = PreparedExperts(w_up, w_down, max_tokens=max(land, 1), **sc)
+        gl = torch.Generator(device=device)
+        gl.manual_seed(4321 + rank)
+        x_land = torch.randn((max(land, 1), cfg.D), generator=gl, device=device, dtype=torch.float32).to(x.dtype)
+        y_land = torch.empty((max(land, 1), cfg.D), device=device, dtype=torch.float32)
+        lgs32 = lgs.to(torch.int32)
+        for _ in range(2):
+            local(x_land, lgs32, out=y_land)
+        comp_ms = timed(lambda: local(x_land, lgs32, out=y_land), args.steps)
+        del local, x_land, y_land
+        mine = torch.tensor([statistics.mean(step_ms), statistics.mean(comp_ms), float(land),
+                             float(step_clock.get("sm_mhz") or 0.0)], dtype=torch.float64, device=device)
+        ep_rank = torch.empty((world, 4), dtype=torch.float64, device=device)
+        dist.all_gather_into_tensor(ep_rank, mine)
+        ep_rank = ep_rank.cpu().tolist()
+        if _lib.device_status(reset=True):
+            raise RuntimeError("device status set by the compute-only leg")
+
     # e2e: every step copies its inputs from pinned host memory, runs the
     # public call and reads Y back into pinned host memory.  Consecutive steps
     # are pipelined on three streams (copy in, compute, copy out) over two
@@ -505,6 +533,26 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
                 line["roofline"]["traffic"] = json.loads(prof.read_text()).get("traffic_bytes_per_launch")
             except Exception:
                 pass
+    if ep_rank is not None:
+        st_ms = [r[0] for r in ep_rank]
+        cp_ms = [r[1] for r in ep_rank]
+        rows = [int(r[2]) for r in ep_rank]
+        slow = max(range(world), key=lambda r: st_ms[r])
+        heavy = max(range(world), key=lambda r: cp_ms[r])
+        line["ep"] = {
+            "rank_step_ms": [round(v, 4) for v in st_ms],
+            "rank_compute_only_ms": [round(v, 4) for v in cp_ms],
+            "rank_landing_rows": rows,
+            "rank_sm_mhz_device": [round(r[3]) for r in ep_rank],
+            "rows_imbalance": max(rows) / (sum(rows) / world) if sum(rows) else None,
+            "exchange_overhead_ms": max(st_ms) - max(cp_ms),
+            "sets_the_step": (f"rank {heavy}'s expert GEMMs on its {rows[heavy]} landing rows take "
+                              f"{cp_ms[heavy]:.3f} ms of the slowest rank's (rank {slow}) "
+                              f"{st_ms[slow]:.3f} ms step; the rest ({max(st_ms) - max(cp_ms):.3f} ms) is the "
+                              f"exchange beyond the overlap"),
+            "compute_only": "this rank's experts on a landing-sized input through the single-GPU grouped GEMMs, "
+                            "no exchange, timed like the step (L2 flushed)",
+        }
     line["clocks"] = clocks.summary(t0, t1)
     line["clocks"]["sm_mhz_device"] = step_clock.get("sm_mhz")
     line["clocks"]["device_sms_sampled"] = step_clock.get("sms")
