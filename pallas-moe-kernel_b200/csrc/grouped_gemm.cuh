@@ -137,7 +137,10 @@ struct GemmCfg {
   static constexpr int STAGE = PLANES * (A_BYTES + WIDE * B_BYTES);  // operand stage
   static constexpr int NS = TF32 ? 3 : ((BFP8 || WIDE == 2) ? 4 : 6); // operand stages
   static constexpr int NR = BFP8 ? 10 : 0;             // raw e4m3 stages (HBM stream runs ahead)
-  static constexpr int EPI_WARPS = 4;
+  // 3xTF32 tiles hold all 512 TMEM columns (no overlap with the next tile's
+  // MMAs), so their epilogue runs on eight warps: two per TMEM lane quadrant,
+  // each draining half of the tile's columns.
+  static constexpr int EPI_WARPS = TF32 ? 8 : 4;
   static constexpr int CVT_WARPS = BFP8 ? 8 : 0;  // two per SM sub-partition
   static constexpr int OUT_STAGE = EPI_WARPS * 32 * 128;  // 4 KB per warp: 32 rows x 128 B
   static constexpr int BAR_BYTES = BFP8 ? 512 : 256;
@@ -625,7 +628,7 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32, WIDE>::LAUNCH_BOUND, 
       }
       const size_t n4 = (size_t)(p.M - total) * p.N / 4;
       float4* base = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (size_t)total * p.N);
-      const int etid = (int)threadIdx.x - 64;  // epilogue threads are 64 .. 64 + 127
+      const int etid = (int)threadIdx.x - 64;  // epilogue threads are 64 .. 64 + 32 EPI_WARPS - 1
       for (size_t i = (size_t)blockIdx.x * (C::EPI_WARPS * 32) + etid; i < n4;
            i += (size_t)gridDim.x * (C::EPI_WARPS * 32))
         base[i] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -647,13 +650,16 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32, WIDE>::LAUNCH_BOUND, 
       const float mul = BFP8 ? exp2i(-fp8_tile_shift(p.b_scale, p.K, p.N, cur.e, nb, lane)) : 1.f;
       // Columns of this tile inside N (the last column tile may be partial).
       const int ncol = p.N - nb * C::TILE_N < C::TILE_N ? p.N - nb * C::TILE_N : C::TILE_N;
+      // 3xTF32: this warp's half of the columns, [cb, ce).
+      const int cb = TF32 ? (int)((warp - 2u) >> 2) * (C::BN / 2) : 0;
+      const int ce = TF32 ? (ncol < cb + C::BN / 2 ? ncol : cb + C::BN / 2) : ncol;
       if constexpr (TF32 && EPI == 0) {
         // 32 columns per step: GELU (f32 accuracy), then the tf32 split
         // g = hi + lo (tf32_hi_bits); each plane goes out through the 32-row
         // x 128-byte staging as full-line row stores.
         float4* wst4 = reinterpret_cast<float4*>(wst);
 #pragma unroll 1
-        for (int c0 = 0; c0 < ncol; c0 += 32) {
+        for (int c0 = cb; c0 < ce; c0 += 32) {
           uint32_t v[32], w[32];
           tmem_ld32(acc + c0, v);
           tmem_ld32(acc + C::BN + c0, w);  // cross terms
@@ -852,7 +858,7 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32, WIDE>::LAUNCH_BOUND, 
         float* Y = reinterpret_cast<float*>(p.out) + (size_t)nb * C::BN;
         float4* wst4 = reinterpret_cast<float4*>(wst);
 #pragma unroll 1
-        for (int c0 = 0; c0 < ncol; c0 += 32) {
+        for (int c0 = cb; c0 < ce; c0 += 32) {
           uint32_t v[32], w[32];
           tmem_ld32(acc + c0, v);
           tmem_ld32(acc + C::BN + c0, w);
