@@ -572,6 +572,70 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
 
 
 # --------------------------------------------------------------------- whole MoE layer (routing stage)
+def quick_config(cfg, steps: int, warmup: int, device) -> dict:
+    """Device-resident figures of one more configuration on this GPU: the
+    reference entry point (raw weights in, Y out) and the fused kernel(s)
+    alone (weights prepared), alternated launch by launch with L2 flushed
+    before each, with the device clock of that region.  No e2e leg and no
+    CPU baseline: these ride along the headline line as evidence."""
+    import torch
+    from src import _lib, analysis
+    from src.kernel import PreparedExperts, fused_ragged_dot_caller
+
+    x, w_up, w_down, gs_np, scales = make_workload(cfg, device)
+    sc = {} if scales is None else {"w_up_scale": scales[0], "w_down_scale": scales[1]}
+    gs_dev = torch.from_numpy(gs_np).to(device)
+    experts = PreparedExperts(w_up, w_down, max_tokens=cfg.M, **sc)
+    y = torch.empty((cfg.M, cfg.D), device=device, dtype=torch.float32)
+    ws = torch.empty(max(experts.ws_bytes, 1), device=device, dtype=torch.uint8)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step_fn():
+        return fused_ragged_dot_caller(x, w_up, w_down, gs_dev, BM=16, BF=64, max_group_size=cfg.M,
+                                       out=y, workspace=ws, **sc)
+
+    def kern_fn():
+        return experts(x, gs_dev, out=y)
+
+    for _ in range(warmup):
+        step_fn()
+        kern_fn()
+    torch.cuda.synchronize(device)
+    _lib.device_status(reset=True)
+    dclk = DeviceClock(device)
+    s_ev, k_ev = [], []
+    c_a = dclk.sample(stream)
+    for _ in range(steps):
+        for fn, evs in ((step_fn, s_ev), (kern_fn, k_ev)):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            evs.append((a, b))
+    c_b = dclk.sample(stream)
+    torch.cuda.synchronize(device)
+    if _lib.device_status(reset=True):
+        raise RuntimeError(f"device status set while timing {cfg.name}")
+    s_ms = statistics.mean(a.elapsed_time(b) for a, b in s_ev)
+    k_ms = statistics.mean(a.elapsed_time(b) for a, b in k_ev)
+    mhz = DeviceClock.mhz(c_a, c_b).get("sm_mhz")
+    peaks, _ = load_peaks()
+    r = analysis.roofline(cfg.M, cfg.D, cfg.F, gs_np.tolist(), cfg.dtype, kernel_ms=k_ms, peaks=peaks)
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    clk_peak = (F16_FLOP_PER_CLK_SM * sms * mhz * 1e6 / 1e12 / (6.0 if cfg.dtype == "f32" else 1.0)
+                if mhz else None)
+    out = {"workload": cfg.name, "value": cfg.M / (s_ms / 1e3), "unit": "tokens/s", "ms_per_step": s_ms,
+           "kernel_ms": k_ms, "bound": r["bound"], "achieved": r["achieved"], "roofline_unit": r["unit"],
+           "frac": r["frac"], "sm_mhz_device": mhz,
+           "frac_at_clock": (r["achieved"] / clk_peak if clk_peak and r["bound"] == "tensor" else None),
+           "steps": steps, "warmup": warmup}
+    del x, w_up, w_down, experts, y, ws, flush
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_layer(args, cfg, device) -> dict:
     """Routing stage around the expert MLP on one GPU: top-k routing of
     ``tokens`` router inputs over E experts, stable permutation by expert, row
@@ -970,6 +1034,9 @@ def main() -> int:
     ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
                     help="N>1: token exchange by the library's kernels over NVLink peer memory (peer) "
                          "or by NCCL send/recv from Python (nccl)")
+    ap.add_argument("--no-other-configs", dest="other_configs", action="store_false",
+                    help="N=1: skip the device-resident figures of the other configurations (c1..c5) that "
+                         "otherwise ride along the line under other_configs")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -1024,6 +1091,18 @@ def main() -> int:
             if not args.no_cpu_baseline and world == 1:
                 base = cpu_reference(cfg, budget_s=args.ref_budget)
                 line["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            if world == 1 and args.other_configs and not (args.tokens or args.experts or args.dmodel
+                                                          or args.dff or args.dtype):
+                others = {}
+                for name in ("c1", "c2", "c3", "c5"):
+                    if name == args.config:
+                        continue
+                    try:
+                        others[name] = quick_config(CONFIGS[name], steps=min(args.steps, 20), warmup=3,
+                                                    device=device)
+                    except Exception as exc:  # reported, never hides the headline line
+                        others[name] = {"error": f"{type(exc).__name__}: {exc}"}
+                line["other_configs"] = others
             print(json.dumps(line), flush=True)
     finally:
         if world > 1:
