@@ -152,7 +152,8 @@ def _worker(rank, world, port, case, q):
         from oracle import moe_oracle as orc
         from src import _lib
         from src.ep import PeerExpertParallelMLP
-        from src.routing import multinomial_group_sizes, zipf_group_sizes
+        from src.routing import (dequantize_e4m3_blockwise, multinomial_group_sizes, quantize_e4m3_blockwise,
+                                 zipf_group_sizes)
         torch.cuda.set_device(rank)
         dev = torch.device("cuda", rank)
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -163,11 +164,17 @@ def _worker(rank, world, port, case, q):
         wu = (rng.standard_normal((E, D, F)) / np.sqrt(D)).astype(np.float32)
         wd = (rng.standard_normal((E, F, D)) / np.sqrt(F)).astype(np.float32)
         tdt = torch.float32 if dt == "f32" else torch.bfloat16
-        wu_t = torch.from_numpy(wu).to(dev, tdt)
-        wd_t = torch.from_numpy(wd).to(dev, tdt)
         El = E // world
-        layer = PeerExpertParallelMLP(wu_t[rank * El:(rank + 1) * El], wd_t[rank * El:(rank + 1) * El],
-                                      rank=rank, world=world, max_tokens=M, waves=waves)
+        own = slice(rank * El, (rank + 1) * El)
+        if dt == "fp8":   # e4m3 weights with 128 x 128 block scales; the oracle sees them dequantised
+            (qu, su), (qd, sd) = (quantize_e4m3_blockwise(torch.from_numpy(w).to(dev)) for w in (wu, wd))
+            wu_t, wd_t = dequantize_e4m3_blockwise(qu, su), dequantize_e4m3_blockwise(qd, sd)
+            layer = PeerExpertParallelMLP(qu[own], qd[own], rank=rank, world=world, max_tokens=M, waves=waves,
+                                          w_up_scale=su[own], w_down_scale=sd[own])
+        else:
+            wu_t = torch.from_numpy(wu).to(dev, tdt)
+            wd_t = torch.from_numpy(wd).to(dev, tdt)
+            layer = PeerExpertParallelMLP(wu_t[own], wd_t[own], rank=rank, world=world, max_tokens=M, waves=waves)
         errs = []
         r2 = np.random.default_rng(100 + rank)
         for step in range(3):
@@ -192,7 +199,8 @@ def _worker(rank, world, port, case, q):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("case,tol", [((2048, 128, 512, 4, "f32", 1), 1e-5), ((2048, 128, 512, 4, "f32", 3), 1e-5),
-                                      ((2048, 512, 1024, 4, "bf16", 2), 1e-2), ((1024, 512, 1024, 8, "bf16", 1), 1e-2)])
+                                      ((2048, 512, 1024, 4, "bf16", 2), 1e-2), ((1024, 512, 1024, 8, "bf16", 1), 1e-2),
+                                      ((2048, 512, 1024, 8, "fp8", 1), 2e-2)])
 def test_engine_two_gpus(case, tol):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
