@@ -439,7 +439,10 @@ int moe_sm_clock_sample(uint64_t* out, int32_t blocks, void* stream);
  * for both, 1 evict_normal for both, 2 A evict_first, 3 B evict_first),
  * 7 = e4m3-weight GELU experts (0 automatic: expert super-tiles when M <=
  * 384 E, 1 row-tiled pair kernel, 2 expert super-tiles), 8 = bf16 down GEMM
- * tile width (0 automatic = 256 columns, 1 256 columns, 2 512 columns).
+ * tile width (0 automatic = 256 columns, 1 256 columns, 2 512 columns),
+ * 10 = fused small-D kernel's last wave (0 automatic: a last wave of at most
+ * half the grid runs as half units when the call's preparation launch runs
+ * anyway, 1 whole units only).
  * Returns 0 or MOE_ERR_INVALID_ARG.
  */
 int moe_set_tuning(int32_t key, int64_t value);

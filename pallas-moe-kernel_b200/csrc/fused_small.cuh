@@ -56,7 +56,70 @@ struct FusedParams {
   int* status;                // device status word (kStatus* bits)
   unsigned long long* trace;  // MOE_TRACE builds: per-CTA event timeline (else unused)
   int skip_tail;              // 1: leave rows at or past sum(group_sizes) unwritten
+  int tail_halves;            // 1: a last partial wave of at most half the grid runs as half units
 };
+
+// Work units of the fused kernel.  Unit u of the persistent grid (CTA c takes
+// u = c, c + G, ...) is normally (128-row block u / S, F-split u % S) with NCH
+// hidden chunks.  When the units do not fill the last wave and that wave
+// would hold at most G / 2 of them, each of those last units is split into
+// two halves of NCH / 2 chunks that run on two CTAs and reduce-add into Y
+// (rows zeroed up front).  Two partial sums added onto zero give the same
+// bits in either order, so results stay deterministic.
+struct SmallUnits {
+  int full;    // units [0, full) are whole
+  int halves;  // 2: units from `full` on are halves; 1: none
+};
+// Block count of the routing (the same clamping as BlockCursorT).
+__device__ __forceinline__ int small_block_count(const int32_t* gs, int E, int M, int shift = 7) {
+  int nb = 0, row = 0;
+  for (int e = 0; e < E; ++e) {
+    int g = __ldg(gs + e);
+    g = g < 0 ? 0 : g;
+    const int rem = M - row;
+    g = g > rem ? (rem > 0 ? rem : 0) : g;
+    row += g;
+    nb += (g + (1 << shift) - 1) >> shift;
+  }
+  return nb;
+}
+__device__ __forceinline__ SmallUnits small_units(const int32_t* gs, int E, int M, int splits, int nch, int grid,
+                                                  int tail_halves) {
+  const int u0 = small_block_count(gs, E, M) * splits;
+  const int full = (u0 / grid) * grid;
+  const int tail = u0 - full;
+  if (tail_halves && tail > 0 && 2 * tail <= grid && nch % 2 == 0) return {full, 2};
+  return {u0, 1};
+}
+// First row of global 128-row block `block`; the routed row count when the
+// block is past the last one.
+__device__ __forceinline__ int small_block_row(const int32_t* gs, int E, int M, int block) {
+  int nb = 0, row = 0;
+  for (int e = 0; e < E; ++e) {
+    int g = __ldg(gs + e);
+    g = g < 0 ? 0 : g;
+    const int rem = M - row;
+    g = g > rem ? (rem > 0 ? rem : 0) : g;
+    const int n = (g + 127) >> 7;
+    if (block < nb + n) return row + (block - nb) * 128;
+    nb += n;
+    row += g;
+  }
+  return row;
+}
+struct UnitWork {
+  int gb;      // global 128-row block
+  int fch0;    // first hidden chunk
+  int nch;     // hidden chunks
+  bool atomic; // reduce-add into Y
+};
+__device__ __forceinline__ UnitWork unit_work(int u, SmallUnits su, int S, int NCH, bool atomic_out) {
+  if (u < su.full) return {u / S, (u % S) * NCH, NCH, atomic_out};
+  const int v = u - su.full;
+  const int w = su.full + v / su.halves;
+  const int n = NCH / su.halves;
+  return {w / S, (w % S) * NCH + (v % su.halves) * n, n, atomic_out || su.halves > 1};
+}
 
 // Optional timeline of pipeline events (clock64 per event) for CTA-level
 // analysis; compiled in only with -DMOE_TRACE.  Layout per CTA: 4 rows
@@ -105,6 +168,7 @@ struct FusedCfg {
   static constexpr int NS_FIT = (kMaxSmemPerBlock - 1024 - BAR_BYTES - X_BYTES - Y_STAGE) / STAGE;
   static constexpr int NS = NS_FIT > 8 ? 8 : NS_FIT;
   static constexpr int SMEM = 1024 + X_BYTES + NS * STAGE + Y_STAGE + BAR_BYTES;
+  static_assert((2 * NS + 9) * 8 + 4 * 4 <= BAR_BYTES, "barriers, TMEM slot, abort flag and unit plan");
   // TMEM columns: Y accumulator [0, D); hidden buffer b at D + b * HCOLS
   // (accumulator / hi plane first, lo plane after it); X_lo after both.
   static constexpr int HCOLS = PL * BF;
@@ -223,11 +287,16 @@ __global__ void __launch_bounds__(64 + 256, 1)
   uint64_t* y_empty = x_full + 8;       // epilogue drained Y_acc
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(x_full + 9);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* plan_smem = reinterpret_cast<int*>(tmem_slot + 2);  // SmallUnits of this launch
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
 
   if (threadIdx.x == 0) {
+    const SmallUnits su0 = small_units(p.group_sizes, p.E, p.M, p.splits, p.chunks_per_split, (int)gridDim.x,
+                                       p.tail_halves);
+    plan_smem[0] = su0.full;
+    plan_smem[1] = su0.halves;
     for (int i = 0; i < C::NS; ++i) {
       mbar_init(full + i, 1);
       mbar_init(empty + i, 1);
@@ -265,6 +334,8 @@ __global__ void __launch_bounds__(64 + 256, 1)
 
   const int S = p.splits;
   const int NCH = p.chunks_per_split;
+  const SmallUnits su{plan_smem[0], plan_smem[1]};
+  const bool atomic_all = p.atomic_out != 0;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -289,11 +360,13 @@ __global__ void __launch_bounds__(64 + 256, 1)
         }
       };
       for (int u = blockIdx.x; ok; u += gridDim.x, ++ui) {
-        const int gb = u / S;
+        const UnitWork uw = unit_work(u, su, S, NCH, atomic_all);
+        const int gb = uw.gb;
         if (!cur.seek(gb, p.group_sizes, p.E, p.M)) break;
         const int e = cur.e;
         const int row0 = cur.row_begin + (gb - cur.blk_begin) * C::BM;
-        const int fch0 = (u % S) * NCH;
+        const int fch0 = uw.fch0;
+        const int nch = uw.nch;
         if constexpr (X_RES) {
           if (!mbar_wait(x_empty, (ui & 1u) ^ 1u, abort_flag, p.status)) break;
           // Raw X (the bf16 operand, or f32 split in place by the GELU warps).
@@ -303,9 +376,9 @@ __global__ void __launch_bounds__(64 + 256, 1)
           // Warm L2 with the next unit's X tile so its load at the end of this
           // unit does not wait on HBM.
           BlockCursor nxt = cur;
-          const int u_next = u + (int)gridDim.x;
-          if (nxt.seek(u_next / S, p.group_sizes, p.E, p.M)) {
-            const int nrow0 = nxt.row_begin + (u_next / S - nxt.blk_begin) * C::BM;
+          const int gb_next = unit_work(u + (int)gridDim.x, su, S, NCH, atomic_all).gb;
+          if (nxt.seek(gb_next, p.group_sizes, p.E, p.M)) {
+            const int nrow0 = nxt.row_begin + (gb_next - nxt.blk_begin) * C::BM;
             for (int s = 0; s < D / C::ATOM; ++s) tma_prefetch_l2_2d(&maps.x[0], s * C::ATOM, nrow0);
           }
         }
@@ -354,12 +427,12 @@ __global__ void __launch_bounds__(64 + 256, 1)
           advance();
           return true;
         };
-        for (int j = 0; j < NCH && ok; ++j) {
+        for (int j = 0; j < nch && ok; ++j) {
           for (int s = 0; s < C::N1 && ok; ++s) ok = load_s1(j, s);
           if (j > 0)
             for (int t = 0; t < C::N2 && ok; ++t) ok = load_s2(j - 1, t);
         }
-        for (int t = 0; t < C::N2 && ok; ++t) ok = load_s2(NCH - 1, t);
+        for (int t = 0; t < C::N2 && ok; ++t) ok = load_s2(nch - 1, t);
       }
     }
   } else if (warp == 1) {
@@ -389,8 +462,9 @@ __global__ void __launch_bounds__(64 + 256, 1)
         }
       };
       for (int u = blockIdx.x; ok; u += gridDim.x, ++ui) {
-        const int gb = u / S;
-        if (!cur.seek(gb, p.group_sizes, p.E, p.M)) break;
+        const UnitWork uw = unit_work(u, su, S, NCH, atomic_all);
+        const int nch = uw.nch;
+        if (!cur.seek(uw.gb, p.group_sizes, p.E, p.M)) break;
         if constexpr (X_RES) {
           if (!mbar_wait_warp(x_ready, ui & 1u, abort_flag, p.status)) break;
           tc_fence_after();
@@ -465,14 +539,14 @@ __global__ void __launch_bounds__(64 + 256, 1)
           }
           return true;
         };
-        for (int j = 0; j < NCH && ok; ++j) {
+        for (int j = 0; j < nch && ok; ++j) {
           ok = mma1(j);
-          if (ok && X_RES && j == NCH - 1) umma_commit(x_empty);
+          if (ok && X_RES && j == nch - 1) umma_commit(x_empty);
           if (ok && j > 0) ok = mma2(j - 1);
         }
-        if (ok) ok = mma2(NCH - 1);
+        if (ok) ok = mma2(nch - 1);
         if (ok) umma_commit(y_full);
-        hcount += NCH;
+        hcount += nch;
       }
     }
   } else {
@@ -556,14 +630,16 @@ __global__ void __launch_bounds__(64 + 256, 1)
     };
 
     int u = blockIdx.x;
-    bool have = cur.seek(u / S, p.group_sizes, p.E, p.M);
+    UnitWork uw = unit_work(u, su, S, NCH, atomic_all);
+    bool have = cur.seek(uw.gb, p.group_sizes, p.E, p.M);
     if (have && X_RES) ok = C::kTF32 ? split_x(0) : pass_x(0);
     while (have && ok) {
-      const int gb = u / S;
+      const int gb = uw.gb;
+      const int nch = uw.nch;
       const int row0 = cur.row_begin + (gb - cur.blk_begin) * C::BM;
       const int row_end = cur.row_begin + cur.rows;
       // Hidden chunks: TMEM accumulator -> GELU -> MMA2 operand.
-      for (int j = 0; j < NCH && ok; ++j) {
+      for (int j = 0; j < nch && ok; ++j) {
         const uint32_t hb = (hcount + j) & 1u;
         const uint32_t use = (hcount + j) >> 1;
         if (!warp_wait(h_full + hb, use & 1u)) {
@@ -612,13 +688,14 @@ __global__ void __launch_bounds__(64 + 256, 1)
         if (warp == 2 && lane == 0) MOE_TRACE_EV(2, (int)(2 * (hcount + j) + 1));
       }
       if (!ok) break;
-      hcount += NCH;
+      hcount += nch;
 
       // Look ahead: prepare the next unit's X operand before draining Y so
       // the tensor core can start the next unit's MMA1 meanwhile.
       const int u_next = u + gridDim.x;
+      const UnitWork uw_next = unit_work(u_next, su, S, NCH, atomic_all);
       BlockCursor nxt = cur;
-      const bool have_next = nxt.seek(u_next / S, p.group_sizes, p.E, p.M);
+      const bool have_next = nxt.seek(uw_next.gb, p.group_sizes, p.E, p.M);
       if (have_next && X_RES) {
         ok = C::kTF32 ? split_x(ui + 1) : pass_x(ui + 1);
         if (!ok) break;
@@ -633,11 +710,12 @@ __global__ void __launch_bounds__(64 + 256, 1)
       float4* wstage = ystage + (warp - 2u) * 256u;
 #pragma unroll 1
       for (int c0 = half * (D / 2); c0 < (int)(half + 1) * (D / 2); c0 += 32)
-        store_y_block<D>(lane_base + c0, wstage, p.y, row0 + (int)(q * 32u), row_end, c0, lane, p.atomic_out != 0);
+        store_y_block<D>(lane_base + c0, wstage, p.y, row0 + (int)(q * 32u), row_end, c0, lane, uw.atomic);
       tc_fence_before();
       mbar_arrive(y_empty);
 
       u = u_next;
+      uw = uw_next;
       cur = nxt;
       have = have_next;
       ++ui;

@@ -47,6 +47,7 @@ static int64_t g_tune_group_m = 0;  // grouped GEMMs: rasterisation group in 256
 static int64_t g_tune_l2 = 0;       // grouped GEMMs: L2 hint mode of the A / B loads (GemmParams::l2_mode)
 static int64_t g_tune_fp8 = 0;      // e4m3 weights: 0 automatic, 1 row-tiled pair kernel, 2 expert super-tiles
 static int64_t g_tune_wide = 0;     // bf16 down GEMM: 0 automatic, 1 256-column tiles, 2 512-column tiles
+static int64_t g_tune_tail = 0;     // fused small-D kernel: 0 automatic (half units in a short last wave), 1 off
 
 // bf16 down GEMM (f32 Y): 256-column tiles unless 512 are asked for.  At C4
 // the 512-column tiles cut the down GEMM's DRAM reads by a third (fewer
@@ -313,6 +314,10 @@ struct PrepArgs {
   float4* y;
   size_t y_n4;
   int y_blocks;
+  // Zero only the rows of the fused kernel's half units (one F-split): the
+  // launch's unit plan is recomputed here from the group sizes.
+  const int32_t* gs;
+  int y_tail, M, nch, grid;
 };
 
 __global__ void __launch_bounds__(256) small_prep_kernel(const PrepArgs a) {
@@ -340,7 +345,14 @@ __global__ void __launch_bounds__(256) small_prep_kernel(const PrepArgs a) {
     return;
   }
   b -= a.x_blocks;
-  for (size_t i = (size_t)b * 256 + t; i < a.y_n4; i += (size_t)a.y_blocks * 256)
+  size_t n0 = 0, n1 = a.y_n4;
+  if (a.y_tail) {
+    const SmallUnits su = small_units(a.gs, a.E, a.M, 1, a.nch, a.grid, 1);
+    if (su.halves == 1) return;
+    n0 = (size_t)small_block_row(a.gs, a.E, a.M, su.full) * (size_t)a.D / 4;
+    n1 = (size_t)small_block_row(a.gs, a.E, a.M, 1 << 30) * (size_t)a.D / 4;
+  }
+  for (size_t i = n0 + (size_t)b * 256 + t; i < n1; i += (size_t)a.y_blocks * 256)
     a.y[i] = make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
@@ -1108,6 +1120,11 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
   prm.status = status;
   prm.trace = reinterpret_cast<unsigned long long*>(g_tune_trace);
   prm.skip_tail = opt.skip_tail ? 1 : 0;
+  // Half units in a short last wave need their Y rows zeroed up front: only
+  // when the preparation launch runs anyway (F-splits zero all of Y; f32
+  // calls that split raw weights or X), so no launch is added for them.
+  const bool f32_prep = dtype == MOE_DTYPE_F32 && (split_weights || !plan.x_res);
+  prm.tail_halves = (!pair && g_tune_tail == 0 && (splits > 1 || f32_prep)) ? 1 : 0;
 
   FusedMaps maps;
   memset(&maps, 0, sizeof(maps));
@@ -1148,6 +1165,19 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
       pa.y = reinterpret_cast<float4*>(y);
       pa.y_n4 = (size_t)M * D / 4;
       pa.y_blocks = (int)std::min<size_t>((pa.y_n4 + 255) / 256, (size_t)cap);
+    } else if (prm.tail_halves && M > 0) {
+      // Half units (at most ctas / 2 blocks of 128 rows) reduce-add into
+      // rows zeroed here; the kernel recomputes the same plan.
+      pa.y = reinterpret_cast<float4*>(y);
+      pa.y_tail = 1;
+      pa.gs = gs;
+      pa.M = (int)M;
+      pa.D = D;
+      pa.E = E;
+      pa.nch = prm.chunks_per_split;
+      pa.grid = ctas;
+      const size_t max4 = (size_t)(ctas / 2) * 128 * D / 4;
+      pa.y_blocks = (int)std::min<size_t>((max4 + 255) / 256, (size_t)cap);
     }
     const int blocks = 2 * pa.w_blocks + pa.x_blocks + pa.y_blocks;
     if (blocks > 0) {
@@ -1390,6 +1420,10 @@ int moe_set_tuning(int32_t key, int64_t value) {
     case 8:
       if (value > 2) return fail(MOE_ERR_INVALID_ARG, "down-GEMM tile width choice must be 0, 1 or 2");
       g_tune_wide = value;
+      return 0;
+    case 10:
+      if (value > 1) return fail(MOE_ERR_INVALID_ARG, "tail-unit choice must be 0 or 1");
+      g_tune_tail = value;
       return 0;
   }
   return fail(MOE_ERR_INVALID_ARG, "unknown tuning key %d", key);

@@ -327,9 +327,19 @@ def _launch_model(L: dict, M: int, D: int, F: int, E: int, g: list[int], dtype: 
         xb = IN_BYTES[dtype] * (2 if dtype == "f32" and D > 128 else 1)  # D = 256 f32 streams X hi + lo planes
         ybytes = M * D * 4 * (2 if L["f_splits"] > 1 else 1)  # F-split CTAs add into Y (read + write)
         dram = routed * D * xb + active * 2 * D * F * wplanes + ybytes
-        out.update(units=units, rows_processed=rows_pad, padded_rows=rows_pad - routed,
-                   waves=units / L["grid"] if L["grid"] else 0.0,
-                   wave_efficiency=units / (math.ceil(units / L["grid"]) * L["grid"]) if units else 1.0,
+        # A last partial wave of at most grid / 2 units runs as half units
+        # (two CTAs per unit, half of its hidden chunks each): the makespan
+        # is the full waves plus half a unit.
+        G = L["grid"]
+        full = (units // G) * G if G else units
+        tail = units - full
+        nch = F // L["tile_n"] // max(L["f_splits"], 1) if L["tile_n"] else 0
+        halves = 2 if tail > 0 and 2 * tail <= G and nch % 2 == 0 else 1
+        makespan = full // G + (0.5 if halves == 2 else (1 if tail else 0)) if G else 0
+        out.update(units=full + tail * halves, half_units=tail * halves if halves == 2 else 0,
+                   rows_processed=rows_pad, padded_rows=rows_pad - routed,
+                   waves=units / G if G else 0.0,
+                   wave_efficiency=units / G / makespan if units and makespan else 1.0,
                    useful_flops=4 * routed * D * F, issued_f16_equiv_flops=issued, compulsory_dram_bytes=dram)
     elif name == "small_prep_kernel":
         wsplit = L["grid"] > 0 and dtype == "f32"

@@ -63,7 +63,7 @@ def _oracle_rows(x, w_up, w_down, gs, rows):
 
 
 def _reset():
-    for key in (1, 2, 4):
+    for key in (1, 2, 4, 10):
         _lib.set_tuning(key, 0)
 
 
@@ -160,6 +160,35 @@ def test_schedule_variants(dtype, splits, ctas, family):
     x, wu, wd = make_inputs_numpy(M, D, F, E, seed=11)
     y, x, wu, wd = _run(x, wu, wd, gs, dtype)
     _check(y, x, wu, wd, gs, dtype)
+
+
+def test_tail_half_units():
+    """A last wave of at most half the grid runs as half units: two CTAs
+    per 128-row block, each over half of F, reduce-adding into rows the
+    preparation launch zeroed (f32 with raw weights: that launch splits the
+    weights anyway).  Parity with the oracle on a NaN-poisoned output, the
+    same bits on every run (two partial sums onto zero), and agreement with
+    the whole-unit schedule (tuning key 10)."""
+    M, D, F, E = 1536, 128, 512, 3
+    gs = make_group_sizes_pattern(M, E, "skewed")
+    nb = int(sum((g + 127) // 128 for g in gs))
+    # the widest grid whose last wave holds 1 .. G/2 blocks; one F-split
+    # (with several, every unit reduce-adds and the order of the adds varies)
+    ctas = max(G for G in range(2, nb) if 0 < nb % G <= G // 2)
+    _lib.set_tuning(1, 1)
+    _lib.set_tuning(2, ctas)
+    x, wu, wd = make_inputs_numpy(M, D, F, E, seed=13)
+    runs = []
+    for _ in range(2):
+        out = torch.full((M, D), float("nan"), device="cuda:0")
+        y, xr, wur, wdr = _run(x, wu, wd, gs, "f32", out=out)
+        runs.append(y)
+    assert np.array_equal(runs[0], runs[1])
+    _check(runs[0], xr, wur, wdr, gs, "f32")
+    _lib.set_tuning(10, 1)
+    whole, *_ = _run(x, wu, wd, gs, "f32")
+    assert not np.array_equal(runs[0], whole)   # the half units did run
+    assert float(np.abs(runs[0] - whole).max()) <= 1e-5 * float(np.abs(whole).max())
 
 
 def test_negative_group_size_counts_as_zero():
