@@ -182,7 +182,7 @@ int moe_fused_mlp_prepared(const void* x, const void* w_up, const void* w_down, 
  * Limits: D in {64, 128}, F % 64 == 0, E * D * F <= 1,048,576 (else
  * MOE_ERR_WORKSPACE_TOO_SMALL, and moe_fused_mlp with a workspace is the way).
  * The first call on a device looks up the scratch array's device address
- * (cudaGetSymbolAddress), so make that first call before any stream capture.
+ * (cudaGetSymbolAddress, a host-side runtime call); later calls reuse it.
  * After cudaDeviceReset the next call looks it up again (the array is a new
  * allocation of the new context and starts with undefined contents).
  * All calls share the one array: calls that can overlap on the GPU (other
