@@ -307,6 +307,7 @@ struct PrepArgs {
   float *wd_hi, *wd_lo;  // W_down (E, F, D) -> planes (E, D, F)
   int D, F, E;
   int w_blocks;          // tiles per weight matrix
+  const int32_t* w_gs;   // group sizes: experts with no rows keep unsplit planes (no kernel reads them); null = all
   const float4* x;
   float4 *x_hi, *x_lo;
   size_t x_n4;
@@ -330,6 +331,7 @@ __global__ void __launch_bounds__(256) small_prep_kernel(const PrepArgs a) {
     const int R = down ? a.F : a.D, C = down ? a.D : a.F;
     const int tc = (C + 31) / 32, tr = (R + 31) / 32;
     const int e = b / (tr * tc), rem = b % (tr * tc);
+    if (a.w_gs && __ldg(a.w_gs + e) <= 0) return;
     split_transpose_tile(down ? a.wd : a.wu, down ? a.wd_hi : a.wu_hi, down ? a.wd_lo : a.wu_lo, R, C, e,
                          (rem % tc) * 32, (rem / tc) * 32, t & 31, t >> 5, tile);
     return;
@@ -528,6 +530,7 @@ static int run_large_tf32(const float* x, const float* w_up, const float* w_down
       pa.F = F;
       pa.E = E;
       pa.w_blocks = E * ((D + 31) / 32) * ((F + 31) / 32);
+      pa.w_gs = gs;
     }
     pa.x = reinterpret_cast<const float4*>(x);
     pa.x_hi = reinterpret_cast<float4*>(x_hi);
@@ -1153,6 +1156,7 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
       pa.F = F;
       pa.E = E;
       pa.w_blocks = E * ((D + 31) / 32) * ((F + 31) / 32);
+      pa.w_gs = gs;
     }
     if (f32 && !pair && !plan.x_res) {
       pa.x = static_cast<const float4*>(x);
