@@ -492,6 +492,9 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
                    "l2": "flushed before every step (256 MiB write)"},
         "useful_tflops": alg["flops"] * world / (ms_per_step / 1e3) / 1e12,
         "gpu_launches": launches_per_step * args.steps,
+        # per-step event times of the timed region (this rank's when N > 1), as the
+        # reference's sweep reports them: median with p10 / p90
+        "step_ms_percentiles": _percentiles(step_ms),
     }
     if rl is not None:
         k_avg = statistics.mean(rl["kern_ms"])
@@ -572,6 +575,15 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
 
 
 # --------------------------------------------------------------------- whole MoE layer (routing stage)
+def _percentiles(ms: list) -> dict:
+    """p10 / median / p90 (nearest rank), min and max of per-step times."""
+    v = sorted(ms)
+    if not v:
+        return {}
+    q = lambda f: v[min(len(v) - 1, max(0, math.ceil(f * len(v)) - 1))]  # noqa: E731
+    return {"p10": q(0.1), "p50": statistics.median(v), "p90": q(0.9), "min": v[0], "max": v[-1], "n": len(v)}
+
+
 def quick_config(cfg, steps: int, warmup: int, device) -> dict:
     """Device-resident figures of one more configuration on this GPU: the
     reference entry point (raw weights in, Y out) and the fused kernel(s)
@@ -630,7 +642,8 @@ def quick_config(cfg, steps: int, warmup: int, device) -> dict:
            "kernel_ms": k_ms, "bound": r["bound"], "achieved": r["achieved"], "roofline_unit": r["unit"],
            "frac": r["frac"], "sm_mhz_device": mhz,
            "frac_at_clock": (r["achieved"] / clk_peak if clk_peak and r["bound"] == "tensor" else None),
-           "steps": steps, "warmup": warmup}
+           "steps": steps, "warmup": warmup,
+           "step_ms_percentiles": _percentiles([a.elapsed_time(b) for a, b in s_ev])}
     del x, w_up, w_down, experts, y, ws, flush
     torch.cuda.empty_cache()
     return out
