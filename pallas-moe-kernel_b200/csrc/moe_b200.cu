@@ -349,10 +349,17 @@ __global__ void __launch_bounds__(256) small_prep_kernel(const PrepArgs a) {
   b -= a.x_blocks;
   size_t n0 = 0, n1 = a.y_n4;
   if (a.y_tail) {
-    const SmallUnits su = small_units(a.gs, a.E, a.M, 1, a.nch, a.grid, 1);
-    if (su.halves == 1) return;
-    n0 = (size_t)small_block_row(a.gs, a.E, a.M, su.full) * (size_t)a.D / 4;
-    n1 = (size_t)small_block_row(a.gs, a.E, a.M, 1 << 30) * (size_t)a.D / 4;
+    // One thread computes the plan's row range for the block (the branch is
+    // block-uniform, so the barrier is reached by every thread).
+    __shared__ unsigned long long range[2];
+    if (t == 0) {
+      const SmallUnits su = small_units(a.gs, a.E, a.M, 1, a.nch, a.grid, 1);
+      range[0] = su.halves == 1 ? 0 : (size_t)small_block_row(a.gs, a.E, a.M, su.full) * (size_t)a.D / 4;
+      range[1] = su.halves == 1 ? 0 : (size_t)small_block_row(a.gs, a.E, a.M, 1 << 30) * (size_t)a.D / 4;
+    }
+    __syncthreads();
+    n0 = range[0];
+    n1 = range[1];
   }
   for (size_t i = n0 + (size_t)b * 256 + t; i < n1; i += (size_t)a.y_blocks * 256)
     a.y[i] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -1181,7 +1188,7 @@ static int run_small(const void* x, const void* w_up, const void* w_down, const 
       pa.nch = prm.chunks_per_split;
       pa.grid = ctas;
       const size_t max4 = (size_t)(ctas / 2) * 128 * D / 4;
-      pa.y_blocks = (int)std::min<size_t>((max4 + 255) / 256, (size_t)cap);
+      pa.y_blocks = (int)std::min<size_t>((max4 + 2047) / 2048, (size_t)di->sms);  // ~8 float4 per thread
     }
     const int blocks = 2 * pa.w_blocks + pa.x_blocks + pa.y_blocks;
     if (blocks > 0) {
