@@ -115,35 +115,55 @@ __global__ void __launch_bounds__(kPermBlock) perm_hist_kernel(const int32_t* __
   for (int e = threadIdx.x; e < E; e += blockDim.x) block_hist[(int64_t)blockIdx.x * E + e] = s_h[e];
 }
 
-// One CTA: thread e walks the blocks of expert e (block_hist becomes each
-// block's first sorted row of expert e); then an exclusive scan over experts
-// places the experts.
+// One CTA of 32 warps; warp w owns experts w, w + 32, ...  block_hist[b][e]
+// holds block b's entry count for expert e and becomes the block's first
+// sorted row of expert e: the experts' exclusive offset plus the exclusive
+// prefix over earlier blocks.  Pass 1 sums each expert's column (warp
+// reduction), one warp scans the totals over experts, pass 2 scans each
+// column in chunks of 32 blocks (warp-wide inclusive scan, carried across
+// chunks), so every load of a chunk is in flight at once.
+__device__ __forceinline__ int warp_inclusive_scan(int v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += t;
+  }
+  return v;
+}
 __global__ void __launch_bounds__(1024) perm_scan_kernel(int32_t* __restrict__ block_hist, int64_t nblocks, int E,
                                                          int32_t* __restrict__ group_sizes) {
   __shared__ int s_base[kRouteMaxExperts];
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    int run = 0;
-    for (int64_t b = 0; b < nblocks; ++b) {
-      const int c = block_hist[b * E + e];
-      block_hist[b * E + e] = run;
-      run += c;
-    }
-    group_sizes[e] = run;
-    s_base[e] = run;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int run = 0;
-    for (int e = 0; e < E; ++e) {
-      const int c = s_base[e];
-      s_base[e] = run;
-      run += c;
+  const int lane = (int)(threadIdx.x & 31u), warp = (int)(threadIdx.x >> 5), nw = (int)(blockDim.x >> 5);
+  for (int e = warp; e < E; e += nw) {
+    int sum = 0;
+    for (int64_t b = lane; b < nblocks; b += 32) sum += block_hist[b * E + e];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) {
+      s_base[e] = sum;
+      group_sizes[e] = sum;
     }
   }
   __syncthreads();
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    const int base = s_base[e];
-    for (int64_t b = 0; b < nblocks; ++b) block_hist[b * E + e] += base;
+  if (warp == 0) {
+    int carry = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int v = e0 + lane < E ? s_base[e0 + lane] : 0;
+      const int inc = warp_inclusive_scan(v, lane);
+      if (e0 + lane < E) s_base[e0 + lane] = carry + inc - v;
+      carry += __shfl_sync(0xffffffffu, inc, 31);
+    }
+  }
+  __syncthreads();
+  for (int e = warp; e < E; e += nw) {
+    int carry = s_base[e];
+    for (int64_t b0 = 0; b0 < nblocks; b0 += 32) {
+      const int64_t b = b0 + lane;
+      const int v = b < nblocks ? block_hist[b * E + e] : 0;
+      const int inc = warp_inclusive_scan(v, lane);
+      if (b < nblocks) block_hist[b * E + e] = carry + inc - v;
+      carry += __shfl_sync(0xffffffffu, inc, 31);
+    }
   }
 }
 
