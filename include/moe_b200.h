@@ -102,7 +102,7 @@ int moe_fused_mlp_launch_count(int64_t M, int32_t D, int32_t F, int32_t E, int32
 enum {
   MOE_MMA_NONE = 0,    /* no tensor-core work (conversion / split launches) */
   MOE_MMA_BF16 = 1,    /* tcgen05 kind::f16 on bf16 operands */
-  MOE_MMA_F16 = 2,     /* tcgen05 kind::f16 on f16 operands (e4m3 weights decoded in shared memory) */
+  MOE_MMA_BF16_E4M3 = 2, /* tcgen05 kind::f16 on bf16 operands, e4m3 weights decoded to bf16 in shared memory */
   MOE_MMA_TF32X3 = 3   /* tcgen05 kind::tf32, three products per f32 product */
 };
 typedef struct moe_launch_desc {
@@ -332,8 +332,8 @@ int moe_fused_mlp_swiglu(const void* x, const void* w_gate_up, const void* w_dow
  *                  block, then the up block of the same columns).
  * moe_fused_mlp_swiglu_fp8   y (M, D) f32 from x, w_gate_up / s_gate_up and
  *                  w_down (E, F, D) e4m3 / s_down (E, F/128, D/128); workspace
- *                  moe_fused_mlp_swiglu_fp8_workspace_size bytes (H and X in
- *                  f16), 256-byte aligned.
+ *                  moe_fused_mlp_swiglu_fp8_workspace_size bytes (H in bf16),
+ *                  256-byte aligned.
  */
 int moe_swiglu_interleave_fp8(const void* w_gate, const void* w_up, const float* s_gate, const float* s_up,
                               void* w_gate_up, float* s_gate_up, int32_t E, int32_t D, int32_t F, void* stream);

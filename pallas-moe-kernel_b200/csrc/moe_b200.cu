@@ -377,8 +377,8 @@ static bool large_supported(int D, int F, int dtype) {
 }
 static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-// Large-D workspace.  bf16: H (M, F) bf16.  e4m3 weights: H (M, F) f16, then
-// X (M, D) f16.  f32 (3xTF32): the tf32 hi/lo planes of W_up^T (E, F, D) and
+// Large-D workspace.  bf16 and e4m3 weights: H (M, F) bf16.  f32 (3xTF32):
+// the tf32 hi/lo planes of W_up^T (E, F, D) and
 // W_down^T (E, D, F) -- the layout moe_prepare_weights writes -- then X hi/lo
 // (M, D) and H hi/lo (M, F), all f32.
 struct Tf32LargeLayout {
@@ -402,21 +402,7 @@ static Tf32LargeLayout tf32_large_layout(int64_t M, int D, int F, int E) {
 }
 static size_t large_ws_bytes(int64_t M, int D, int F, int E, int dtype) {
   if (dtype == MOE_DTYPE_F32) return tf32_large_layout(M, D, F, E).total;
-  const size_t h = align256((size_t)M * F * 2);
-  return dtype == MOE_DTYPE_FP8_E4M3_BLK128 ? h + (size_t)M * D * 2 : h;
-}
-
-// bf16 -> f16 (8 values per thread step), saturating at +-65504: the f16
-// operand of the e4m3-weight GEMMs.  Exact for every bf16 value in f16 range
-// (down to f16's subnormals).
-__global__ void bf16_to_f16_kernel(const uint4* __restrict__ x, uint4* __restrict__ out, size_t n8) {
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (size_t)gridDim.x * blockDim.x) {
-    const uint4 v = x[i];
-    auto cvt = [](uint32_t w) {
-      return pack_f16x2_sat(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
-    };
-    out[i] = make_uint4(cvt(v.x), cvt(v.y), cvt(v.z), cvt(v.w));
-  }
+  return align256((size_t)M * F * 2);  // H (bf16; also with e4m3 weights)
 }
 
 template <int EPI, bool BFP8, bool TF32 = false, int WIDE = 1>
@@ -590,20 +576,11 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
     return fail(MOE_ERR_INVALID_ARG, "FP8 weights need w_up_scale and w_down_scale");
   int* status = di->status;
   const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  const auto F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const auto U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
-  // e4m3 weights: the GEMMs run on f16 operands; X is converted once.
-  const auto A16 = fp8 ? F16 : BF16;
+  // e4m3 weights: the GEMMs run on bf16 operands (the weights decoded to
+  // bf16 in shared memory), so X is read as given.
+  const auto A16 = BF16;
   const void* xa = x;
-  if (fp8) {
-    if (reinterpret_cast<uintptr_t>(x) & 15u) return fail(MOE_ERR_MISALIGNED, "x must be 16-byte aligned");
-    void* x16 = static_cast<uint8_t*>(ws) + align256((size_t)M * F * 2);
-    const size_t n8 = (size_t)M * D / 8;
-    const int blocks = (int)std::min<size_t>((n8 + 255) / 256, (size_t)di->sms * 8);
-    bf16_to_f16_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint4*>(x), static_cast<uint4*>(x16), n8);
-    MOE_CUDA_TRY(cudaGetLastError());
-    xa = x16;
-  }
   // Small experts with e4m3 weights: expert super-tiles (grouped_gemm_swap.cuh),
   // unless the down GEMM must store Y rows into their source ranks.
   const bool swap = fp8 && !opt.scatter && fp8_use_swap(M, E);
@@ -611,9 +588,9 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
     // Token rows in 32-, 64- and 128-row boxes; e4m3 weights {128, 64, 1}.
     auto swap_maps = [&](SwapMaps* m, const void* rows, int K, const void* w, int N) -> int {
       memset(m, 0, sizeof(*m));
-      if (int r = make_map_2d(&m->x32, rows, F16, 2, (uint64_t)M, K, 64, 32)) return r;
-      if (int r = make_map_2d(&m->x64, rows, F16, 2, (uint64_t)M, K, 64, 64)) return r;
-      if (int r = make_map_2d(&m->x128, rows, F16, 2, (uint64_t)M, K, 64, 128)) return r;
+      if (int r = make_map_2d(&m->x32, rows, BF16, 2, (uint64_t)M, K, 64, 32)) return r;
+      if (int r = make_map_2d(&m->x64, rows, BF16, 2, (uint64_t)M, K, 64, 64)) return r;
+      if (int r = make_map_2d(&m->x128, rows, BF16, 2, (uint64_t)M, K, 64, 128)) return r;
       return make_map_3d(&m->w, w, U8, 1, (uint64_t)E, K, N, 128, 64);
     };
     SwapMaps s1, s2;
@@ -902,12 +879,14 @@ __global__ void swiglu_interleave_scales_kernel(const float* __restrict__ gate, 
 static bool swiglu_supported(int D, int F) { return D >= 256 && D % 256 == 0 && F % 128 == 0; }
 
 static size_t swiglu_ws_bytes(int64_t M, int D, int F, bool fp8) {
-  return align256((size_t)M * F * 2) + (fp8 ? align256((size_t)M * D * 2) : 0);
+  (void)D;
+  (void)fp8;
+  return align256((size_t)M * F * 2);  // H (bf16; also with e4m3 weights)
 }
 
 // SwiGLU experts on the two grouped GEMMs.  e4m3 weights (fp8): block
 // scales s_gu (E, D/128, 2F/128) interleaved like the weights and s_down
-// (E, F/128, D/128); the GEMMs run on f16 operands, X converted once.
+// (E, F/128, D/128); the GEMMs run on bf16 operands (weights decoded to bf16).
 static int run_swiglu(const void* x, const void* w_gu, const void* w_down, const float* s_gu, const float* s_down,
                       const int32_t* gs, float* y, int64_t M, int D, int F, int E, bool fp8, void* ws,
                       size_t ws_bytes, cudaStream_t st) {
@@ -919,19 +898,10 @@ static int run_swiglu(const void* x, const void* w_gu, const void* w_down, const
   if (reinterpret_cast<uintptr_t>(ws) & 255u) return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
   int* status = di->status;
   const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  const auto A16 = fp8 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : BF16;
+  const auto A16 = BF16;  // e4m3 weights are decoded to bf16: X is read as given
   const auto U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const int ctas = (int)g_tune_ctas;
   const void* xa = x;
-  if (fp8) {
-    if (reinterpret_cast<uintptr_t>(x) & 15u) return fail(MOE_ERR_MISALIGNED, "x must be 16-byte aligned");
-    void* x16 = static_cast<uint8_t*>(ws) + align256((size_t)M * F * 2);
-    const size_t n8 = (size_t)M * D / 8;
-    const int blocks = (int)std::min<size_t>((n8 + 255) / 256, (size_t)di->sms * 8);
-    bf16_to_f16_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint4*>(x), static_cast<uint4*>(x16), n8);
-    MOE_CUDA_TRY(cudaGetLastError());
-    xa = x16;
-  }
   // up: H = SiLU(X @ W_gate[e]) * (X @ W_up[e]) over the interleaved (E*D, 2F) weights
   GemmMaps m1;
   memset(&m1, 0, sizeof(m1));
@@ -1355,8 +1325,8 @@ static void ep_release(moe_ep_s* ep) {
 static_assert(kEpMaxWorld == 8, "EpScatter holds 8 peer buffers");
 
 static int ep_mlp_launches(const moe_ep_s* ep) {
-  if (!small_supported(ep->D, ep->F, ep->dtype))                   // (X -> f16 +) up + down grouped GEMMs
-    return ep->dtype == MOE_DTYPE_FP8_E4M3_BLK128 ? 3 : 2;
+  if (!small_supported(ep->D, ep->F, ep->dtype))                   // up + down grouped GEMMs
+    return 2;
   return (ep->dtype == MOE_DTYPE_F32 && ep->D == 256) ? 2 : 1;   // (+ X split) fused kernel
 }
 
@@ -2092,8 +2062,8 @@ int moe_fused_mlp_launch_count(int64_t M, int32_t D, int32_t F, int32_t E, int32
   if (M == 0) return 0;
   if (!small_supported(D, F, dtype)) {
     if (!large_supported(D, F, dtype)) return fail(MOE_ERR_UNSUPPORTED_SHAPE, "D=%d F=%d dtype=%d", D, F, dtype);
-    // bf16: up GEMM, down GEMM; e4m3: X -> f16 first; f32: the tf32 split first
-    return dtype == MOE_DTYPE_BF16 ? 2 : 3;
+    // bf16 and e4m3 weights: up GEMM, down GEMM; f32: the tf32 split first
+    return dtype == MOE_DTYPE_F32 ? 3 : 2;
   }
   int dev;
   DevInfo* di;
@@ -2131,14 +2101,14 @@ template <int EPI, bool BFP8, bool TF32, int WIDE = 1>
 static void desc_gemm(moe_launch_desc* d, const char* name, int pairs, int N, int K) {
   using C = GemmCfg<EPI, BFP8, TF32, WIDE>;
   desc_set(d, name, 2 * pairs, C::THREADS, C::SMEM, C::TMEM_COLS, 2, 2 * C::BM, C::TILE_N, C::BK, C::NS,
-           TF32 ? MOE_MMA_TF32X3 : (BFP8 ? MOE_MMA_F16 : MOE_MMA_BF16), N, K, 1, (int)C::NACC);
+           TF32 ? MOE_MMA_TF32X3 : (BFP8 ? MOE_MMA_BF16_E4M3 : MOE_MMA_BF16), N, K, 1, (int)C::NACC);
 }
 // Super-tile kernel: tile_m = tokens per super-tile, tile_n = features per tile.
 template <int EPI>
 static void desc_swap(moe_launch_desc* d, const char* name, int pairs, int N, int K) {
   using C = SwapCfg<EPI>;
   desc_set(d, name, 2 * pairs, C::THREADS, C::SMEM, C::TMEM_COLS, 2, C::TOKENS, 2 * C::FM, C::BK, C::NS,
-           MOE_MMA_F16, N, K, 1, 2);
+           MOE_MMA_BF16_E4M3, N, K, 1, 2);
 }
 template <int MODE, int D, int BF, bool XR>
 static void desc_small(moe_launch_desc* d, int ctas, int F, int splits) {
@@ -2257,8 +2227,6 @@ int moe_describe_plan(int64_t M, int32_t D, int32_t F, int32_t E, int32_t dtype,
       desc_gemm<0, false, true>(&d[n++], "grouped_gemm_pair_kernel (up)", pairs, F, D);
       desc_gemm<1, false, true>(&d[n++], "grouped_gemm_pair_kernel (down)", pairs, D, F);
     } else if (dtype == MOE_DTYPE_FP8_E4M3_BLK128) {
-      const int xb = (int)std::min<int64_t>(((int64_t)M * D / 8 + 255) / 256, (int64_t)sms * 8);
-      desc_set(&d[n++], "bf16_to_f16_kernel", xb, 256, 0, 0, 1, 0, 0, 0, 0, MOE_MMA_NONE, 0, 0, 1, 0);
       if (fp8_use_swap(M, E)) {
         desc_swap<0>(&d[n++], "grouped_gemm_swap_kernel (up)", pairs, F, D);
         desc_swap<1>(&d[n++], "grouped_gemm_swap_kernel (down)", pairs, D, F);

@@ -346,8 +346,6 @@ def _launch_model(L: dict, M: int, D: int, F: int, E: int, g: list[int], dtype: 
         # weight split of the experts with rows: read W, write hi + lo (12 B per element)
         out.update(units=L["grid"], useful_flops=0, issued_f16_equiv_flops=0,
                    compulsory_dram_bytes=(active * 2 * D * F * 12 if wsplit else 0))
-    elif name == "bf16_to_f16_kernel":
-        out.update(units=L["grid"], useful_flops=0, issued_f16_equiv_flops=0, compulsory_dram_bytes=M * D * 4)
     out["smem_fraction"] = L["smem_bytes"] / SMEM_LIMIT
     out["tmem_fraction"] = L["tmem_cols"] / TMEM_COLS
     return out

@@ -88,8 +88,7 @@ class ExpertParallelMLP:
                     return self._experts(xr, gs)
                 finally:
                     _lib.set_tuning(2, 0)
-            fp8 = w_up_local.dtype == torch.float8_e4m3fn
-            self.launches_per_wave = (3 if fp8 else 2) if w_up_local.shape[1] > 256 else 1
+            self.launches_per_wave = 2 if w_up_local.shape[1] > 256 else 1
         else:
             self.launches_per_wave = 0
         self.expert_fn = expert_fn

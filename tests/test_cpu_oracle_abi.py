@@ -192,14 +192,15 @@ def test_launch_count_host_side():
     assert L.moe_fused_mlp_launch_count(0, 128, 512, 8, 0) == 0
     assert L.moe_fused_mlp_launch_count(-1, 128, 512, 8, 0) == -1
     assert L.moe_fused_mlp_launch_count(16, 128, 512, 8, 9) == -1
-    # Two grouped GEMMs for bf16 large D, plus the X conversion for e4m3
-    # weights, or the tf32 split for f32 outside the fused small-D kernels.
+    # Two grouped GEMMs for bf16 large D and for e4m3 weights (decoded in
+    # shared memory), plus the tf32 split for f32 outside the fused small-D
+    # kernels.
     assert L.moe_fused_mlp_launch_count(32768, 4096, 14336, 8, 1) == 2
-    assert L.moe_fused_mlp_launch_count(65536, 7168, 2048, 256, 2) == 3
+    assert L.moe_fused_mlp_launch_count(65536, 7168, 2048, 256, 2) == 2
     assert L.moe_fused_mlp_launch_count(16, 384, 512, 8, 1) == 2
     assert L.moe_fused_mlp_launch_count(16, 320, 448, 4, 1) == 2
     assert L.moe_fused_mlp_launch_count(16, 512, 512, 4, 0) == 3
-    assert L.moe_fused_mlp_launch_count(16, 320, 448, 4, 2) == 3
+    assert L.moe_fused_mlp_launch_count(16, 320, 448, 4, 2) == 2
     # Rows that do not start on 16-byte boundaries have no kernel (TMA).
     assert L.moe_fused_mlp_launch_count(16, 100, 512, 8, 1) == -2
     assert L.moe_fused_mlp_launch_count(16, 130, 512, 8, 0) == -2

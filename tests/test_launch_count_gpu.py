@@ -33,7 +33,7 @@ def _library_kernels(fn) -> list[str]:
     (16384, 128, 512, 4, "bf16"),    # one wave of whole blocks: the fused kernel alone
     (512, 128, 512, 4, "bf16"),      # F split across CTAs: Y zeroed first
     (1024, 512, 1024, 4, "bf16"),    # two grouped GEMMs
-    (1024, 512, 1024, 4, "fp8"),     # X to f16 + two grouped GEMMs
+    (1024, 512, 1024, 4, "fp8"),     # two grouped GEMMs (weights decoded in shared memory)
     (1024, 320, 448, 4, "f32"),      # tf32 split + two 3xTF32 grouped GEMMs
 ])
 def test_launch_count_matches_launched_kernels(M, D, F, E, dt):
