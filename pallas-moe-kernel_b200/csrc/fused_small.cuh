@@ -83,13 +83,43 @@ __device__ __forceinline__ int small_block_count(const int32_t* gs, int E, int M
   }
   return nb;
 }
-__device__ __forceinline__ SmallUnits small_units(const int32_t* gs, int E, int M, int splits, int nch, int grid,
-                                                  int tail_halves) {
-  const int u0 = small_block_count(gs, E, M) * splits;
+// The same count by a whole warp: 32 group sizes per load, the running total
+// (clamped at M) from a warp scan -- one memory round trip per 32 experts
+// instead of one per expert.  Every lane returns the count.
+__device__ __forceinline__ int small_block_count_warp(const int32_t* gs, int E, int M, uint32_t lane) {
+  int nb = 0;
+  long long row = 0;  // unclamped running total of the earlier experts
+  for (int e0 = 0; e0 < E; e0 += 32) {
+    int g = e0 + (int)lane < E ? __ldg(gs + e0 + lane) : 0;
+    g = g < 0 ? 0 : (g > M ? M : g);
+    long long incl = g;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long t = __shfl_up_sync(0xffffffffu, incl, o);
+      if ((int)lane >= o) incl += t;
+    }
+    // clamping the running total at M (as BlockCursorT does) leaves M - prefix
+    // rows for this expert, at least 0
+    const long long rem = (long long)M - (row + incl - g);
+    const int gc = (long long)g > rem ? (rem > 0 ? (int)rem : 0) : g;
+    int n = (gc + 127) >> 7;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+    nb += n;
+    row += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  return nb;
+}
+__device__ __forceinline__ SmallUnits small_units_from(int nb, int splits, int nch, int grid, int tail_halves) {
+  const int u0 = nb * splits;
   const int full = (u0 / grid) * grid;
   const int tail = u0 - full;
   if (tail_halves && tail > 0 && 2 * tail <= grid && nch % 2 == 0) return {full, 2};
   return {u0, 1};
+}
+__device__ __forceinline__ SmallUnits small_units(const int32_t* gs, int E, int M, int splits, int nch, int grid,
+                                                  int tail_halves) {
+  return small_units_from(small_block_count(gs, E, M), splits, nch, grid, tail_halves);
 }
 // First row of global 128-row block `block`; the routed row count when the
 // block is past the last one.
@@ -292,11 +322,15 @@ __global__ void __launch_bounds__(64 + 256, 1)
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
 
+  if (warp == 0) {
+    const int nb = small_block_count_warp(p.group_sizes, p.E, p.M, lane);
+    if (lane == 0) {
+      const SmallUnits su0 = small_units_from(nb, p.splits, p.chunks_per_split, (int)gridDim.x, p.tail_halves);
+      plan_smem[0] = su0.full;
+      plan_smem[1] = su0.halves;
+    }
+  }
   if (threadIdx.x == 0) {
-    const SmallUnits su0 = small_units(p.group_sizes, p.E, p.M, p.splits, p.chunks_per_split, (int)gridDim.x,
-                                       p.tail_halves);
-    plan_smem[0] = su0.full;
-    plan_smem[1] = su0.halves;
     for (int i = 0; i < C::NS; ++i) {
       mbar_init(full + i, 1);
       mbar_init(empty + i, 1);
@@ -373,14 +407,6 @@ __global__ void __launch_bounds__(64 + 256, 1)
           mbar_arrive_expect_tx(x_full, C::X_PLANE);
           for (int s = 0; s < D / C::ATOM; ++s)
             tma_load_2d(xbuf + s * C::XBOX, &maps.x[0], x_full, s * C::ATOM, row0);
-          // Warm L2 with the next unit's X tile so its load at the end of this
-          // unit does not wait on HBM.
-          BlockCursor nxt = cur;
-          const int gb_next = unit_work(u + (int)gridDim.x, su, S, NCH, atomic_all).gb;
-          if (nxt.seek(gb_next, p.group_sizes, p.E, p.M)) {
-            const int nrow0 = nxt.row_begin + (gb_next - nxt.blk_begin) * C::BM;
-            for (int s = 0; s < D / C::ATOM; ++s) tma_prefetch_l2_2d(&maps.x[0], s * C::ATOM, nrow0);
-          }
         }
         auto load_s1 = [&](int j, int s) -> bool {
           if (!next_stage()) return false;
@@ -431,6 +457,19 @@ __global__ void __launch_bounds__(64 + 256, 1)
           for (int s = 0; s < C::N1 && ok; ++s) ok = load_s1(j, s);
           if (j > 0)
             for (int t = 0; t < C::N2 && ok; ++t) ok = load_s2(j - 1, t);
+          if constexpr (X_RES) {
+            // Warm L2 with the next unit's X tile so that its load at the end
+            // of this unit does not wait on HBM.  Issued after the unit's
+            // first stages: finding the next unit walks the group sizes.
+            if (j == 0 && ok) {
+              BlockCursor nxt = cur;
+              const int gb_next = unit_work(u + (int)gridDim.x, su, S, NCH, atomic_all).gb;
+              if (nxt.seek(gb_next, p.group_sizes, p.E, p.M)) {
+                const int nrow0 = nxt.row_begin + (gb_next - nxt.blk_begin) * C::BM;
+                for (int s = 0; s < D / C::ATOM; ++s) tma_prefetch_l2_2d(&maps.x[0], s * C::ATOM, nrow0);
+              }
+            }
+          }
         }
         for (int t = 0; t < C::N2 && ok; ++t) ok = load_s2(nch - 1, t);
       }
