@@ -103,7 +103,8 @@ enum {
   MOE_MMA_NONE = 0,    /* no tensor-core work (conversion / split launches) */
   MOE_MMA_BF16 = 1,    /* tcgen05 kind::f16 on bf16 operands */
   MOE_MMA_BF16_E4M3 = 2, /* tcgen05 kind::f16 on bf16 operands, e4m3 weights decoded to bf16 in shared memory */
-  MOE_MMA_TF32X3 = 3   /* tcgen05 kind::tf32, three products per f32 product */
+  MOE_MMA_TF32X3 = 3,  /* tcgen05 kind::tf32, three products per f32 product */
+  MOE_MMA_F16_E4M3 = 4 /* tcgen05 kind::f16 on f16 operands, e4m3 weights decoded to f16 (down GEMM: f16 H) */
 };
 typedef struct moe_launch_desc {
   char kernel[48];       /* kernel family */
@@ -332,7 +333,7 @@ int moe_fused_mlp_swiglu(const void* x, const void* w_gate_up, const void* w_dow
  *                  block, then the up block of the same columns).
  * moe_fused_mlp_swiglu_fp8   y (M, D) f32 from x, w_gate_up / s_gate_up and
  *                  w_down (E, F, D) e4m3 / s_down (E, F/128, D/128); workspace
- *                  moe_fused_mlp_swiglu_fp8_workspace_size bytes (H in bf16),
+ *                  moe_fused_mlp_swiglu_fp8_workspace_size bytes (H in f16),
  *                  256-byte aligned.
  */
 int moe_swiglu_interleave_fp8(const void* w_gate, const void* w_up, const float* s_gate, const float* s_up,

@@ -158,10 +158,13 @@ struct GemmCfg {
   // rather than 3K/8 (each accumulate step into TMEM truncates, an error that
   // grows with the number of steps), at the cost of that overlap.
   static constexpr uint32_t NACC = (TF32 || WIDE == 2) ? 1 : 2;
-  // e4m3 weights run as bf16 operands (bf16 X as given, bf16 H, bf16 dequantised B).
+  // e4m3 weights: the up GEMM runs on bf16 operands (the caller's X, weights
+  // decoded to bf16) and stores H in f16; the down GEMM runs on f16 operands
+  // (H, weights decoded to f16 with a shorter decode).
+  static constexpr bool DEC_F16 = BFP8 && EPI == 1;
   // 16-bit B is read MN-major (the weights' own layout); tf32 B is K-major.
   static constexpr uint32_t IDESC = TF32 ? make_idesc(kFmtTF32, 256, BN, 0, 0)
-                                         : make_idesc(kFmtBF16, 256, BN, 0, 1);
+                                         : make_idesc(DEC_F16 ? kFmtF16 : kFmtBF16, 256, BN, 0, 1);
   static constexpr uint32_t TX = 2 * STAGE;                // both CTAs (bf16 or tf32 B)
   static constexpr uint32_t TX_A = 2 * A_BYTES;            // both CTAs' A (FP8 B arrives converted)
   static constexpr int RAW_WARP = 2 + EPI_WARPS + CVT_WARPS;  // FP8: producer of the raw ring
@@ -203,6 +206,38 @@ __device__ __forceinline__ uint2 e4m3x4_to_bf16x4(uint32_t v, float s) {
       : "r"(h23));
   return make_uint2(pack_bf16x2(a0 * s, a1 * s), pack_bf16x2(a2 * s, a3 * s));
 }
+
+// Four e4m3 values -> four f16 (two f16x2 words) times the block scale s2
+// (an f16x2 pair).  e4m3 values are exact in f16, so the multiply's rounding
+// is the only one; decode and multiply are one instruction per pair each.
+__device__ __forceinline__ uint2 e4m3x4_to_f16x4(uint32_t v, uint32_t s2) {
+  uint32_t h01, h23;
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, lo;\n\tcvt.rn.f16x2.e4m3x2 %1, hi;\n\t}"
+      : "=r"(h01), "=r"(h23)
+      : "r"(v));
+  asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(h01) : "r"(s2));
+  asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(h23) : "r"(s2));
+  return make_uint2(h01, h23);
+}
+
+// Block scale of one K step in the form the decoder of the GEMM takes, and
+// the decode of four e4m3 values with it: f16 operands (the down GEMM: its A
+// operand is H, which the up GEMM stores in f16) or bf16 operands (the up
+// GEMM, whose A operand is the caller's bf16 X).
+template <bool F16>
+struct E4m3Decoder {
+  uint32_t s2;
+  float sf;
+  __device__ __forceinline__ explicit E4m3Decoder(float scale) {
+    if constexpr (F16) s2 = pack_f16x2_sat(scale, scale);
+    else sf = scale;
+  }
+  __device__ __forceinline__ uint2 operator()(uint32_t v) const {
+    if constexpr (F16) return e4m3x4_to_f16x4(v, s2);
+    else return e4m3x4_to_bf16x4(v, sf);
+  }
+};
 
 // Power-of-two exponent k of an FP8 tile: 2^k brings the largest block scale
 // of the tile's two 128-column blocks (over all of K) into [1, 2), so the
@@ -554,7 +589,7 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32, WIDE>::LAUNCH_BOUND, 
         const int kblk = (kb * C::BK) / 128;
         const float s_reg = __shfl_sync(0xffffffffu, kblk < 32 ? s_lo : s_hi, kblk & 31);
         const float sc = kblk < 64 ? s_reg : (col_in ? __ldg(srow + (size_t)kblk * nnb_scale) : 0.f);
-        const float s2 = sc * up;
+        const E4m3Decoder<C::DEC_F16> dec(sc * up);
         const uint8_t* src = rawring + rs * C::B8_BYTES + r * 128;             // 128-byte swizzled raw row
         uint8_t* dst = ring + stage * C::STAGE + C::A_BYTES + h * (64 * 128) + r * 128;  // atom h, row r
         const int rsw = r & 7;
@@ -562,8 +597,8 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32, WIDE>::LAUNCH_BOUND, 
         for (int c = 0; c < 4; ++c) {
           const int chunk = 4 * h + c;  // 16 raw bytes = columns 16*chunk .. +15
           const uint4 v = *reinterpret_cast<const uint4*>(src + ((chunk ^ rsw) << 4));
-          const uint2 b0 = e4m3x4_to_bf16x4(v.x, s2), b1 = e4m3x4_to_bf16x4(v.y, s2);
-          const uint2 b2 = e4m3x4_to_bf16x4(v.z, s2), b3 = e4m3x4_to_bf16x4(v.w, s2);
+          const uint2 b0 = dec(v.x), b1 = dec(v.y);
+          const uint2 b2 = dec(v.z), b3 = dec(v.w);
           const int j0 = 2 * c, j1 = 2 * c + 1;  // output 16-byte chunks in the atom row
           *reinterpret_cast<uint4*>(dst + ((j0 ^ rsw) << 4)) = make_uint4(b0.x, b0.y, b1.x, b1.y);
           *reinterpret_cast<uint4*>(dst + ((j1 ^ rsw) << 4)) = make_uint4(b2.x, b2.y, b3.x, b3.y);
@@ -723,10 +758,10 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32, WIDE>::LAUNCH_BOUND, 
 #pragma unroll
               for (int k = 0; k < 4; ++k) {
                 uint4 w;
-                w.x = pack_bf16x2(g(8 * k + 0), g(8 * k + 1));
-                w.y = pack_bf16x2(g(8 * k + 2), g(8 * k + 3));
-                w.z = pack_bf16x2(g(8 * k + 4), g(8 * k + 5));
-                w.w = pack_bf16x2(g(8 * k + 6), g(8 * k + 7));
+                w.x = pack_f16x2_sat(g(8 * k + 0), g(8 * k + 1));
+                w.y = pack_f16x2_sat(g(8 * k + 2), g(8 * k + 3));
+                w.z = pack_f16x2_sat(g(8 * k + 4), g(8 * k + 5));
+                w.w = pack_f16x2_sat(g(8 * k + 6), g(8 * k + 7));
                 srow[(4 * hh + k) ^ (lane & 7)] = w;
               }
             }
@@ -797,11 +832,11 @@ __global__ void __launch_bounds__(GemmCfg<EPI, BFP8, TF32, WIDE>::LAUNCH_BOUND, 
             tmem_ld32(acc + C::BN / 2 + c0 + 32 * hh, u);
             tmem_ld_wait();
             // e4m3 weights: the tile was accumulated with weights scaled by
-            // 2^k (mul = 2^-k); H is the bf16 operand of the down GEMM.
+            // 2^k (mul = 2^-k); H is the f16 operand of the down GEMM.
             auto h = [&](int i) {
               return silu_fast(__uint_as_float(g[i]) * mul) * (__uint_as_float(u[i]) * mul);
             };
-            auto pk = [&](float a, float b) { return pack_bf16x2(a, b); };
+            auto pk = [&](float a, float b) { return BFP8 ? pack_f16x2_sat(a, b) : pack_bf16x2(a, b); };
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               uint4 w;

@@ -9,7 +9,7 @@
 //   out^T[features, tokens] = W^T[features, K] . X^T[K, tokens]
 //
 // with the decoded weights as the MMA's A operand (M = 256 features over the
-// CTA pair, MN-major: the weights' own layout, the same bf16 tile the
+// CTA pair, MN-major: the weights' own layout, the same 16-bit tile the
 // converters already produce) and the expert's tokens as B (K-major rows of X
 // or H), N = the token count rounded up to 32.  A super-tile holds up to 384
 // tokens in two chunks (N <= 256 and N <= 128): each decoded weight stage
@@ -24,7 +24,7 @@
 //
 // Warp roles as in grouped_gemm_pair_kernel with e4m3 weights: warp 0 TMA
 // producer of X rows (both CTAs), warp 1 TMEM owner + MMA issuer (leader),
-// warps 2..5 epilogue, warps 6..13 converters (e4m3 -> bf16, two groups on
+// warps 2..5 epilogue, warps 6..13 converters (e4m3 -> bf16 / f16, two groups on
 // alternate K steps), warp 14 producer of the raw e4m3 ring.
 //
 // Token rows arrive in as few TMA boxes as possible (one 128-row box for a
@@ -38,7 +38,7 @@
 namespace moe {
 
 // Tensor maps of the super-tile kernel: the token rows (X, or H for the down
-// GEMM) as [M, K] bf16 with 32-, 64- and 128-row boxes of one 128-byte swizzle
+// GEMM) as [M, K] 16-bit rows (bf16 X, f16 H) with 32-, 64- and 128-row boxes of one 128-byte swizzle
 // row each, and the e4m3 weights as [E][K][N] bytes, box {128, 64, 1}.
 struct SwapMaps {
   CUtensorMap x32, x64, x128;
@@ -49,7 +49,7 @@ template <int EPI>
 struct SwapCfg {
   static_assert(EPI == 0 || EPI == 1, "GELU -> H or f32 Y");
   static constexpr int FM = 128;                     // features per CTA (MMA M = 256 per pair)
-  static constexpr int BK = 64;                      // K per stage (one 128-byte bf16 row)
+  static constexpr int BK = 64;                      // K per stage (one 128-byte row of 16-bit values)
   static constexpr int N0 = 256, N1 = 128;           // tokens of chunk 0 / chunk 1 (MMA N)
   static constexpr int TOKENS = N0 + N1;             // tokens per super-tile
   static constexpr int A_BYTES = FM * BK * 2;        // 16 KB decoded weights (MN-major)
@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(SwapCfg<EPI>::THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
-  uint8_t* ring = smem;                              // [NS] {A bf16 | B chunk 0 | B chunk 1}
+  uint8_t* ring = smem;                              // [NS] {A 16-bit | B chunk 0 | B chunk 1}
   uint8_t* rawring = ring + C::NS * C::STAGE;        // [NR] raw e4m3 weight tiles
   uint64_t* bars = reinterpret_cast<uint64_t*>(rawring + C::NR * C::B8_BYTES);
   uint64_t* full = bars;                  // [NS] leader: producer + converters of both CTAs
@@ -254,8 +254,11 @@ __global__ void __launch_bounds__(SwapCfg<EPI>::THREADS, 1)
           ok = mbar_wait_warp(acc_empty + b1, ((b1 ? use1 : use0) & 1u) ^ 1u, abort_flag, p.status);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t idesc0 = make_idesc(kFmtBF16, 256, (uint32_t)s.nr[0], 1, 0);
-        const uint32_t idesc1 = make_idesc(kFmtBF16, 256, (uint32_t)(s.nr[1] ? s.nr[1] : 32), 1, 0);
+        // up GEMM: bf16 operands (the caller's X); down GEMM: f16 (H as the up
+        // GEMM stored it, weights decoded to f16).
+        constexpr uint32_t fmt = EPI == 1 ? kFmtF16 : kFmtBF16;
+        const uint32_t idesc0 = make_idesc(fmt, 256, (uint32_t)s.nr[0], 1, 0);
+        const uint32_t idesc1 = make_idesc(fmt, 256, (uint32_t)(s.nr[1] ? s.nr[1] : 32), 1, 0);
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait_warp(full + stage, phase, abort_flag, p.status)) {
             ok = false;
@@ -317,10 +320,10 @@ __global__ void __launch_bounds__(SwapCfg<EPI>::THREADS, 1)
       }
     }
   } else if (warp >= 2u + C::EPI_WARPS) {
-    // ------------------------------------------------------------ e4m3 -> bf16 converters (both CTAs)
+    // ------------------------------------------------------------ e4m3 -> bf16 (up) / f16 (down) converters (both CTAs)
     // As in grouped_gemm_pair_kernel: two groups of four warps on alternate K
     // steps; thread t of a group takes k-row t % 64 and half t / 64 of the
-    // 128 features of this CTA, and writes the MN-major swizzled bf16 tile
+    // 128 features of this CTA, and writes the MN-major swizzled 16-bit tile
     // that is the MMA's A operand here.
     const int ct = (int)threadIdx.x - 64 - C::EPI_WARPS * 32;  // 0..255
     const int grp = ct >> 7;
@@ -350,7 +353,7 @@ __global__ void __launch_bounds__(SwapCfg<EPI>::THREADS, 1)
         const int kblk = (kb * C::BK) / 128;
         const float s_reg = __shfl_sync(0xffffffffu, kblk < 32 ? s_lo : s_hi, kblk & 31);
         const float sc = kblk < 64 ? s_reg : (col_in ? __ldg(srow + (size_t)kblk * nnb_scale) : 0.f);
-        const float s2 = sc * up;
+        const E4m3Decoder<EPI == 1> dec(sc * up);
         const uint8_t* src = rawring + rs * C::B8_BYTES + r * 128;
         uint8_t* dst = ring + stage * C::STAGE + h * (64 * 128) + r * 128;
         const int rsw = r & 7;
@@ -358,8 +361,8 @@ __global__ void __launch_bounds__(SwapCfg<EPI>::THREADS, 1)
         for (int c = 0; c < 4; ++c) {
           const int chunk = 4 * h + c;
           const uint4 v = *reinterpret_cast<const uint4*>(src + ((chunk ^ rsw) << 4));
-          const uint2 b0 = e4m3x4_to_bf16x4(v.x, s2), b1 = e4m3x4_to_bf16x4(v.y, s2);
-          const uint2 b2 = e4m3x4_to_bf16x4(v.z, s2), b3 = e4m3x4_to_bf16x4(v.w, s2);
+          const uint2 b0 = dec(v.x), b1 = dec(v.y);
+          const uint2 b2 = dec(v.z), b3 = dec(v.w);
           const int j0 = 2 * c, j1 = 2 * c + 1;
           *reinterpret_cast<uint4*>(dst + ((j0 ^ rsw) << 4)) = make_uint4(b0.x, b0.y, b1.x, b1.y);
           *reinterpret_cast<uint4*>(dst + ((j1 ^ rsw) << 4)) = make_uint4(b2.x, b2.y, b3.x, b3.y);
@@ -428,7 +431,7 @@ __global__ void __launch_bounds__(SwapCfg<EPI>::THREADS, 1)
             for (int j = 0; j < 32; ++j)
               if (j < jn && f_in) Y[(size_t)j * p.N] = __uint_as_float(v[j]) * mul;
           } else {
-            // H (bf16): lanes 2i and 2i+1 hold features f, f+1; the even lane
+            // H (f16, the down GEMM's operand): lanes 2i and 2i+1 hold features f, f+1; the even lane
             // stores both for token j, the odd lane both for token j+1.
             uint16_t* H = reinterpret_cast<uint16_t*>(p.out) + (size_t)(tokc + j0) * p.N + (f & ~1);
             const bool odd = lane & 1u;
@@ -439,7 +442,7 @@ __global__ void __launch_bounds__(SwapCfg<EPI>::THREADS, 1)
               const float o0 = __shfl_xor_sync(0xffffffffu, g0, 1);
               const float o1 = __shfl_xor_sync(0xffffffffu, g1, 1);
               const int jj = odd ? j + 1 : j;
-              const uint32_t w = odd ? pack_bf16x2(o1, g1) : pack_bf16x2(g0, o0);
+              const uint32_t w = odd ? pack_f16x2_sat(o1, g1) : pack_f16x2_sat(g0, o0);
               if (jj < jn && f_in) *reinterpret_cast<uint32_t*>(H + (size_t)jj * p.N) = w;
             }
           }

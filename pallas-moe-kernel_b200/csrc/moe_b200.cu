@@ -377,7 +377,7 @@ static bool large_supported(int D, int F, int dtype) {
 }
 static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-// Large-D workspace.  bf16 and e4m3 weights: H (M, F) bf16.  f32 (3xTF32):
+// Large-D workspace.  bf16: H (M, F) bf16; e4m3 weights: H (M, F) f16.  f32 (3xTF32):
 // the tf32 hi/lo planes of W_up^T (E, F, D) and
 // W_down^T (E, D, F) -- the layout moe_prepare_weights writes -- then X hi/lo
 // (M, D) and H hi/lo (M, F), all f32.
@@ -402,7 +402,7 @@ static Tf32LargeLayout tf32_large_layout(int64_t M, int D, int F, int E) {
 }
 static size_t large_ws_bytes(int64_t M, int D, int F, int E, int dtype) {
   if (dtype == MOE_DTYPE_F32) return tf32_large_layout(M, D, F, E).total;
-  return align256((size_t)M * F * 2);  // H (bf16; also with e4m3 weights)
+  return align256((size_t)M * F * 2);  // H (bf16; f16 with e4m3 weights)
 }
 
 template <int EPI, bool BFP8, bool TF32 = false, int WIDE = 1>
@@ -577,27 +577,30 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
   int* status = di->status;
   const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const auto U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
-  // e4m3 weights: the GEMMs run on bf16 operands (the weights decoded to
-  // bf16 in shared memory), so X is read as given.
+  // e4m3 weights: the up GEMM runs on bf16 operands (X as given, weights
+  // decoded to bf16 in shared memory) and stores H in f16, the down GEMM's
+  // 16-bit type (weights decoded to f16).
   const auto A16 = BF16;
+  const auto H16 = fp8 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : BF16;
   const void* xa = x;
   // Small experts with e4m3 weights: expert super-tiles (grouped_gemm_swap.cuh),
   // unless the down GEMM must store Y rows into their source ranks.
   const bool swap = fp8 && !opt.scatter && fp8_use_swap(M, E);
   if (swap) {
     // Token rows in 32-, 64- and 128-row boxes; e4m3 weights {128, 64, 1}.
-    auto swap_maps = [&](SwapMaps* m, const void* rows, int K, const void* w, int N) -> int {
+    auto swap_maps = [&](SwapMaps* m, const void* rows, CUtensorMapDataType rt, int K, const void* w,
+                         int N) -> int {
       memset(m, 0, sizeof(*m));
-      if (int r = make_map_2d(&m->x32, rows, BF16, 2, (uint64_t)M, K, 64, 32)) return r;
-      if (int r = make_map_2d(&m->x64, rows, BF16, 2, (uint64_t)M, K, 64, 64)) return r;
-      if (int r = make_map_2d(&m->x128, rows, BF16, 2, (uint64_t)M, K, 64, 128)) return r;
+      if (int r = make_map_2d(&m->x32, rows, rt, 2, (uint64_t)M, K, 64, 32)) return r;
+      if (int r = make_map_2d(&m->x64, rows, rt, 2, (uint64_t)M, K, 64, 64)) return r;
+      if (int r = make_map_2d(&m->x128, rows, rt, 2, (uint64_t)M, K, 64, 128)) return r;
       return make_map_3d(&m->w, w, U8, 1, (uint64_t)E, K, N, 128, 64);
     };
     SwapMaps s1, s2;
-    if (int r = swap_maps(&s1, xa, D, w_up, F)) return r;
+    if (int r = swap_maps(&s1, xa, BF16, D, w_up, F)) return r;
     GemmParams p1{gs, ws, (int)M, E, F, D, 8, status, w_up_scale, 0};
     if (int r = launch_swap<0>(s1, p1, di, st, ctas)) return r;
-    if (int r = swap_maps(&s2, ws, F, w_down, D)) return r;
+    if (int r = swap_maps(&s2, ws, H16, F, w_down, D)) return r;
     GemmParams p2{gs, y, (int)M, E, D, F, 8, status, w_down_scale, opt.skip_tail ? 1 : 0};
     return launch_swap<1>(s2, p2, di, st, ctas);
   }
@@ -617,7 +620,7 @@ static int run_large(const void* x, const void* w_up, const void* w_down, const 
   // down: Y = H @ W_down[e]
   GemmMaps m2;
   memset(&m2, 0, sizeof(m2));
-  if (int r = make_map_2d(&m2.a, ws, A16, 2, (uint64_t)M, F, 64, 128)) return r;
+  if (int r = make_map_2d(&m2.a, ws, H16, 2, (uint64_t)M, F, 64, 128)) return r;
   if (fp8) {
     if (int r = make_map_3d(&m2.b, w_down, U8, 1, (uint64_t)E, F, D, 128, 64)) return r;
   } else {
@@ -881,12 +884,12 @@ static bool swiglu_supported(int D, int F) { return D >= 256 && D % 256 == 0 && 
 static size_t swiglu_ws_bytes(int64_t M, int D, int F, bool fp8) {
   (void)D;
   (void)fp8;
-  return align256((size_t)M * F * 2);  // H (bf16; also with e4m3 weights)
+  return align256((size_t)M * F * 2);  // H (bf16; f16 with e4m3 weights)
 }
 
 // SwiGLU experts on the two grouped GEMMs.  e4m3 weights (fp8): block
 // scales s_gu (E, D/128, 2F/128) interleaved like the weights and s_down
-// (E, F/128, D/128); the GEMMs run on bf16 operands (weights decoded to bf16).
+// (E, F/128, D/128); the up GEMM runs on bf16 operands, the down GEMM on f16 (H f16).
 static int run_swiglu(const void* x, const void* w_gu, const void* w_down, const float* s_gu, const float* s_down,
                       const int32_t* gs, float* y, int64_t M, int D, int F, int E, bool fp8, void* ws,
                       size_t ws_bytes, cudaStream_t st) {
@@ -898,7 +901,8 @@ static int run_swiglu(const void* x, const void* w_gu, const void* w_down, const
   if (reinterpret_cast<uintptr_t>(ws) & 255u) return fail(MOE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
   int* status = di->status;
   const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  const auto A16 = BF16;  // e4m3 weights are decoded to bf16: X is read as given
+  const auto A16 = BF16;  // e4m3 weights: bf16 up GEMM on X as given; f16 H for the down GEMM
+  const auto H16 = fp8 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : BF16;
   const auto U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const int ctas = (int)g_tune_ctas;
   const void* xa = x;
@@ -917,7 +921,7 @@ static int run_swiglu(const void* x, const void* w_gu, const void* w_down, const
   // down: Y = H @ W_down[e]
   GemmMaps m2;
   memset(&m2, 0, sizeof(m2));
-  if (int r = make_map_2d(&m2.a, ws, A16, 2, (uint64_t)M, F, 64, 128)) return r;
+  if (int r = make_map_2d(&m2.a, ws, H16, 2, (uint64_t)M, F, 64, 128)) return r;
   if (fp8) {
     if (int r = make_map_3d(&m2.b, w_down, U8, 1, (uint64_t)E, F, D, 128, 64)) return r;
   } else {
@@ -2101,14 +2105,15 @@ template <int EPI, bool BFP8, bool TF32, int WIDE = 1>
 static void desc_gemm(moe_launch_desc* d, const char* name, int pairs, int N, int K) {
   using C = GemmCfg<EPI, BFP8, TF32, WIDE>;
   desc_set(d, name, 2 * pairs, C::THREADS, C::SMEM, C::TMEM_COLS, 2, 2 * C::BM, C::TILE_N, C::BK, C::NS,
-           TF32 ? MOE_MMA_TF32X3 : (BFP8 ? MOE_MMA_BF16_E4M3 : MOE_MMA_BF16), N, K, 1, (int)C::NACC);
+           TF32 ? MOE_MMA_TF32X3 : (BFP8 ? (EPI == 1 ? MOE_MMA_F16_E4M3 : MOE_MMA_BF16_E4M3) : MOE_MMA_BF16), N, K, 1,
+           (int)C::NACC);
 }
 // Super-tile kernel: tile_m = tokens per super-tile, tile_n = features per tile.
 template <int EPI>
 static void desc_swap(moe_launch_desc* d, const char* name, int pairs, int N, int K) {
   using C = SwapCfg<EPI>;
   desc_set(d, name, 2 * pairs, C::THREADS, C::SMEM, C::TMEM_COLS, 2, C::TOKENS, 2 * C::FM, C::BK, C::NS,
-           MOE_MMA_BF16_E4M3, N, K, 1, 2);
+           EPI == 1 ? MOE_MMA_F16_E4M3 : MOE_MMA_BF16_E4M3, N, K, 1, 2);
 }
 template <int MODE, int D, int BF, bool XR>
 static void desc_small(moe_launch_desc* d, int ctas, int F, int splits) {

@@ -27,7 +27,8 @@ ERRORS = {
     -7: "MOE_ERR_MISALIGNED",
 }
 
-MMA_KINDS = {0: "none", 1: "kind::f16 (bf16)", 2: "kind::f16 (bf16 from e4m3)", 3: "kind::tf32 x3"}
+MMA_KINDS = {0: "none", 1: "kind::f16 (bf16)", 2: "kind::f16 (bf16 from e4m3)", 3: "kind::tf32 x3",
+             4: "kind::f16 (f16 from e4m3)"}
 
 
 class LaunchDesc(ctypes.Structure):

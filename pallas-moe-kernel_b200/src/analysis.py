@@ -276,7 +276,7 @@ def roofline(M: int, D: int, F: int, group_sizes: Sequence[int], dtype: str, ker
     return out
 
 
-_PRODUCTS = {0: 0, 1: 1, 2: 1, 3: 6}  # bf16-equivalent MMA work per useful multiply-add, per MMA kind
+_PRODUCTS = {0: 0, 1: 1, 2: 1, 3: 6, 4: 1}  # bf16-equivalent MMA work per useful multiply-add, per MMA kind
 
 
 def _launch_model(L: dict, M: int, D: int, F: int, E: int, g: list[int], dtype: str) -> dict:
