@@ -388,7 +388,12 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
     # are pipelined on three streams (copy in, compute, copy out) over two
     # device and two host buffer slots, as a serving loop runs them: H2D of
     # step i+1 and D2H of step i-1 overlap the compute of step i.
-    numa = bind_to_gpu_numa_node(device.index) if world > 1 else {"numa_bound": False, "reason": "one GPU"}
+    # Pinned host buffers on the GPU's NUMA node (first touch after binding);
+    # the original affinity comes back after the host-copy legs, so that the
+    # CPU baseline keeps every host thread.
+    affinity = os.sched_getaffinity(0)
+    numa = (bind_to_gpu_numa_node(device.index) if args.numa_bind == "on"
+            else {"numa_bound": False, "reason": "--numa-bind off"})
     xh = x.cpu().pin_memory()
     gsh = torch.from_numpy(gs_np).pin_memory()
     yh = [torch.empty((cfg.M, cfg.D), dtype=torch.float32).pin_memory() for _ in range(2)]
@@ -458,6 +463,7 @@ def run_ours(args, cfg, rank, world, device) -> dict | None:
     c1.record(stream)
     torch.cuda.synchronize(device)
     copy_ms = c0.elapsed_time(c1)
+    os.sched_setaffinity(0, affinity)
 
     vals = torch.tensor([total_ms, e2e_ms, copy_ms], dtype=torch.float64, device=device)
     if world > 1:
@@ -1047,6 +1053,8 @@ def main() -> int:
     ap.add_argument("--transport", default="peer", choices=["peer", "nccl"],
                     help="N>1: token exchange by the library's kernels over NVLink peer memory (peer) "
                          "or by NCCL send/recv from Python (nccl)")
+    ap.add_argument("--numa-bind", default="on", choices=["on", "off"],
+                    help="bind the process to the GPU's NUMA node before pinning the e2e host buffers")
     ap.add_argument("--no-other-configs", dest="other_configs", action="store_false",
                     help="N=1: skip the device-resident figures of the other configurations (c1..c5) that "
                          "otherwise ride along the line under other_configs")
