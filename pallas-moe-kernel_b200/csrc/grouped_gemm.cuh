@@ -173,7 +173,10 @@ struct GemmCfg {
   // was scheduled under it), or of the FP8 block with its extra warps.
   static constexpr int LAUNCH_BOUND = THREADS > 320 ? THREADS : 320;
   static_assert(SMEM <= kMaxSmemPerBlock, "shared memory budget");
-  static_assert(!BFP8 || (NS % 2 == 0 && NR % 2 == 0), "alternating converter groups keep fixed stage parities");
+  // Even ring depths: each raw stage is then always used by the same one of
+  // the two alternating converter groups, which consumed its previous use, so
+  // a parity wait cannot take a phase two uses old for the awaited one.
+  static_assert(!BFP8 || (NS % 2 == 0 && NR % 2 == 0), "converter groups need even ring depths (mbarrier parity aliasing)");
 };
 
 struct GemmMaps {

@@ -69,7 +69,13 @@ struct SwapCfg {
   static constexpr int RAW_WARP = 2 + EPI_WARPS + CVT_WARPS;
   static constexpr int THREADS = 64 + (EPI_WARPS + CVT_WARPS) * 32 + 32;
   static_assert(SMEM <= kMaxSmemPerBlock, "shared memory budget");
-  static_assert(NS % 2 == 0 && NR % 2 == 0, "alternating converter groups keep fixed stage parities");
+  // The two converter groups take alternate K steps (g even / odd).  With an
+  // even ring depth every use of a raw stage falls to the same group, which
+  // consumed the previous use, so its parity wait on raw_full can never see a
+  // phase two uses old as complete.  With an odd depth the groups share the
+  // stages and a group can run two phases ahead (a build with NR = 3 decoded
+  // stale tiles).
+  static_assert(NS % 2 == 0 && NR % 2 == 0, "converter groups need even ring depths (mbarrier parity aliasing)");
 };
 
 // Super-tile walk: global tile index -> (expert, token super-tile, feature
