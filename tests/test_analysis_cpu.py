@@ -14,7 +14,6 @@ import json
 import math
 from pathlib import Path
 
-import numpy as np
 import pytest
 
 from src import _lib, analysis

@@ -4,7 +4,6 @@ brute force, and the C ABI's argument checks (no GPU work)."""
 import ctypes
 
 import numpy as np
-import pytest
 
 from oracle import moe_oracle as orc
 from src import _lib
